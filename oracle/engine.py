@@ -1,0 +1,187 @@
+"""The batched greedy decode engine restated in numpy (test infrastructure).
+
+``OracleEngine`` mirrors ``sheetsage2_refined/engine.py:52-369`` without the
+rescoring terms: construction (55-149), ``load`` (180-232), ``run`` (234-246),
+``finished`` (248-252), ``take`` (254-262) and the step ``_forward``
+(294-357).  ``step(forced=...)`` additionally lets a test force the
+committed token per slot (teacher forcing) and returns the raw logits.
+
+The decoder forward is ``TokenDecoder`` (decoder.py:58-151) evaluated one
+token per row against the per-slot caches; the prefix prefill of ``load``
+(engine.py:199-207, decoder.py:118-151) is evaluated as the same single-token
+forward over the prefix positions in order, which equals the reference's
+causal forward up to float32 summation order.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from sheetsage2_refined_b200.grammar import ENDED
+from sheetsage2_refined_b200.vocab_table import EOS, OUT
+from sheetsage2_refined_b200.weights import POSITION_OFFSET
+
+from .grammar import make_grammar_oracle
+from .numerics import bf16, gelu, layer_norm, softmax
+
+
+class OracleEngine:
+    def __init__(self, config, state_dict: dict, grammar, *, batch: int, frames: int, mode: str = "bf16",
+                 logit_bias: np.ndarray | None = None):
+        if mode not in ("fp32", "bf16"):
+            raise ValueError(mode)
+        self.config, self.mode, self.batch, self.frames = config, mode, batch, frames
+        self.max_tokens = config.max_tokens
+        self.heads, self.head_dim = config.heads, config.width // config.heads
+        rnd = bf16 if mode == "bf16" else (lambda a: np.asarray(a, np.float32))
+        self._round = rnd
+        sd = {k: np.asarray(v, np.float32) for k, v in state_dict.items()}
+        # Linear weights as the engine holds them (engine.py:118-123): bf16 copies on CUDA.
+        self.lin = {}
+        for i in range(config.layers):
+            p = f"layers.{i}."
+            for name in ("self_attn.q", "self_attn.k", "self_attn.v", "self_attn.out",
+                         "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.out", "fc1", "fc2"):
+                w, b = sd[f"{p}{name}.weight"], sd[f"{p}{name}.bias"]
+                self.lin[(i, name)] = (np.ascontiguousarray(rnd(w).T), rnd(b))
+            for norm in ("self_attn_norm", "cross_attn_norm", "final_norm"):
+                self.lin[(i, norm)] = (sd[f"{p}{norm}.weight"], sd[f"{p}{norm}.bias"])
+        self.tok_emb = sd["token_embedding.weight"]  # the lookup stays fp32 (engine.py:298-301)
+        self.pos_emb = sd["position_embedding.weight"]
+        self.emb_norm = (sd["embedding_norm.weight"], sd["embedding_norm.bias"])
+        self.out_emb_t = np.ascontiguousarray(rnd(self.tok_emb).T)  # tied logits (engine.py:123,315)
+        self.grammar = make_grammar_oracle(grammar)
+        self.logit_bias = None if logit_bias is None else np.asarray(logit_bias, np.float32)
+
+        H, hd, L = self.heads, self.head_dim, config.layers
+        self.self_k = [np.zeros((batch, H, self.max_tokens, hd), np.float32) for _ in range(L)]
+        self.self_v = [np.zeros((batch, H, self.max_tokens, hd), np.float32) for _ in range(L)]
+        self.cross_k = [np.zeros((batch, H, frames, hd), np.float32) for _ in range(L)]
+        self.cross_v = [np.zeros((batch, H, frames, hd), np.float32) for _ in range(L)]
+        self.frames_real = np.full(batch, frames, np.int64)
+        self.out = np.zeros((batch, self.max_tokens), np.int64)
+        self.state = self.grammar.new_state(batch)
+        self.state["finished"][:] = True
+        self.state["token"] = np.full(batch, EOS, np.int64)
+        self.state["position"] = np.zeros(batch, np.int64)
+        self.stop = np.full(batch, np.inf, np.float64)
+        self.loaded = [False] * batch
+
+    # ------------------------------------------------------------ numerics
+    def _linear(self, layer: int, name: str, x: np.ndarray) -> np.ndarray:
+        wt, b = self.lin[(layer, name)]
+        return self._round(self._round(x) @ wt + b)
+
+    def _split(self, y: np.ndarray) -> np.ndarray:
+        return y.reshape(self.heads, self.head_dim)
+
+    def _attend(self, q: np.ndarray, k: np.ndarray, v: np.ndarray) -> np.ndarray:
+        """engine.py:286-292 for one row: q ``[H, hd]``, k/v ``[H, n, hd]`` (only the visible keys)."""
+
+        rnd = self._round
+        scores = rnd(np.einsum("hd,hnd->hn", q, k)) * np.float32(self.head_dim ** -0.5)
+        p = rnd(softmax(scores))
+        return rnd(np.einsum("hn,hnd->hd", p, v)).reshape(-1)
+
+    def _row_forward(self, slot: int, token: int, position: int) -> np.ndarray:
+        """Final hidden state (fp32) of one token at ``position`` of ``slot``; writes its K/V."""
+
+        x = self.tok_emb[token] + self.pos_emb[position + POSITION_OFFSET]
+        x = layer_norm(x, *self.emb_norm)
+        n_cross = int(self.frames_real[slot])
+        for i in range(self.config.layers):
+            k = self._split(self._linear(i, "self_attn.k", x))
+            v = self._split(self._linear(i, "self_attn.v", x))
+            self.self_k[i][slot, :, position] = k
+            self.self_v[i][slot, :, position] = v
+            q = self._split(self._linear(i, "self_attn.q", x))
+            a = self._attend(q, self.self_k[i][slot, :, : position + 1], self.self_v[i][slot, :, : position + 1])
+            x = layer_norm(x + self._linear(i, "self_attn.out", a), *self.lin[(i, "self_attn_norm")])
+            q = self._split(self._linear(i, "cross_attn.q", x))
+            a = self._attend(q, self.cross_k[i][slot, :, :n_cross], self.cross_v[i][slot, :, :n_cross])
+            x = layer_norm(x + self._linear(i, "cross_attn.out", a), *self.lin[(i, "cross_attn_norm")])
+            h = self._round(gelu(self._linear(i, "fc1", x)))
+            x = layer_norm(x + self._linear(i, "fc2", h), *self.lin[(i, "final_norm")])
+        return x
+
+    def _logits(self, x: np.ndarray) -> np.ndarray:
+        return self._round(self._round(x) @ self.out_emb_t).astype(np.float32)
+
+    # --------------------------------------------------------------- slots
+    def free_slots(self) -> list[int]:
+        return [s for s in range(self.batch) if not self.loaded[s]]
+
+    def load(self, slot: int, memory, prefix: list[int], stop_seconds, frames: int | None = None,
+             target: int | None = None) -> None:
+        """engine.py:180-232 (without the rescoring tables); ``target`` feeds the table grammar."""
+
+        memory = np.asarray(memory, np.float32).reshape(-1, self.config.width)
+        frames = self.frames if frames is None else frames
+        n = len(prefix)
+        for i in range(self.config.layers):
+            # decoder.py:108-113 — cross K/V of every memory frame, projected once per window
+            k = self._linear(i, "cross_attn.k", memory[: self.frames])
+            v = self._linear(i, "cross_attn.v", memory[: self.frames])
+            f = k.shape[0]
+            self.cross_k[i][slot] = 0.0
+            self.cross_v[i][slot] = 0.0
+            self.cross_k[i][slot, :, :f] = k.reshape(f, self.heads, self.head_dim).transpose(1, 0, 2)
+            self.cross_v[i][slot, :, :f] = v.reshape(f, self.heads, self.head_dim).transpose(1, 0, 2)
+        self.frames_real[slot] = frames
+        for pos in range(n - 1):  # prefix prefill (engine.py:200-205)
+            self._row_forward(slot, prefix[pos], pos)
+        self.out[slot, :n] = prefix
+        for name, value in self.grammar.prefix_state(prefix, prefix.index(OUT)).items():
+            self.state[name][slot] = value[0]
+        if target is not None and "target" in self.state:
+            self.state["target"][slot] = target
+        self.state["token"][slot] = prefix[-1]
+        self.state["position"][slot] = n - 1
+        self.stop[slot] = np.inf if stop_seconds is None else stop_seconds
+        self.loaded[slot] = True
+
+    def step(self, forced: np.ndarray | None = None):
+        """One step (engine.py:294-357). Returns ``(raw logits [B, V], greedy choice [B])``.
+
+        ``forced[slot] >= 0`` commits that token instead of the greedy one
+        (teacher forcing); rows that are finished are not evaluated.
+        """
+
+        st = self.state
+        token, position = st["token"], st["position"]
+        active = ~st["finished"]
+        logits = np.zeros((self.batch, self.grammar.vocab_size), np.float32)
+        for slot in np.nonzero(active)[0]:
+            x = self._row_forward(int(slot), int(token[slot]), int(position[slot]))
+            logits[slot] = self._logits(x)
+        biased = logits if self.logit_bias is None else logits + self.logit_bias
+        masked = np.where(self.grammar.allowed(st), biased, -np.inf)
+        greedy = masked.argmax(axis=-1)
+        choice = greedy.copy()
+        if forced is not None:
+            choice = np.where(np.asarray(forced) >= 0, forced, choice)
+        choice = np.where(active, choice, token)
+        new_position = np.where(active, position + 1, position)
+        rows = np.arange(self.batch)
+        self.out[rows, new_position] = np.where(active, choice, self.out[rows, new_position])
+        self.grammar.update(st, choice, active, self.stop, new_position >= self.max_tokens - 1)
+        token[...] = choice
+        position[...] = new_position
+        return logits, greedy
+
+    def run(self, steps: int) -> None:
+        for _ in range(steps):
+            self.step()
+
+    def finished(self) -> list[int]:
+        return [s for s in range(self.batch) if self.loaded[s] and self.state["finished"][s]]
+
+    def take(self, slot: int) -> tuple[list[int], str]:
+        """engine.py:254-262."""
+
+        length = int(self.state["position"][slot]) + 1
+        tokens = self.out[slot, :length].tolist()
+        if tokens[-1] != EOS:
+            tokens.append(EOS)
+        self.loaded[slot] = False
+        return tokens, ENDED[int(self.state["ended"][slot])]

@@ -1,0 +1,219 @@
+"""Generate the golden fixtures of this directory by running the reference itself.
+
+Run in a container that has the reference checkout (read-only) at
+``/root/reference``::
+
+    python tests/golden/make_golden.py
+
+The reference package is imported from that checkout with a stub for
+``soundfile`` (only ``transcribe.load_waveform`` uses it).  Its CPU path is
+float32 and eager (``engine.py:69-70,244-245``), so the files hold the
+reference's own float32 results: greedy tokens and end reasons from
+``BatchDecoder`` and teacher-forced logits from ``TokenDecoder.forward``.
+For the synthetic vocabularies a table grammar (the rule documented in
+``sheetsage2_refined_b200.grammar.TableGrammar``) is put into the reference
+engine through its grammar duck type (``engine.grammar`` and extra state).
+
+Files:
+
+* ``c1_table.npz``      — 2L/d256/V512 decoder, one slot, 128 greedy steps.
+* ``c2_head.npz``       — 12L/d1024/V2048 decoder, F=1500, first 24 steps.
+* ``batch_table.npz``   — three slots with prefill, masking, limit, refill.
+* ``real_grammar.npz``  — real 32,576-token vocabulary and ``TokenGrammar``,
+  two prompt sets, stop seconds and a mode bias.
+* ``grammar_trace.npz`` — ``TokenGrammar`` state after every token of seeded
+  random walks through the allowed tokens (EOS included), per prompt set.
+"""
+
+from __future__ import annotations
+
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(REPO / "tests"))
+sys.modules.setdefault("soundfile", types.ModuleType("soundfile"))
+sys.path.insert(0, "/root/reference")
+
+from sheetsage2_refined.decoder import DecoderConfig as RefConfig  # noqa: E402
+from sheetsage2_refined.decoder import TokenDecoder  # noqa: E402
+from sheetsage2_refined.engine import BatchDecoder  # noqa: E402
+from sheetsage2_refined.grammar import TokenGrammar  # noqa: E402
+from sheetsage2_refined.vocab import Vocab  # noqa: E402
+
+import scenarios as sc  # noqa: E402
+from sheetsage2_refined_b200.weights import memory_array, synthetic_state_dict  # noqa: E402
+
+
+class TorchTableGrammar:
+    """The table grammar in the reference engine's grammar duck type (engine.py:74,211,349,355)."""
+
+    def __init__(self, desc):
+        self.table = torch.tensor(desc.table)
+        self.states, self.multiplier = desc.states, desc.multiplier
+        self.time_seconds = torch.tensor(desc.time_seconds)
+        self.prompts = desc.prompts
+
+    def allowed(self, state):
+        return self.table[state["g"]]
+
+    def update(self, state, tokens, active, stop, at_limit):
+        g = (self.multiplier * state["g"] + tokens) % self.states
+        count = state["count"] + 1
+        done = count >= state["target"]
+        ended = torch.where(done, 1, torch.where(at_limit, 3, 0))
+        finished = done | at_limit
+        state["g"].copy_(torch.where(active, g, state["g"]))
+        state["count"].copy_(torch.where(active, count, state["count"]))
+        state["ended"].copy_(torch.where(active & finished, ended, state["ended"]))
+        state["finished"].copy_(state["finished"] | (active & finished))
+
+    def prefix_state(self, tokens, out_index, device):
+        g = 0
+        for token in tokens[out_index + 1 :]:
+            g = (self.multiplier * g + token) % self.states
+        z = lambda v: torch.tensor([v], dtype=torch.long)  # noqa: E731
+        return {"g": z(g), "count": z(0), "finished": torch.tensor([False]), "ended": z(0)}
+
+
+def ref_decoder(config, seed):
+    decoder = TokenDecoder(RefConfig(vocab_size=config.vocab_size, width=config.width, layers=config.layers,
+                                     heads=config.heads, ffn_width=config.ffn_width, max_tokens=config.max_tokens))
+    state = {k: torch.from_numpy(v) for k, v in synthetic_state_dict(config, seed).items()}
+    decoder.load_state_dict(state, strict=True)
+    return decoder.eval()
+
+
+def table_engine(decoder, desc, batch, frames):
+    engine = BatchDecoder(decoder, Vocab(), batch=batch, frames=frames)
+    engine.grammar = TorchTableGrammar(desc)
+    engine.state["g"] = torch.zeros(batch, dtype=torch.long)
+    engine.state["count"] = torch.zeros(batch, dtype=torch.long)
+    engine.state["target"] = torch.full((batch,), np.iinfo(np.int64).max, dtype=torch.long)
+    return engine
+
+
+def ref_loader(engine, width, frames_engine):
+    def load(slot, memory_seed, prefix, stop, frames, target):
+        memory = torch.from_numpy(memory_array(frames_engine, width, memory_seed))
+        engine.load(slot, memory, prefix, stop, frames)
+        if target is not None:
+            engine.state["target"][slot] = target
+    return load
+
+
+def teacher_forced(decoder, memory_seed, frames_engine, frames, tokens, first):
+    """Logits predicting ``tokens[first+1:]`` from the full prefix (decoder.py:98-151)."""
+
+    memory = torch.from_numpy(memory_array(frames_engine, decoder.config.width, memory_seed))
+    cache = decoder.new_cache(memory, torch.tensor([frames]))
+    logits = decoder(torch.tensor([tokens[:-1]]), cache)[0]
+    return logits[first:].numpy().astype(np.float32)
+
+
+@torch.no_grad()
+def make_single(name, config, seed, desc, memory_seed, frames, steps):
+    decoder = ref_decoder(config, seed)
+    engine = table_engine(decoder, desc, 1, frames)
+    tokens, ended = sc.single(engine, ref_loader(engine, config.width, frames), steps, memory_seed, frames,
+                              target=steps)
+    logits = teacher_forced(decoder, memory_seed, frames, frames, tokens[: steps + 2], 1)
+    np.savez_compressed(HERE / name, tokens=np.array(tokens), ended=np.array(ended), logits=logits)
+    print(name, len(tokens), ended, logits.shape)
+
+
+@torch.no_grad()
+def make_batch():
+    decoder = ref_decoder(sc.C1_SHORT, sc.BATCH_SEED)
+    engine = table_engine(decoder, sc.batch_grammar(), 3, sc.BATCH_FRAMES)
+    taken = sc.continuous_batch(engine, ref_loader(engine, sc.C1_SHORT.width, sc.BATCH_FRAMES))
+    slots = np.array([s for s, _, _ in taken])
+    ended = np.array([e for _, _, e in taken])
+    lengths = np.array([len(t) for _, t, _ in taken])
+    flat = np.concatenate([np.array(t) for _, t, _ in taken])
+    np.savez_compressed(HERE / "batch_table.npz", slots=slots, ended=ended, lengths=lengths, tokens=flat)
+    print("batch_table", list(zip(slots.tolist(), lengths.tolist(), ended.tolist())))
+
+
+def mode_bias_values():
+    return [0.0, 1.5, -0.5, 2.0, 0.25, -1.0, 3.0, 0.5, -2.0]
+
+
+@torch.no_grad()
+def make_real():
+    vocab = Vocab()
+    decoder = ref_decoder(sc.REAL_TINY, sc.REAL_SEED)
+    out = {}
+    for i, prompts in enumerate(sc.REAL_PROMPT_SETS):
+        bias = mode_bias_values() if "key_mode" in prompts else None
+        engine = BatchDecoder(decoder, vocab, batch=2, frames=sc.REAL_FRAMES, prompts=prompts, mode_bias=bias)
+        prefix = vocab.prompt_prefix(prompts)
+        load = ref_loader(engine, sc.REAL_TINY.width, sc.REAL_FRAMES)
+        load(0, 31 + i, prefix, 2.5, sc.REAL_FRAMES, None)
+        load(1, 41 + i, prefix + [vocab.start["shift"] + 3], None, 50, None)
+        for _ in range(40):
+            engine.run(5)
+            if len(engine.finished()) == 2:
+                break
+        for slot in (0, 1):
+            finished = bool(engine.state["finished"][slot])
+            length = int(engine.state["position"][slot]) + 1
+            out[f"p{i}_s{slot}_tokens"] = engine.out[slot, :length].numpy().copy()
+            out[f"p{i}_s{slot}_ended"] = np.array(int(engine.state["ended"][slot]))
+            out[f"p{i}_s{slot}_finished"] = np.array(finished)
+            print("real", i, slot, length, finished, int(engine.state["ended"][slot]))
+    np.savez_compressed(HERE / "real_grammar.npz", **out)
+
+
+@torch.no_grad()
+def make_trace():
+    vocab = Vocab()
+    out = {}
+    names = ("in_shift", "shift_run", "payload", "last_field", "incomplete", "finished", "ended")
+    for i, prompts in enumerate(sc.REAL_PROMPT_SETS):
+        grammar = TokenGrammar(vocab, "cpu", prompts)
+        rng = np.random.default_rng(1000 + i)
+        state = TokenGrammar.new_state(1, "cpu")
+        stop = torch.tensor([120.0], dtype=torch.float64)
+        tokens, states, masks = [], [], []
+        for step in range(600):
+            allowed = grammar.allowed(state)[0].numpy()
+            masks.append(np.packbits(allowed))
+            choices = np.nonzero(allowed)[0]
+            eos_ok = allowed[2]
+            if eos_ok and rng.random() < 0.02:
+                token = 2
+            else:
+                # prefer non-time tokens so that events get several fields
+                non_time = choices[(choices < vocab.start["time"]) | (choices >= vocab.end["time"])]
+                pool = non_time if len(non_time) and rng.random() < 0.8 else choices
+                token = int(rng.choice(pool))
+            at_limit = torch.tensor([step == 599])
+            grammar.update(state, torch.tensor([token]), torch.tensor([True]), stop, at_limit)
+            tokens.append(token)
+            states.append([int(state[n][0]) for n in names])
+            if bool(state["finished"][0]):
+                state = TokenGrammar.new_state(1, "cpu")
+        out[f"p{i}_tokens"] = np.array(tokens)
+        out[f"p{i}_states"] = np.array(states)
+        out[f"p{i}_masks"] = np.stack(masks)
+        prefix = vocab.prompt_prefix(prompts) + tokens[:25]
+        ps = grammar.prefix_state(prefix, prefix.index(3), "cpu")
+        out[f"p{i}_prefix_state"] = np.array([int(ps[n][0]) for n in names])
+    np.savez_compressed(HERE / "grammar_trace.npz", **out)
+    print("grammar_trace written")
+
+
+if __name__ == "__main__":
+    torch.manual_seed(0)
+    make_trace()
+    make_single("c1_table.npz", sc.C1, sc.C1_SEED, sc.c1_grammar(), sc.C1_MEMORY_SEED, sc.C1_FRAMES, sc.C1_STEPS)
+    make_batch()
+    make_real()
+    make_single("c2_head.npz", sc.C2, sc.C2_SEED, sc.c2_grammar(), sc.C2_MEMORY_SEED, sc.C2_FRAMES, 24)
