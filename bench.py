@@ -1,0 +1,371 @@
+"""Decoder token-loop throughput on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload single|batched]
+
+Workloads (synthetic: seeded N(0, 0.02) weights, N(0, 1) encoder memory, a
+seeded 8-state table grammar allowing 25% of the vocabulary per state):
+
+* ``single`` (default): one song, 12-layer d1024/16-head/FFN4096 decoder,
+  vocabulary 2048, bf16 memory [1, 1500, 1024], greedy decode of 2048 tokens
+  at batch 1.  A step = load the window (cross K/V projection) and decode its
+  2048 tokens.
+* ``batched``: 64 slots of the same decoder, frames U[600, 3000], target
+  lengths U[512, 4096], continuous batching with finished songs replaced; a
+  step = 64 steps of the whole batch plus the refills they trigger.
+
+Under torchrun every rank decodes its own songs on its own GPU (no
+collective on the data path; weak scaling) and ``value`` is the tokens of all
+ranks divided by the slowest rank's time.  ``--impl reference`` times the
+reference's CPU decode path, restated by the oracle (float32 numpy, all host
+cores), on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+from sheetsage2_refined_b200.grammar import TableGrammar  # noqa: E402
+from sheetsage2_refined_b200.vocab_table import OUT, SOS  # noqa: E402
+from sheetsage2_refined_b200.weights import DecoderConfig, DecoderWeights, synthetic_state_dict  # noqa: E402
+
+METRIC = "decoder tokens/s per GPU and box (greedy, batch 1/64); ms/step; % HBM roofline"
+CONFIG = DecoderConfig(vocab_size=2048, width=1024, layers=12, heads=16, ffn_width=4096, max_tokens=5120)
+WEIGHT_SEED, MEMORY_SEED, GRAMMAR_SEED = 1, 101, 8
+SINGLE_FRAMES, SINGLE_TOKENS = 1500, 2048
+BATCH, BATCH_FRAMES = 64, 3000
+CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits")
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.path = index, None, None
+
+    def __enter__(self):
+        import tempfile
+
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index), "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def reduce_max(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU arm
+def cpu_decode_sample(seconds: float = 10.0, min_tokens: int = 8):
+    """The reference's CPU decode path (the oracle's float32 mode) on the single-song workload.
+
+    Loads the window (cross K/V of 1500 frames), then decodes greedily until
+    ``seconds`` of decode time have passed.  Returns (tokens/s, tokens, cores).
+    """
+
+    from oracle.engine import OracleEngine
+    from sheetsage2_refined_b200.weights import memory_array
+
+    grammar = TableGrammar(CONFIG.vocab_size, states=8, density=0.25, seed=GRAMMAR_SEED)
+    eng = OracleEngine(CONFIG, synthetic_state_dict(CONFIG, WEIGHT_SEED), grammar, batch=1, frames=SINGLE_FRAMES,
+                       mode="fp32")
+    eng.load(0, memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED), [SOS, OUT], None, SINGLE_FRAMES,
+             target=SINGLE_TOKENS)
+    eng.step()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while n < min_tokens or time.perf_counter() - t0 < seconds:
+        eng.step()
+        n += 1
+    dt = time.perf_counter() - t0
+    return n / dt, n, os.cpu_count() or 1
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    values = []
+    tokens = 0
+    for _ in range(args.warmup):
+        cpu_decode_sample(seconds=1.0, min_tokens=2)
+    for _ in range(args.steps):
+        v, n, cores = cpu_decode_sample(seconds=args.cpu_seconds / max(args.steps, 1), min_tokens=4)
+        values.append(v)
+        tokens += n
+    value = statistics.mean(values)
+    sample = (f"single-song workload: greedy decode from position 1, {tokens} tokens over {args.steps} steps, "
+              "float32 numpy restatement of the reference CPU path")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "single-song decode, 12L d1024 h16 ffn4096 V2048, F=1500, batch 1",
+                   "global_batch": 1, "seq_len": SINGLE_TOKENS, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_b200(args, world, rank, local):
+    import torch
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    from sheetsage2_refined_b200 import BatchDecoder
+    from sheetsage2_refined_b200.weights import memory_array
+
+    grammar = TableGrammar(CONFIG.vocab_size, states=8, density=0.25, seed=GRAMMAR_SEED)
+    dec = DecoderWeights(CONFIG, synthetic_state_dict(CONFIG, WEIGHT_SEED))
+    # S2R_ENGINE_FLAGS (S2R_FLAG_* bits) lets a profiler run use plain launches
+    flags = int(os.environ.get("S2R_ENGINE_FLAGS", "0"))
+    if args.workload == "single":
+        eng = BatchDecoder(dec, None, batch=1, frames=SINGLE_FRAMES, grammar=grammar, device=device, flags=flags)
+        mem_host = torch.from_numpy(memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED + rank)).to(torch.bfloat16)
+        mem_dev = mem_host.to(device)
+        mem_pinned = mem_host.pin_memory()
+
+        def step_device():
+            eng.load(0, mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+            eng.run(SINGLE_TOKENS)
+            return SINGLE_TOKENS
+
+        def step_e2e():
+            eng.load(0, mem_pinned, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+            eng.run(SINGLE_TOKENS)
+            done = eng.finished()
+            tokens, _ = eng.take(0)
+            assert done == [0] and len(tokens) == SINGLE_TOKENS + 3
+            return SINGLE_TOKENS
+
+        h2d = SINGLE_FRAMES * CONFIG.width * 2 + 2 * 8
+        d2h = (SINGLE_TOKENS + 3) * 8 + 1
+        workload = "single-song decode, 12L d1024 h16 ffn4096 V2048, bf16 memory [1,1500,1024], 2048 tokens, batch 1"
+        global_batch, seq_len = 1, SINGLE_TOKENS
+    else:
+        raise SystemExit("batched workload: not implemented yet")
+
+    stream = torch.cuda.current_stream(device)
+    # warm-up (also captures the step graph)
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize(device)
+
+    # roofline: per-kernel times of one profiled step in the middle of a decode
+    eng.load(0, mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+    eng.run(SINGLE_TOKENS // 2)
+    prof = profile(eng)
+    eng.run(SINGLE_TOKENS)
+    torch.cuda.synchronize(device)
+
+    def timed(fn, k):
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tokens = 0
+        start.record(stream)
+        for _ in range(k):
+            tokens += fn()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        return start.elapsed_time(end), tokens
+
+    gpu_index = local
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        try:
+            gpu_index = int(visible.split(",")[local])
+        except (ValueError, IndexError):
+            pass
+    with ClockSampler(gpu_index) as clocks:
+        ms, tokens = timed(step_device, args.steps)
+    clock_summary = clocks.summary()
+    ms_e2e, tokens_e2e = timed(step_e2e, max(1, args.steps // 2))
+
+    ms_max = reduce_max(ms, world, device)
+    ms_e2e_max = reduce_max(ms_e2e, world, device)
+    tokens_all = reduce_sum(tokens, world, device)
+    tokens_e2e_all = reduce_sum(tokens_e2e, world, device)
+    value = tokens_all / (ms_max / 1000.0)
+    e2e = tokens_e2e_all / (ms_e2e_max / 1000.0)
+
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        v, n, cores = cpu_decode_sample(seconds=args.cpu_seconds)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} greedy tokens of the single-song workload from position 1 (load excluded), "
+                         "float32 numpy restatement of the reference CPU path, all host cores"}
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload, "global_batch": global_batch * world, "seq_len": seq_len,
+                       "parallelism": f"song-sharded x{world}",
+                       "l2": "inputs larger than L2 (352 MB of weights streamed per token)"},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            # per step: cross K/V projection (one per layer), the 1-row prefill of the
+            # prefix (8 per layer but only the K/V projection in the last), then the decode
+            "gpu_launches": args.steps * (CONFIG.layers + 8 * (CONFIG.layers - 1) + 1
+                                          + eng.step_launches * SINGLE_TOKENS),
+            "clocks": clock_summary,
+            "roofline": roofline(prof, peak, peak_kind),
+            "step_roofline": prof["step"],
+            "kernel_classes": {k: {"us_per_launch": 1000.0 * v["ms"] / max(v["launches"], 1),
+                                   "launches": v["launches"],
+                                   "gbs": v["bytes_per_launch"] / max(v["ms"] / max(v["launches"], 1), 1e-9) / 1e6}
+                               for k, v in prof["classes"].items()},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def profile(eng):
+    import ctypes as C
+
+    from sheetsage2_refined_b200 import _lib
+
+    ms = (C.c_float * 9)()
+    by = (C.c_double * 9)()
+    n = (C.c_int32 * 9)()
+    _lib.check(eng._lib.s2r_profile_step(eng._ctx, ms, by, n, eng._stream()))
+    classes = {name: {"ms": ms[i], "launches": n[i], "bytes_per_launch": by[i]} for i, name in enumerate(CLASS_NAMES)}
+    total_ms = sum(ms[i] for i in range(9))
+    total_bytes = sum(by[i] * n[i] for i in range(9))
+    return {"classes": classes, "step": {"ms_kernels": total_ms, "bytes": total_bytes,
+                                         "gbs": total_bytes / (total_ms * 1e-3) / 1e9}}
+
+
+def roofline(prof, peak, peak_kind):
+    name, c = max(prof["classes"].items(), key=lambda kv: kv[1]["ms"])
+    per_launch_s = c["ms"] / max(c["launches"], 1) / 1000.0
+    achieved = c["bytes_per_launch"] / per_launch_s / 1e9
+    return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+            "bytes_per_launch": c["bytes_per_launch"], "us_per_launch": per_launch_s * 1e6}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--workload", default="single", choices=("single", "batched"))
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_b200(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,199 @@
+/*
+ * s2r.h — C ABI of the B200 decode engine for SheetSage2-Refined's
+ * grammar-constrained greedy decoder token loop.
+ *
+ * The engine replaces the reference's `BatchDecoder`
+ * (sheetsage2_refined/engine.py:52-369): a batch of independent decode
+ * slots, each with its own paged self-attention K/V cache, resident
+ * cross-attention K/V of its encoder window, grammar state and output
+ * buffer.  One step feeds every live slot its last token through the
+ * post-LayerNorm decoder (decoder.py:58-151), picks the next token under the
+ * grammar mask with a greedy argmax and advances the grammar, all on the GPU.
+ *
+ * Conventions
+ *  - Every entry point returns an `s2r_status`; none aborts.  The message of
+ *    the last failure on the calling thread is `s2r_last_error()`.
+ *  - Pointers to caller data may be host or device memory (unified
+ *    addressing) unless stated otherwise; the engine copies what it keeps.
+ *  - `stream` is a `cudaStream_t` (NULL: the legacy default stream).  Work is
+ *    ordered on it; entry points that return host data synchronise it.
+ *  - Not thread-safe: one host thread drives one engine (as the reference).
+ */
+#ifndef S2R_H
+#define S2R_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define S2R_ABI_VERSION 1
+#define S2R_PAGE_TOKENS 64 /* tokens per self-attention K/V page */
+#define S2R_NO_TARGET INT64_MAX
+
+typedef enum s2r_status {
+  S2R_OK = 0,
+  S2R_EINVAL = 1,   /* bad argument (the reference raises ValueError/IndexError) */
+  S2R_ECUDA = 2,    /* a CUDA call failed */
+  S2R_ENOMEM = 3,   /* device memory or K/V pages exhausted */
+  S2R_ESTATE = 4,   /* call out of order (e.g. take of a slot that is not loaded) */
+  S2R_ENOTSUP = 5,  /* shape the kernels do not support */
+  S2R_EDEVICE = 6   /* a kernel found a broken invariant, reported it and skipped its work */
+} s2r_status;
+
+typedef enum s2r_grammar_kind {
+  S2R_GRAMMAR_CLASS = 0, /* TokenGrammar: 13 token classes + per-slot state */
+  S2R_GRAMMAR_TABLE = 1  /* synthetic [states, vocab] table grammar */
+} s2r_grammar_kind;
+
+typedef enum s2r_dtype { S2R_F32 = 0, S2R_BF16 = 1 } s2r_dtype;
+
+/* Decoder shape and engine sizes.
+ * Replaces DecoderConfig (decoder.py:12-21) plus the BatchDecoder constructor
+ * arguments `batch` and `frames` (engine.py:55-66). */
+typedef struct s2r_config {
+  int32_t vocab_size;
+  int32_t width;      /* multiple of 64, at most 4096 */
+  int32_t layers;
+  int32_t heads;      /* width / heads must be 64 */
+  int32_t ffn_width;  /* multiple of 64, at most 4096 */
+  int32_t max_tokens; /* decoder context; position rows = max_tokens + 2 */
+  int32_t batch;      /* decode slots */
+  int32_t frames;     /* cross-attention frames held per slot */
+  int32_t kv_pages;   /* self K/V pool in pages of S2R_PAGE_TOKENS tokens;
+                         0 = batch * ceil(max_tokens / S2R_PAGE_TOKENS) */
+  int32_t flags;      /* S2R_FLAG_* */
+} s2r_config;
+
+#define S2R_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
+#define S2R_FLAG_NO_GRAPH 2u /* issue steps as plain launches, no CUDA graph */
+
+/* One decoder layer's float32 parameters, named as in
+ * TokenDecoder.state_dict() (decoder.py:28-84).  Linear weights are
+ * [out, in] row-major, as torch stores them. */
+typedef struct s2r_layer_weights {
+  const float *self_q_w, *self_q_b, *self_k_w, *self_k_b;
+  const float *self_v_w, *self_v_b, *self_out_w, *self_out_b;
+  const float *self_norm_w, *self_norm_b;
+  const float *cross_q_w, *cross_q_b, *cross_k_w, *cross_k_b;
+  const float *cross_v_w, *cross_v_b, *cross_out_w, *cross_out_b;
+  const float *cross_norm_w, *cross_norm_b;
+  const float *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+  const float *final_norm_w, *final_norm_b;
+} s2r_layer_weights;
+
+/* Replaces the weight copies BatchDecoder makes at construction
+ * (engine.py:118-123): Linear weights and biases and the tied output
+ * embedding are rounded to bfloat16 on the device; embeddings used for the
+ * lookup and LayerNorm parameters stay float32. */
+typedef struct s2r_weights {
+  const float* token_embedding;    /* [vocab_size, width] */
+  const float* position_embedding; /* [max_tokens + 2, width] */
+  const float* embedding_norm_w;   /* [width] */
+  const float* embedding_norm_b;   /* [width] */
+  const s2r_layer_weights* layers; /* [layers] (host array of structs) */
+} s2r_weights;
+
+/* Replaces TokenGrammar construction (grammar.py:79-97) or, for synthetic
+ * vocabularies, a table grammar.  Arrays are host or device memory. */
+typedef struct s2r_grammar {
+  int32_t kind;                  /* s2r_grammar_kind */
+  const int8_t* token_class;     /* CLASS: [vocab] class 0..12 of each token */
+  const int32_t* field_of_class; /* CLASS: [13] (grammar.py:52) */
+  const double* time_seconds;    /* [vocab] seconds of time tokens, -inf otherwise */
+  int32_t states;                /* TABLE: number of states */
+  int32_t multiplier;            /* TABLE: s' = (multiplier * s + token) mod states */
+  const uint8_t* table;          /* TABLE: [states, vocab] 1 = allowed */
+} s2r_grammar;
+
+typedef struct s2r_ctx s2r_ctx;
+
+/* ABI version of the loaded library (S2R_ABI_VERSION it was built with). */
+int32_t s2r_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* s2r_last_error(void);
+
+/* Build an engine on `device`: allocate caches and state, copy and round the
+ * weights, copy the grammar.  Every slot starts finished and unloaded.
+ * Replaces BatchDecoder.__init__ (engine.py:55-149). */
+int32_t s2r_create(const s2r_config* config, const s2r_weights* weights, const s2r_grammar* grammar,
+                   int32_t device, s2r_ctx** out);
+
+/* Free everything the engine owns.  Replaces dropping the engine
+ * (transcribe.py:212 frees the old caches before a rebuild). */
+int32_t s2r_destroy(s2r_ctx* ctx);
+
+/* Additive float32 bias on the logits of every slot ([vocab], NULL clears),
+ * applied after the bfloat16 logits are widened and before the grammar mask.
+ * Replaces the `mode_bias` term (engine.py:77-80,316-317). */
+int32_t s2r_set_logit_bias(s2r_ctx* ctx, const float* bias);
+
+/* Start `slot` on a window.  `memory` is the encoder memory
+ * [memory_frames, width] (float32 or bfloat16); cross-attention sees its
+ * first `frames` frames (1 <= frames <= min(memory_frames, config.frames)).
+ * `prefix` (host, n_prefix >= 1 tokens, containing OUT = 3) is prefilled: the
+ * K/V of prefix[0 .. n-2] are written, the grammar state is replayed from the
+ * token after OUT, and the slot resumes with token prefix[n-1] at position
+ * n-1 (n_prefix <= max_tokens - 1).  `stop_seconds` ends the slot at the
+ * first time token at or after it (+inf: never).  `target` is the table
+ * grammar's generated-token count (S2R_NO_TARGET: none).
+ * Replaces BatchDecoder.load (engine.py:180-232) without rescoring tables. */
+int32_t s2r_load_slot(s2r_ctx* ctx, int32_t slot, const void* memory, int32_t memory_dtype,
+                      int32_t memory_frames, int32_t frames, const int64_t* prefix, int32_t n_prefix,
+                      double stop_seconds, int64_t target, void* stream);
+
+/* Advance every slot by `n_steps` tokens; finished slots stay put.  No host
+ * synchronisation.  Replaces BatchDecoder.run (engine.py:234-246). */
+int32_t s2r_step(s2r_ctx* ctx, int32_t n_steps, void* stream);
+
+/* One step with test hooks (host arrays, each may be NULL): `forced[slot]` >=
+ * 0 commits that token instead of the greedy choice (teacher forcing);
+ * `logits` receives the raw float32 logits [batch, vocab] (bfloat16-rounded,
+ * before bias and mask); `greedy` receives the masked argmax of every slot.
+ * Synchronises `stream`.  No counterpart in the reference's engine; its
+ * teacher-forced logits come from TokenDecoder.forward (decoder.py:118-124). */
+int32_t s2r_step_debug(s2r_ctx* ctx, const int64_t* forced, float* logits, int64_t* greedy, void* stream);
+
+/* Copy the per-slot finished flags to host `finished` [batch] (synchronises).
+ * Returns S2R_EDEVICE if a kernel has reported an error since the last check.
+ * Replaces the device read of BatchDecoder.finished (engine.py:248-252). */
+int32_t s2r_poll_finished(s2r_ctx* ctx, uint8_t* finished, void* stream);
+
+/* Copy slot's tokens out[0 .. position] to host `tokens`, append EOS when the
+ * last token is not EOS, report the end reason (0 running, 1 eos, 2 stop,
+ * 3 limit) and release the slot's K/V pages.  Fails with S2R_EINVAL if
+ * `capacity` is too small (`*length` then holds the size needed).
+ * Replaces BatchDecoder.take (engine.py:254-262). */
+int32_t s2r_take(s2r_ctx* ctx, int32_t slot, int64_t* tokens, int32_t capacity, int32_t* length,
+                 int32_t* ended, void* stream);
+
+/* Device address, element count and dtype code (0 f32, 1 bf16, 2 i64, 3 u8,
+ * 4 f64, 5 i32) of a named engine buffer, for zero-copy views: "token",
+ * "position", "finished", "ended", "in_shift", "shift_run", "payload",
+ * "last_field", "incomplete", "g", "count", "target", "stop", "out",
+ * "frames". Replaces reads of BatchDecoder.state / .out (engine.py:138-144). */
+int32_t s2r_get_buffer(s2r_ctx* ctx, const char* name, void** ptr, int64_t* numel, int32_t* dtype);
+
+/* Run one decode step (it advances the slots like s2r_step) as a CUDA graph
+ * with an event node after every kernel and no overlap between kernels, and
+ * report per kernel
+ * class — 0 qkv, 1 self attention, 2 self out-projection, 3 cross q,
+ * 4 cross attention, 5 cross out-projection, 6 fc1, 7 fc2, 8 logits — the
+ * summed device time in ms, the algorithmic bytes of one launch and the
+ * launch count (host arrays of 9).  Synchronises `stream`.  Measurement only;
+ * no counterpart in the reference. */
+int32_t s2r_profile_step(s2r_ctx* ctx, float* ms, double* bytes, int32_t* launches, void* stream);
+
+/* Kernel launches one decode step issues (for launch accounting). */
+int32_t s2r_step_launches(s2r_ctx* ctx);
+
+/* K/V pages of the pool that no slot holds. */
+int32_t s2r_free_pages(s2r_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* S2R_H */

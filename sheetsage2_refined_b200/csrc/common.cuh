@@ -1,0 +1,101 @@
+// Shared device helpers for the decode-step kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace s2r {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kHeadDim = 64;
+constexpr int kPageTokens = 64;
+constexpr float kLnEps = 1e-5f;  // torch.nn.LayerNorm default
+
+// bfloat16 -> float of the low / high half of a packed pair.
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Round to bfloat16 (nearest, ties to even) and widen back.
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// 16-byte streaming load that does not allocate in L1 (weights, K/V).
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait until every kernel this one depends on has finished and
+// its writes are visible.  Both are no-ops when the launch has no PDL edge.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Which slot, position and input token a row of the current launch stands for.
+// Decode: row r is slot r with the slot's own token and position.  Prefill:
+// every row belongs to one slot, rows are consecutive positions from pos0 and
+// the tokens come from a device array.
+struct RowMap {
+  int prefill;            // 0 decode, 1 prefill
+  int slot;               // prefill slot
+  int pos0;               // prefill first position
+  const int32_t* tokens;  // prefill tokens [rows]
+};
+
+struct SlotState {
+  int64_t* token;
+  int64_t* position;
+  uint8_t* finished;
+  int64_t* ended;
+  uint8_t* in_shift;
+  int64_t* shift_run;
+  int64_t* payload;
+  int64_t* last_field;
+  int64_t* incomplete;
+  int64_t* g;
+  int64_t* count;
+  int64_t* target;
+  double* stop;
+  int64_t* out;         // [batch, max_tokens]
+  int32_t* frames;      // real cross frames per slot
+  int32_t* page_table;  // [batch, pages_per_slot]
+};
+
+__device__ __forceinline__ int row_slot(const RowMap& rm, int r) { return rm.prefill ? rm.slot : r; }
+__device__ __forceinline__ int row_pos(const RowMap& rm, const SlotState& st, int r) {
+  return rm.prefill ? rm.pos0 + r : (int)st.position[r];
+}
+__device__ __forceinline__ int row_token(const RowMap& rm, const SlotState& st, int r) {
+  return rm.prefill ? rm.tokens[r] : (int)st.token[r];
+}
+__device__ __forceinline__ bool row_active(const RowMap& rm, const SlotState& st, int r) {
+  return rm.prefill ? true : st.finished[r] == 0;
+}
+
+// Address of token t's 64-dim vector of head h in a paged K or V pool laid
+// out [page][head][kPageTokens][kHeadDim].
+__device__ __forceinline__ size_t paged_offset(const int32_t* page_table, int pages_per_slot, int heads, int slot,
+                                               int h, int t) {
+  int page = page_table[(size_t)slot * pages_per_slot + (t / kPageTokens)];
+  return (((size_t)page * heads + h) * kPageTokens + (t % kPageTokens)) * kHeadDim;
+}
+
+}  // namespace s2r

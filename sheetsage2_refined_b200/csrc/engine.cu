@@ -1,0 +1,1097 @@
+// Host side of the decode engine and the C ABI declared in include/s2r.h.
+//
+// The engine owns every device buffer of a BatchDecoder
+// (sheetsage2_refined/engine.py:118-149): bfloat16 weight copies, the paged
+// self K/V pool, per-slot cross K/V, activations of one step, the slot state
+// and the output tokens.  A decode step is a fixed sequence of kernel
+// launches (8 per layer + 1) that reads every per-slot quantity (token,
+// position, real frames, grammar state) from device memory, so one CUDA graph
+// captured once serves every step, whatever the slots' lengths; consecutive
+// kernels are chained with programmatic dependent launch so that each one
+// starts streaming its weights while the previous one finishes.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/s2r.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "logits.cuh"
+#include "proj.cuh"
+
+using namespace s2r;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CK(call)                                                                                  \
+  do {                                                                                            \
+    cudaError_t err_ = (call);                                                                    \
+    if (err_ != cudaSuccess) return fail(S2R_ECUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(err_), __FILE__, __LINE__); \
+  } while (0)
+
+constexpr int kPrefillRows = 64;
+
+int kch_for(int k) { return k <= 256 ? 1 : k <= 512 ? 2 : k <= 1024 ? 4 : k <= 2048 ? 8 : 16; }
+int mc_for(int m) { return m >= 5 ? 8 : m >= 3 ? 4 : m; }
+
+// Launch with optional programmatic dependent launch and cluster shape.
+template <typename Arg>
+cudaError_t launch_ex(void (*kernel)(Arg), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      int cluster, const Arg& arg) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (pdl) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 0) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = cluster;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, arg);
+}
+
+typedef void (*ProjFn)(const ProjArgs);
+typedef void (*LogitsFn)(const LogitsArgs);
+
+template <int IN, int EPI, int KCH>
+ProjFn pick_mc(int mc) {
+  switch (mc) {
+    case 1: return proj_kernel<KCH, 1, IN, EPI>;
+    case 2: return proj_kernel<KCH, 2, IN, EPI>;
+    case 4: return proj_kernel<KCH, 4, IN, EPI>;
+    default: return proj_kernel<KCH, 8, IN, EPI>;
+  }
+}
+
+template <int IN, int EPI>
+ProjFn pick_proj(int kch, int mc) {
+  switch (kch) {
+    case 1: return pick_mc<IN, EPI, 1>(mc);
+    case 2: return pick_mc<IN, EPI, 2>(mc);
+    case 4: return pick_mc<IN, EPI, 4>(mc);
+    case 8: return pick_mc<IN, EPI, 8>(mc);
+    default: return pick_mc<IN, EPI, 16>(mc);
+  }
+}
+
+ProjFn proj_fn(int in, int epi, int kch, int mc) {
+  if (in == IN_EMBED && epi == EPI_QKV) return pick_proj<IN_EMBED, EPI_QKV>(kch, mc);
+  if (in == IN_LN && epi == EPI_QKV) return pick_proj<IN_LN, EPI_QKV>(kch, mc);
+  if (in == IN_LN && epi == EPI_BF16) return pick_proj<IN_LN, EPI_BF16>(kch, mc);
+  if (in == IN_LN && epi == EPI_GELU) return pick_proj<IN_LN, EPI_GELU>(kch, mc);
+  if (in == IN_BF16 && epi == EPI_RESID) return pick_proj<IN_BF16, EPI_RESID>(kch, mc);
+  if (in == IN_BF16 && epi == EPI_CROSSKV) return pick_proj<IN_BF16, EPI_CROSSKV>(kch, mc);
+  if (in == IN_F32 && epi == EPI_CROSSKV) return pick_proj<IN_F32, EPI_CROSSKV>(kch, mc);
+  return nullptr;
+}
+
+template <int KCH>
+LogitsFn pick_logits_mc(int mc) {
+  switch (mc) {
+    case 1: return logits_kernel<KCH, 1>;
+    case 2: return logits_kernel<KCH, 2>;
+    case 4: return logits_kernel<KCH, 4>;
+    default: return logits_kernel<KCH, 8>;
+  }
+}
+
+LogitsFn logits_fn(int kch, int mc) {
+  switch (kch) {
+    case 1: return pick_logits_mc<1>(mc);
+    case 2: return pick_logits_mc<2>(mc);
+    case 4: return pick_logits_mc<4>(mc);
+    case 8: return pick_logits_mc<8>(mc);
+    default: return pick_logits_mc<16>(mc);
+  }
+}
+
+// Host replay of the class grammar (grammar.py:140-180), used for prefixes.
+struct HostGrammarState {
+  uint8_t in_shift = 1, finished = 0;
+  int64_t shift_run = 0, payload = 0, last_field = -1, incomplete = 0, ended = 0, g = 0;
+};
+
+}  // namespace
+
+struct LayerBufs {
+  bf16 *wqkv, *bqkv, *wo, *bo, *wcq, *bcq, *wckv, *bckv, *wco, *bco, *w1, *b1, *w2, *b2;
+  float *ln_self_g, *ln_self_b, *ln_cross_g, *ln_cross_b, *ln_final_g, *ln_final_b;
+  bf16 *kpool, *vpool, *ck, *cv;
+};
+
+struct s2r_ctx {
+  s2r_config cfg{};
+  int device = 0;
+  int D = 0, H = 0, F = 0, FFN = 0, V = 0, L = 0, B = 0, T = 0, maxM = 0, pps = 0, n_pages = 0;
+  int num_sms = 148;
+  bool pdl = true, use_graph = true;
+  std::vector<void*> allocs;
+  // weights
+  float *tok_emb = nullptr, *pos_emb = nullptr, *emb_ln_g = nullptr, *emb_ln_b = nullptr;
+  bf16* emb_bf16 = nullptr;
+  std::vector<LayerBufs> layers;
+  // activations of one step
+  float *r = nullptr, *x = nullptr;
+  bf16 *q = nullptr, *att = nullptr, *hid = nullptr;
+  void* mem_stage = nullptr;
+  int32_t* prefill_tokens = nullptr;
+  unsigned long long* keys = nullptr;
+  unsigned int* counter = nullptr;
+  int* dev_error = nullptr;  // set by kernels on a broken invariant (0: none)
+  float* bias = nullptr;
+  bool has_bias = false;
+  int64_t* dbg_forced = nullptr;
+  float* dbg_logits = nullptr;
+  int64_t* dbg_greedy = nullptr;
+  SlotState st{};
+  Grammar gr{};
+  // host copies for prefix replay
+  std::vector<int8_t> h_token_class;
+  std::vector<int32_t> h_field;
+  std::vector<double> h_time;
+  // slots
+  std::vector<int> loaded, bound;
+  std::vector<std::vector<int>> slot_pages;
+  std::vector<int> free_pages;
+  std::vector<int32_t> h_page_table;
+  // graph
+  cudaGraphExec_t graph = nullptr;
+  bool graph_dirty = true;
+  cudaStream_t cap_stream = nullptr;
+  // profiling: when set, an event is recorded after every launch of a step
+  std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(s2r_ctx* c, T** p, size_t count) {
+  void* ptr = nullptr;
+  cudaError_t e = cudaMalloc(&ptr, std::max<size_t>(count, 1) * sizeof(T));
+  if (e != cudaSuccess) return fail(S2R_ENOMEM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+  c->allocs.push_back(ptr);
+  *p = static_cast<T*>(ptr);
+  return S2R_OK;
+}
+
+#define TRY(x)                  \
+  do {                          \
+    int rc_ = (x);              \
+    if (rc_ != S2R_OK) return rc_; \
+  } while (0)
+
+enum KernelClass { K_QKV = 0, K_SELF_ATTN, K_SELF_OUT, K_CROSS_Q, K_CROSS_ATTN, K_CROSS_OUT, K_FC1, K_FC2, K_LOGITS, K_CLASSES };
+
+int mark(s2r_ctx* c, int cls, cudaStream_t s) {
+  if (!c->prof) return S2R_OK;
+  cudaEvent_t e;
+  CK(cudaEventCreate(&e));
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(s, &cap));
+  if (cap == cudaStreamCaptureStatusActive)
+    CK(cudaEventRecordWithFlags(e, s, cudaEventRecordExternal));  // an event node of the graph
+  else
+    CK(cudaEventRecord(e, s));
+  c->prof->push_back({cls, e});
+  return S2R_OK;
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restrict__ dst, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+// Copy float32 weights (host or device) into `dst` as bfloat16, through a
+// float32 staging buffer.
+int upload_bf16(s2r_ctx* c, bf16* dst, const float* src, size_t n, float* stage) {
+  if (!src) return fail(S2R_EINVAL, "a weight pointer is NULL");
+  CK(cudaMemcpy(stage, src, n * sizeof(float), cudaMemcpyDefault));
+  f32_to_bf16_kernel<<<std::min<size_t>((n + 255) / 256, 4096), 256>>>(stage, dst, n);
+  CK(cudaGetLastError());
+  return S2R_OK;
+}
+
+int upload_f32(float* dst, const float* src, size_t n) {
+  if (!src) return fail(S2R_EINVAL, "a weight pointer is NULL");
+  CK(cudaMemcpy(dst, src, n * sizeof(float), cudaMemcpyDefault));
+  return S2R_OK;
+}
+
+ProjArgs proj_base(s2r_ctx* c) {
+  ProjArgs a{};
+  a.st = c->st;
+  a.heads = c->H;
+  a.pages_per_slot = c->pps;
+  a.frames_cap = c->F;
+  return a;
+}
+
+int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
+  const int kch = kch_for(a.K), mc = mc_for(std::min(a.M, 8));
+  ProjFn fn = proj_fn(in, epi, kch, mc);
+  if (!fn) return fail(S2R_ENOTSUP, "no projection kernel for in=%d epi=%d", in, epi);
+  const size_t smem = (size_t)(mc == 8 ? 8 : mc) * kch * 256 * sizeof(bf16);
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int blocks = (a.N + 3) / 4;
+  CK(launch_ex(fn, dim3(blocks), dim3(128), smem, s, c->pdl, 0, a));
+  return S2R_OK;
+}
+
+// Every (row, head) is split over the same number of CTAs whatever the batch,
+// so a row's result never depends on how many rows share the launch (decode
+// at any batch and prefill chunks give bit-identical K/V and outputs).
+constexpr int kAttnSplits = 8;
+
+int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s) {
+  AttnArgs a{};
+  a.M = M;
+  a.H = c->H;
+  a.rm = rm;
+  a.st = c->st;
+  a.q = c->q;
+  a.ldq = c->D;
+  a.out = c->att;
+  a.ldo = c->D;
+  a.cross = cross;
+  a.k = cross ? c->layers[layer].ck : c->layers[layer].kpool;
+  a.v = cross ? c->layers[layer].cv : c->layers[layer].vpool;
+  a.pages_per_slot = c->pps;
+  a.frames_cap = c->F;
+  a.splits = kAttnSplits;
+  a.err = c->dev_error;
+  const int C = kAttnSplits;
+  const int maxlen = cross ? c->F : c->T;
+  a.chunk_cap = (maxlen + C - 1) / C;
+  const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
+  CK(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(launch_ex(attn_kernel, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, c->pdl, C, a));
+  return S2R_OK;
+}
+
+// One decoder layer for M rows.  `last_kv_only`: only the K/V append (the
+// prefill's last layer needs nothing else).
+int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaStream_t s) {
+  const LayerBufs& w = c->layers[l];
+  const int D = c->D;
+  {  // 1. (embedding +) LayerNorm -> QKV, K/V append
+    ProjArgs a = proj_base(c);
+    a.rm = rm;
+    a.M = M;
+    a.K = D;
+    a.N = 3 * D;
+    if (l == 0) {
+      a.tok_emb = c->tok_emb;
+      a.pos_emb = c->pos_emb;
+      a.gamma = c->emb_ln_g;
+      a.beta = c->emb_ln_b;
+    } else {
+      a.r = c->r;
+      a.gamma = c->layers[l - 1].ln_final_g;
+      a.beta = c->layers[l - 1].ln_final_b;
+    }
+    a.x_out = c->x;
+    a.W = w.wqkv;
+    a.bias = w.bqkv;
+    a.out = c->q;
+    a.ldo = D;
+    a.k_dst = w.kpool;
+    a.v_dst = w.vpool;
+    TRY(launch_proj(c, a, l == 0 ? IN_EMBED : IN_LN, EPI_QKV, s));
+    TRY(mark(c, K_QKV, s));
+  }
+  if (last_kv_only) return S2R_OK;
+  TRY(launch_attn(c, rm, M, l, false, s));  // 2. self-attention
+  TRY(mark(c, K_SELF_ATTN, s));
+  {                                         // 3. out-projection + residual
+    ProjArgs a = proj_base(c);
+    a.rm = rm;
+    a.M = M;
+    a.K = D;
+    a.N = D;
+    a.xin = c->att;
+    a.ldx = D;
+    a.W = w.wo;
+    a.bias = w.bo;
+    a.r_out = c->r;
+    a.x_res = c->x;
+    TRY(launch_proj(c, a, IN_BF16, EPI_RESID, s));
+    TRY(mark(c, K_SELF_OUT, s));
+  }
+  {  // 4. self_attn_norm -> cross q
+    ProjArgs a = proj_base(c);
+    a.rm = rm;
+    a.M = M;
+    a.K = D;
+    a.N = D;
+    a.r = c->r;
+    a.gamma = w.ln_self_g;
+    a.beta = w.ln_self_b;
+    a.x_out = c->x;
+    a.W = w.wcq;
+    a.bias = w.bcq;
+    a.out = c->q;
+    a.ldo = D;
+    TRY(launch_proj(c, a, IN_LN, EPI_BF16, s));
+    TRY(mark(c, K_CROSS_Q, s));
+  }
+  TRY(launch_attn(c, rm, M, l, true, s));  // 5. cross-attention
+  TRY(mark(c, K_CROSS_ATTN, s));
+  {                                        // 6. cross out-projection + residual
+    ProjArgs a = proj_base(c);
+    a.rm = rm;
+    a.M = M;
+    a.K = D;
+    a.N = D;
+    a.xin = c->att;
+    a.ldx = D;
+    a.W = w.wco;
+    a.bias = w.bco;
+    a.r_out = c->r;
+    a.x_res = c->x;
+    TRY(launch_proj(c, a, IN_BF16, EPI_RESID, s));
+    TRY(mark(c, K_CROSS_OUT, s));
+  }
+  {  // 7. cross_attn_norm -> fc1 + GELU
+    ProjArgs a = proj_base(c);
+    a.rm = rm;
+    a.M = M;
+    a.K = D;
+    a.N = c->FFN;
+    a.r = c->r;
+    a.gamma = w.ln_cross_g;
+    a.beta = w.ln_cross_b;
+    a.x_out = c->x;
+    a.W = w.w1;
+    a.bias = w.b1;
+    a.out = c->hid;
+    a.ldo = c->FFN;
+    TRY(launch_proj(c, a, IN_LN, EPI_GELU, s));
+    TRY(mark(c, K_FC1, s));
+  }
+  {  // 8. fc2 + residual
+    ProjArgs a = proj_base(c);
+    a.rm = rm;
+    a.M = M;
+    a.K = c->FFN;
+    a.N = D;
+    a.xin = c->hid;
+    a.ldx = c->FFN;
+    a.W = w.w2;
+    a.bias = w.b2;
+    a.r_out = c->r;
+    a.x_res = c->x;
+    TRY(launch_proj(c, a, IN_BF16, EPI_RESID, s));
+    TRY(mark(c, K_FC2, s));
+  }
+  return S2R_OK;
+}
+
+int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logits, int64_t* greedy) {
+  RowMap rm{0, 0, 0, nullptr};
+  for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, c->B, l, false, s));
+  LogitsArgs a{};
+  a.M = c->B;
+  a.V = c->V;
+  a.D = c->D;
+  a.max_tokens = c->T;
+  a.st = c->st;
+  a.gr = c->gr;
+  a.r = c->r;
+  a.gamma = c->layers[c->L - 1].ln_final_g;
+  a.beta = c->layers[c->L - 1].ln_final_b;
+  a.emb = c->emb_bf16;
+  a.bias = c->has_bias ? c->bias : nullptr;
+  a.keys = c->keys;
+  a.counter = c->counter;
+  a.forced = forced;
+  a.logits_out = logits;
+  a.greedy_out = greedy;
+  const int kch = kch_for(c->D), mc = mc_for(std::min(c->B, 8));
+  LogitsFn fn = logits_fn(kch, mc);
+  const size_t smem = (size_t)mc * kch * 256 * sizeof(bf16);
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int blocks = std::max(1, std::min((c->V + 7) / 8, 2 * c->num_sms));
+  CK(launch_ex(fn, dim3(blocks), dim3(kLogitsThreads), smem, s, c->pdl, 0, a));
+  TRY(mark(c, K_LOGITS, s));
+  return S2R_OK;
+}
+
+int ensure_graph(s2r_ctx* c) {
+  if (!c->graph_dirty && c->graph) return S2R_OK;
+  if (c->graph) {
+    cudaGraphExecDestroy(c->graph);
+    c->graph = nullptr;
+  }
+  CK(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(c, c->cap_stream, nullptr, nullptr, nullptr);
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(c->cap_stream, &graph);
+  if (rc != S2R_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return fail(S2R_ECUDA, "graph capture: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&c->graph, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return fail(S2R_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  c->graph_dirty = false;
+  return S2R_OK;
+}
+
+void release_pages(s2r_ctx* c, int slot) {
+  for (int p : c->slot_pages[slot]) c->free_pages.push_back(p);
+  c->slot_pages[slot].clear();
+}
+
+// Give `slot` pages for positions 0..last; returns S2R_ENOMEM if the pool is empty.
+int grow_pages(s2r_ctx* c, int slot, int last, bool* changed) {
+  const int need = last / kPageTokens + 1;
+  while ((int)c->slot_pages[slot].size() < need) {
+    if (c->free_pages.empty()) return fail(S2R_ENOMEM, "K/V page pool exhausted (%d pages)", c->n_pages);
+    const int p = c->free_pages.back();
+    c->free_pages.pop_back();
+    c->h_page_table[(size_t)slot * c->pps + c->slot_pages[slot].size()] = p;
+    c->slot_pages[slot].push_back(p);
+    *changed = true;
+  }
+  return S2R_OK;
+}
+
+int upload_page_row(s2r_ctx* c, int slot, cudaStream_t s) {
+  CK(cudaMemcpyAsync(c->st.page_table + (size_t)slot * c->pps, c->h_page_table.data() + (size_t)slot * c->pps,
+                     c->pps * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  return S2R_OK;
+}
+
+void replay_class(const s2r_ctx* c, HostGrammarState& st, int64_t tok) {
+  const int kind = c->h_token_class[tok];
+  const bool is_shift = kind == kShiftT, is_field = kind != kShiftT && kind != kEosT;
+  const bool new_event = is_shift && !st.in_shift && st.payload > 0;
+  int64_t payload = new_event ? 0 : st.payload;
+  if (is_field) payload += 1;
+  int64_t last = new_event ? -1 : st.last_field;
+  if (is_field) last = c->h_field[kind];
+  int64_t inc = new_event ? kNone : st.incomplete;
+  if (is_field) inc = kind == kMeterT ? kAfterMeter : kind == kPitchT ? kAfterPitch : kind == kBassT ? kAfterBass : kNone;
+  const uint8_t in_shift = is_shift ? 1 : (is_field ? 0 : st.in_shift);
+  const int64_t run = is_shift ? st.shift_run + 1 : (is_field ? 0 : st.shift_run);
+  const bool eos = kind == kEosT;
+  const bool stopped = kind == kTimeT && c->h_time[tok] >= INFINITY;  // prefixes replay with stop = +inf
+  st.payload = payload;
+  st.last_field = last;
+  st.incomplete = inc;
+  st.in_shift = in_shift;
+  st.shift_run = run;
+  if (eos || stopped) {
+    st.ended = eos ? 1 : 2;
+    st.finished = 1;
+  }
+}
+
+// Read (and clear) the device error word after the stream's work has finished.
+int check_device_error(s2r_ctx* c, cudaStream_t s) {
+  int err = 0;
+  CK(cudaMemcpyAsync(&err, c->dev_error, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (err == 0) return S2R_OK;
+  CK(cudaMemsetAsync(c->dev_error, 0, sizeof(int), s));
+  return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
+              err == kErrAttnCluster ? "attention launched without its cluster shape"
+                                     : "attention keys exceed the score buffer");
+}
+
+template <typename T>
+int put(T* dev, int slot, T value, cudaStream_t s) {
+  CK(cudaMemcpyAsync(dev + slot, &value, sizeof(T), cudaMemcpyHostToDevice, s));
+  return S2R_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t s2r_abi_version(void) { return S2R_ABI_VERSION; }
+
+const char* s2r_last_error(void) { return g_last_error.c_str(); }
+
+int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_grammar* g, int32_t device, s2r_ctx** out) {
+  if (!cfg || !w || !g || !out) return fail(S2R_EINVAL, "s2r_create: NULL argument");
+  *out = nullptr;
+  const s2r_config k = *cfg;
+  if (k.width <= 0 || k.heads <= 0 || k.width != k.heads * kHeadDim)
+    return fail(S2R_ENOTSUP, "width must be heads * 64 (width %d, heads %d)", k.width, k.heads);
+  if (k.width % 64 || k.width > 4096 || k.ffn_width <= 0 || k.ffn_width % 64 || k.ffn_width > 4096)
+    return fail(S2R_ENOTSUP, "width and ffn_width must be multiples of 64 up to 4096");
+  if (k.layers <= 0 || k.vocab_size <= 4 || k.max_tokens < 2 || k.batch <= 0 || k.frames <= 0)
+    return fail(S2R_EINVAL, "invalid sizes (layers %d vocab %d max_tokens %d batch %d frames %d)", k.layers,
+                k.vocab_size, k.max_tokens, k.batch, k.frames);
+  if (g->kind != S2R_GRAMMAR_CLASS && g->kind != S2R_GRAMMAR_TABLE) return fail(S2R_EINVAL, "unknown grammar kind");
+  if (g->kind == S2R_GRAMMAR_CLASS && (!g->token_class || !g->field_of_class || !g->time_seconds))
+    return fail(S2R_EINVAL, "class grammar needs token_class, field_of_class and time_seconds");
+  if (g->kind == S2R_GRAMMAR_TABLE && (!g->table || g->states <= 0))
+    return fail(S2R_EINVAL, "table grammar needs a table and states > 0");
+  if (!w->layers) return fail(S2R_EINVAL, "weights.layers is NULL");
+
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(S2R_EINVAL, "device %d out of range (%d devices)", device, ndev);
+  CK(cudaSetDevice(device));
+
+  s2r_ctx* c = new s2r_ctx();
+  c->cfg = k;
+  c->device = device;
+  c->D = k.width;
+  c->H = k.heads;
+  c->F = k.frames;
+  c->FFN = k.ffn_width;
+  c->V = k.vocab_size;
+  c->L = k.layers;
+  c->B = k.batch;
+  c->T = k.max_tokens;
+  c->maxM = std::max(k.batch, kPrefillRows);
+  c->pps = (k.max_tokens + kPageTokens - 1) / kPageTokens;
+  c->n_pages = k.kv_pages > 0 ? k.kv_pages : k.batch * c->pps;
+  c->pdl = !(k.flags & S2R_FLAG_NO_PDL);
+  c->use_graph = !(k.flags & S2R_FLAG_NO_GRAPH);
+  cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  auto cleanup = [&](int rc) {
+    s2r_destroy(c);
+    return rc;
+  };
+#define TRYC(x)                    \
+  do {                             \
+    int rc_ = (x);                 \
+    if (rc_ != S2R_OK) return cleanup(rc_); \
+  } while (0)
+
+  const size_t D = c->D, V = c->V, FFN = c->FFN, T = c->T;
+  // weights
+  TRYC(dalloc(c, &c->tok_emb, V * D));
+  TRYC(dalloc(c, &c->pos_emb, (T + 2) * D));
+  TRYC(dalloc(c, &c->emb_ln_g, D));
+  TRYC(dalloc(c, &c->emb_ln_b, D));
+  TRYC(dalloc(c, &c->emb_bf16, V * D));
+  float* stage = nullptr;
+  TRYC(dalloc(c, &stage, std::max(V * D, std::max(3 * D * D, FFN * D))));
+  TRYC(upload_f32(c->tok_emb, w->token_embedding, V * D));
+  TRYC(upload_f32(c->pos_emb, w->position_embedding, (T + 2) * D));
+  TRYC(upload_f32(c->emb_ln_g, w->embedding_norm_w, D));
+  TRYC(upload_f32(c->emb_ln_b, w->embedding_norm_b, D));
+  TRYC(upload_bf16(c, c->emb_bf16, w->token_embedding, V * D, stage));
+  c->layers.resize(c->L);
+  const size_t pool = (size_t)c->n_pages * c->H * kPageTokens * kHeadDim;
+  const size_t cross = (size_t)c->B * c->H * c->F * kHeadDim;
+  for (int l = 0; l < c->L; ++l) {
+    const s2r_layer_weights& lw = w->layers[l];
+    LayerBufs& b = c->layers[l];
+    TRYC(dalloc(c, &b.wqkv, 3 * D * D));
+    TRYC(dalloc(c, &b.bqkv, 3 * D));
+    TRYC(dalloc(c, &b.wo, D * D));
+    TRYC(dalloc(c, &b.bo, D));
+    TRYC(dalloc(c, &b.wcq, D * D));
+    TRYC(dalloc(c, &b.bcq, D));
+    TRYC(dalloc(c, &b.wckv, 2 * D * D));
+    TRYC(dalloc(c, &b.bckv, 2 * D));
+    TRYC(dalloc(c, &b.wco, D * D));
+    TRYC(dalloc(c, &b.bco, D));
+    TRYC(dalloc(c, &b.w1, FFN * D));
+    TRYC(dalloc(c, &b.b1, FFN));
+    TRYC(dalloc(c, &b.w2, D * FFN));
+    TRYC(dalloc(c, &b.b2, D));
+    TRYC(dalloc(c, &b.ln_self_g, D));
+    TRYC(dalloc(c, &b.ln_self_b, D));
+    TRYC(dalloc(c, &b.ln_cross_g, D));
+    TRYC(dalloc(c, &b.ln_cross_b, D));
+    TRYC(dalloc(c, &b.ln_final_g, D));
+    TRYC(dalloc(c, &b.ln_final_b, D));
+    TRYC(dalloc(c, &b.kpool, pool));
+    TRYC(dalloc(c, &b.vpool, pool));
+    TRYC(dalloc(c, &b.ck, cross));
+    TRYC(dalloc(c, &b.cv, cross));
+    TRYC(upload_bf16(c, b.wqkv, lw.self_q_w, D * D, stage));
+    TRYC(upload_bf16(c, b.wqkv + D * D, lw.self_k_w, D * D, stage));
+    TRYC(upload_bf16(c, b.wqkv + 2 * D * D, lw.self_v_w, D * D, stage));
+    TRYC(upload_bf16(c, b.bqkv, lw.self_q_b, D, stage));
+    TRYC(upload_bf16(c, b.bqkv + D, lw.self_k_b, D, stage));
+    TRYC(upload_bf16(c, b.bqkv + 2 * D, lw.self_v_b, D, stage));
+    TRYC(upload_bf16(c, b.wo, lw.self_out_w, D * D, stage));
+    TRYC(upload_bf16(c, b.bo, lw.self_out_b, D, stage));
+    TRYC(upload_bf16(c, b.wcq, lw.cross_q_w, D * D, stage));
+    TRYC(upload_bf16(c, b.bcq, lw.cross_q_b, D, stage));
+    TRYC(upload_bf16(c, b.wckv, lw.cross_k_w, D * D, stage));
+    TRYC(upload_bf16(c, b.wckv + D * D, lw.cross_v_w, D * D, stage));
+    TRYC(upload_bf16(c, b.bckv, lw.cross_k_b, D, stage));
+    TRYC(upload_bf16(c, b.bckv + D, lw.cross_v_b, D, stage));
+    TRYC(upload_bf16(c, b.wco, lw.cross_out_w, D * D, stage));
+    TRYC(upload_bf16(c, b.bco, lw.cross_out_b, D, stage));
+    TRYC(upload_bf16(c, b.w1, lw.fc1_w, FFN * D, stage));
+    TRYC(upload_bf16(c, b.b1, lw.fc1_b, FFN, stage));
+    TRYC(upload_bf16(c, b.w2, lw.fc2_w, D * FFN, stage));
+    TRYC(upload_bf16(c, b.b2, lw.fc2_b, D, stage));
+    TRYC(upload_f32(b.ln_self_g, lw.self_norm_w, D));
+    TRYC(upload_f32(b.ln_self_b, lw.self_norm_b, D));
+    TRYC(upload_f32(b.ln_cross_g, lw.cross_norm_w, D));
+    TRYC(upload_f32(b.ln_cross_b, lw.cross_norm_b, D));
+    TRYC(upload_f32(b.ln_final_g, lw.final_norm_w, D));
+    TRYC(upload_f32(b.ln_final_b, lw.final_norm_b, D));
+    CK(cudaMemset(b.kpool, 0, pool * sizeof(bf16)));
+    CK(cudaMemset(b.vpool, 0, pool * sizeof(bf16)));
+    CK(cudaMemset(b.ck, 0, cross * sizeof(bf16)));
+    CK(cudaMemset(b.cv, 0, cross * sizeof(bf16)));
+  }
+  // activations
+  const size_t M = c->maxM;
+  TRYC(dalloc(c, &c->r, M * D));
+  TRYC(dalloc(c, &c->x, M * D));
+  TRYC(dalloc(c, &c->q, M * D));
+  TRYC(dalloc(c, &c->att, M * D));
+  TRYC(dalloc(c, &c->hid, M * FFN));
+  float* mem_stage = nullptr;
+  TRYC(dalloc(c, &mem_stage, (size_t)c->F * D));
+  c->mem_stage = mem_stage;
+  TRYC(dalloc(c, &c->prefill_tokens, kPrefillRows));
+  TRYC(dalloc(c, &c->keys, c->B));
+  TRYC(dalloc(c, &c->counter, 1));
+  TRYC(dalloc(c, &c->dev_error, 1));
+  CK(cudaMemset(c->dev_error, 0, sizeof(int)));
+  TRYC(dalloc(c, &c->bias, V));
+  TRYC(dalloc(c, &c->dbg_forced, c->B));
+  TRYC(dalloc(c, &c->dbg_logits, (size_t)c->B * V));
+  TRYC(dalloc(c, &c->dbg_greedy, c->B));
+  CK(cudaMemset(c->keys, 0, c->B * sizeof(unsigned long long)));
+  CK(cudaMemset(c->counter, 0, sizeof(unsigned int)));
+  CK(cudaMemset(c->bias, 0, V * sizeof(float)));
+  CK(cudaMemset(c->r, 0, M * D * sizeof(float)));
+  CK(cudaMemset(c->x, 0, M * D * sizeof(float)));
+  // slot state (engine.py:138-146, grammar.py:99-112): every slot starts finished
+  SlotState& st = c->st;
+  const size_t B = c->B;
+  TRYC(dalloc(c, &st.token, B));
+  TRYC(dalloc(c, &st.position, B));
+  TRYC(dalloc(c, &st.finished, B));
+  TRYC(dalloc(c, &st.ended, B));
+  TRYC(dalloc(c, &st.in_shift, B));
+  TRYC(dalloc(c, &st.shift_run, B));
+  TRYC(dalloc(c, &st.payload, B));
+  TRYC(dalloc(c, &st.last_field, B));
+  TRYC(dalloc(c, &st.incomplete, B));
+  TRYC(dalloc(c, &st.g, B));
+  TRYC(dalloc(c, &st.count, B));
+  TRYC(dalloc(c, &st.target, B));
+  TRYC(dalloc(c, &st.stop, B));
+  TRYC(dalloc(c, &st.out, B * T));
+  TRYC(dalloc(c, &st.frames, B));
+  TRYC(dalloc(c, &st.page_table, B * c->pps));
+  {
+    std::vector<int64_t> eos(B, 2), zeros(B, 0), minus(B, -1), none(B, INT64_MAX);
+    std::vector<uint8_t> ones(B, 1);
+    std::vector<double> inf(B, INFINITY);
+    std::vector<int32_t> frames(B, c->F);
+    CK(cudaMemcpy(st.token, eos.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.position, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.finished, ones.data(), B, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.ended, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.in_shift, ones.data(), B, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.shift_run, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.payload, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.last_field, minus.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.incomplete, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.g, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.count, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.target, none.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(st.stop, inf.data(), B * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemset(st.out, 0, B * T * 8));
+    CK(cudaMemcpy(st.frames, frames.data(), B * 4, cudaMemcpyHostToDevice));
+  }
+  c->h_page_table.assign(B * c->pps, 0);
+  CK(cudaMemset(st.page_table, 0, B * c->pps * sizeof(int32_t)));
+  for (int p = c->n_pages - 1; p >= 0; --p) c->free_pages.push_back(p);
+  c->slot_pages.assign(B, {});
+  c->loaded.assign(B, 0);
+  c->bound.assign(B, 0);
+  // grammar
+  Grammar& gr = c->gr;
+  gr.kind = g->kind;
+  if (g->kind == S2R_GRAMMAR_CLASS) {
+    c->h_token_class.resize(V);
+    c->h_field.resize(13);
+    c->h_time.resize(V);
+    CK(cudaMemcpy(c->h_token_class.data(), g->token_class, V, cudaMemcpyDefault));
+    CK(cudaMemcpy(c->h_field.data(), g->field_of_class, 13 * 4, cudaMemcpyDefault));
+    CK(cudaMemcpy(c->h_time.data(), g->time_seconds, V * 8, cudaMemcpyDefault));
+    for (size_t v = 0; v < V; ++v)
+      if (c->h_token_class[v] < 0 || c->h_token_class[v] > 12) {
+        return cleanup(fail(S2R_EINVAL, "token_class[%zu] = %d is not a class 0..12", v, c->h_token_class[v]));
+      }
+    int8_t* tc = nullptr;
+    int32_t* fc = nullptr;
+    double* ts = nullptr;
+    TRYC(dalloc(c, &tc, V));
+    TRYC(dalloc(c, &fc, 13));
+    TRYC(dalloc(c, &ts, V));
+    CK(cudaMemcpy(tc, c->h_token_class.data(), V, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(fc, c->h_field.data(), 13 * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ts, c->h_time.data(), V * 8, cudaMemcpyHostToDevice));
+    gr.token_class = tc;
+    gr.field_of_class = fc;
+    gr.time_seconds = ts;
+  } else {
+    uint8_t* tb = nullptr;
+    TRYC(dalloc(c, &tb, (size_t)g->states * V));
+    CK(cudaMemcpy(tb, g->table, (size_t)g->states * V, cudaMemcpyDefault));
+    gr.table = tb;
+    gr.states = g->states;
+    gr.multiplier = g->multiplier;
+  }
+  CK(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
+  CK(cudaDeviceSynchronize());
+  *out = c;
+  return S2R_OK;
+#undef TRYC
+}
+
+int32_t s2r_destroy(s2r_ctx* c) {
+  if (!c) return S2R_OK;
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  if (c->graph) cudaGraphExecDestroy(c->graph);
+  if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
+  for (void* p : c->allocs) cudaFree(p);
+  delete c;
+  return S2R_OK;
+}
+
+int32_t s2r_set_logit_bias(s2r_ctx* c, const float* bias) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  CK(cudaSetDevice(c->device));
+  CK(cudaDeviceSynchronize());
+  if (bias) {
+    CK(cudaMemcpy(c->bias, bias, (size_t)c->V * sizeof(float), cudaMemcpyDefault));
+  } else {
+    CK(cudaMemset(c->bias, 0, (size_t)c->V * sizeof(float)));
+  }
+  if (c->has_bias != (bias != nullptr)) c->graph_dirty = true;
+  c->has_bias = bias != nullptr;
+  return S2R_OK;
+}
+
+int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memory_dtype, int32_t memory_frames,
+                      int32_t frames, const int64_t* prefix, int32_t n_prefix, double stop_seconds, int64_t target,
+                      void* stream) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  if (slot < 0 || slot >= c->B) return fail(S2R_EINVAL, "slot %d out of range [0, %d)", slot, c->B);
+  if (!memory || (memory_dtype != S2R_F32 && memory_dtype != S2R_BF16)) return fail(S2R_EINVAL, "bad memory argument");
+  if (frames < 1 || frames > memory_frames || frames > c->F)
+    return fail(S2R_EINVAL, "frames %d must be in [1, min(memory_frames %d, engine frames %d)]", frames, memory_frames, c->F);
+  if (!prefix || n_prefix < 1) return fail(S2R_EINVAL, "empty prefix");
+  if (n_prefix > c->T - 1)
+    return fail(S2R_EINVAL, "prefix of %d tokens does not fit the context of %d", n_prefix, c->T);
+  int out_index = -1;
+  for (int i = 0; i < n_prefix; ++i) {
+    if (prefix[i] < 0 || prefix[i] >= c->V) return fail(S2R_EINVAL, "prefix token %lld outside the vocabulary", (long long)prefix[i]);
+    if (out_index < 0 && prefix[i] == 3) out_index = i;
+  }
+  if (out_index < 0) return fail(S2R_EINVAL, "prefix has no <out> token (3)");
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int D = c->D;
+
+  // grammar state after the prefix (grammar.py:182-197)
+  HostGrammarState gs;
+  for (int i = out_index + 1; i < n_prefix; ++i) {
+    if (c->gr.kind == S2R_GRAMMAR_TABLE)
+      gs.g = (c->gr.multiplier * gs.g + prefix[i]) % c->gr.states;
+    else
+      replay_class(c, gs, prefix[i]);
+  }
+  // pages for positions 0 .. n-1
+  release_pages(c, slot);
+  std::fill(c->h_page_table.begin() + (size_t)slot * c->pps, c->h_page_table.begin() + (size_t)(slot + 1) * c->pps, 0);
+  bool changed = false;
+  TRY(grow_pages(c, slot, n_prefix - 1, &changed));
+  TRY(upload_page_row(c, slot, s));
+
+  SlotState& st = c->st;
+  TRY(put<int32_t>(st.frames, slot, frames, s));
+  TRY(put<double>(st.stop, slot, stop_seconds, s));
+  TRY(put<int64_t>(st.target, slot, target, s));
+  TRY(put<int64_t>(st.g, slot, gs.g, s));
+  TRY(put<int64_t>(st.count, slot, 0, s));
+  TRY(put<uint8_t>(st.in_shift, slot, gs.in_shift, s));
+  TRY(put<int64_t>(st.shift_run, slot, gs.shift_run, s));
+  TRY(put<int64_t>(st.payload, slot, gs.payload, s));
+  TRY(put<int64_t>(st.last_field, slot, gs.last_field, s));
+  TRY(put<int64_t>(st.incomplete, slot, gs.incomplete, s));
+  TRY(put<int64_t>(st.ended, slot, gs.ended, s));
+  TRY(put<uint8_t>(st.finished, slot, gs.finished, s));
+  TRY(put<int64_t>(st.token, slot, prefix[n_prefix - 1], s));
+  TRY(put<int64_t>(st.position, slot, (int64_t)n_prefix - 1, s));
+  CK(cudaMemcpyAsync(st.out + (size_t)slot * c->T, prefix, n_prefix * sizeof(int64_t), cudaMemcpyDefault, s));
+
+  // cross K/V of the window (decoder.py:98-116), written straight into the slot
+  const size_t elem = memory_dtype == S2R_F32 ? 4 : 2;
+  CK(cudaMemcpyAsync(c->mem_stage, memory, (size_t)frames * D * elem, cudaMemcpyDefault, s));
+  for (int l = 0; l < c->L; ++l) {
+    ProjArgs a = proj_base(c);
+    a.M = frames;
+    a.K = D;
+    a.N = 2 * D;
+    a.xin = c->mem_stage;
+    a.ldx = D;
+    a.W = c->layers[l].wckv;
+    a.bias = c->layers[l].bckv;
+    a.k_dst = c->layers[l].ck;
+    a.v_dst = c->layers[l].cv;
+    a.cross_slot = slot;
+    TRY(launch_proj(c, a, memory_dtype == S2R_F32 ? IN_F32 : IN_BF16, EPI_CROSSKV, s));
+  }
+  // prefix prefill: K/V of prefix[0 .. n-2] at positions 0 .. n-2 (engine.py:199-205)
+  std::vector<int32_t> toks(kPrefillRows);
+  for (int p0 = 0; p0 < n_prefix - 1; p0 += kPrefillRows) {
+    const int rows = std::min(kPrefillRows, n_prefix - 1 - p0);
+    for (int i = 0; i < rows; ++i) toks[i] = (int32_t)prefix[p0 + i];
+    CK(cudaMemcpyAsync(c->prefill_tokens, toks.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    RowMap rm{1, slot, p0, c->prefill_tokens};
+    for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
+  }
+  CK(cudaGetLastError());
+  c->loaded[slot] = 1;
+  c->bound[slot] = n_prefix - 1;
+  return S2R_OK;
+}
+
+int32_t s2r_step(s2r_ctx* c, int32_t n_steps, void* stream) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  if (n_steps <= 0) return S2R_OK;
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int slot = 0; slot < c->B; ++slot) {
+    if (!c->loaded[slot]) continue;
+    c->bound[slot] = std::min(c->bound[slot] + n_steps, c->T - 1);
+    bool changed = false;
+    TRY(grow_pages(c, slot, c->bound[slot], &changed));
+    if (changed) TRY(upload_page_row(c, slot, s));
+  }
+  if (c->use_graph) {
+    TRY(ensure_graph(c));
+    for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(c->graph, s));
+  } else {
+    for (int i = 0; i < n_steps; ++i) TRY(enqueue_step(c, s, nullptr, nullptr, nullptr));
+  }
+  CK(cudaGetLastError());
+  return S2R_OK;
+}
+
+int32_t s2r_step_debug(s2r_ctx* c, const int64_t* forced, float* logits, int64_t* greedy, void* stream) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (forced) {
+    for (int i = 0; i < c->B; ++i)
+      if (forced[i] >= c->V) return fail(S2R_EINVAL, "forced token %lld outside the vocabulary", (long long)forced[i]);
+    CK(cudaMemcpyAsync(c->dbg_forced, forced, c->B * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+  }
+  for (int slot = 0; slot < c->B; ++slot) {
+    if (!c->loaded[slot]) continue;
+    c->bound[slot] = std::min(c->bound[slot] + 1, c->T - 1);
+    bool changed = false;
+    TRY(grow_pages(c, slot, c->bound[slot], &changed));
+    if (changed) TRY(upload_page_row(c, slot, s));
+  }
+  TRY(enqueue_step(c, s, forced ? c->dbg_forced : nullptr, logits ? c->dbg_logits : nullptr,
+                   greedy ? c->dbg_greedy : nullptr));
+  if (logits)
+    CK(cudaMemcpyAsync(logits, c->dbg_logits, (size_t)c->B * c->V * sizeof(float), cudaMemcpyDeviceToHost, s));
+  if (greedy) CK(cudaMemcpyAsync(greedy, c->dbg_greedy, c->B * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  return check_device_error(c, s);
+}
+
+int32_t s2r_poll_finished(s2r_ctx* c, uint8_t* finished, void* stream) {
+  if (!c || !finished) return fail(S2R_EINVAL, "NULL argument");
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaMemcpyAsync(finished, c->st.finished, c->B, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  return check_device_error(c, s);
+}
+
+int32_t s2r_take(s2r_ctx* c, int32_t slot, int64_t* tokens, int32_t capacity, int32_t* length, int32_t* ended,
+                 void* stream) {
+  if (!c || !length || !ended) return fail(S2R_EINVAL, "NULL argument");
+  if (slot < 0 || slot >= c->B) return fail(S2R_EINVAL, "slot %d out of range [0, %d)", slot, c->B);
+  if (!c->loaded[slot]) return fail(S2R_ESTATE, "slot %d is not loaded", slot);
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int64_t pos = 0, end = 0;
+  CK(cudaMemcpyAsync(&pos, c->st.position + slot, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(&end, c->st.ended + slot, 8, cudaMemcpyDeviceToHost, s));
+  TRY(check_device_error(c, s));
+  const int n = (int)pos + 1;
+  std::vector<int64_t> buf(n);
+  CK(cudaMemcpyAsync(buf.data(), c->st.out + (size_t)slot * c->T, n * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (buf.back() != 2) buf.push_back(2);  // always ends in <eos> (engine.py:259-260)
+  *length = (int32_t)buf.size();
+  if (!tokens || capacity < (int32_t)buf.size()) return fail(S2R_EINVAL, "capacity %d < %zu tokens", capacity, buf.size());
+  std::memcpy(tokens, buf.data(), buf.size() * sizeof(int64_t));
+  *ended = (int32_t)end;
+  c->loaded[slot] = 0;
+  release_pages(c, slot);
+  return S2R_OK;
+}
+
+int32_t s2r_get_buffer(s2r_ctx* c, const char* name, void** ptr, int64_t* numel, int32_t* dtype) {
+  if (!c || !name || !ptr || !numel || !dtype) return fail(S2R_EINVAL, "NULL argument");
+  const SlotState& st = c->st;
+  const int64_t B = c->B;
+  struct Entry {
+    const char* name;
+    void* p;
+    int64_t n;
+    int32_t t;
+  } table[] = {
+      {"token", st.token, B, 2},          {"position", st.position, B, 2},   {"finished", st.finished, B, 3},
+      {"ended", st.ended, B, 2},          {"in_shift", st.in_shift, B, 3},   {"shift_run", st.shift_run, B, 2},
+      {"payload", st.payload, B, 2},      {"last_field", st.last_field, B, 2}, {"incomplete", st.incomplete, B, 2},
+      {"g", st.g, B, 2},                  {"count", st.count, B, 2},         {"target", st.target, B, 2},
+      {"stop", st.stop, B, 4},            {"out", st.out, B * c->T, 2},      {"frames", st.frames, B, 5},
+  };
+  for (const Entry& e : table)
+    if (std::strcmp(e.name, name) == 0) {
+      *ptr = e.p;
+      *numel = e.n;
+      *dtype = e.t;
+      return S2R_OK;
+    }
+  return fail(S2R_EINVAL, "no buffer named '%s'", name);
+}
+
+int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches, void* stream) {
+  if (!c || !ms || !bytes || !launches) return fail(S2R_EINVAL, "NULL argument");
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // algorithmic bytes need the live lengths: read positions, frames and flags
+  std::vector<int64_t> pos(c->B);
+  std::vector<int32_t> frames(c->B);
+  std::vector<uint8_t> fin(c->B);
+  CK(cudaMemcpyAsync(pos.data(), c->st.position, c->B * 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(frames.data(), c->st.frames, c->B * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(fin.data(), c->st.finished, c->B, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  const double D = c->D, FFN = c->FFN, V = c->V, M = c->B, H = c->H;
+  double self_kv = 0, cross_kv = 0;
+  int active = 0;
+  for (int b = 0; b < c->B; ++b)
+    if (!fin[b]) {
+      ++active;
+      self_kv += (double)(pos[b] + 1) * H * kHeadDim * 2 * 2;
+      cross_kv += (double)frames[b] * H * kHeadDim * 2 * 2;
+    }
+  const double per[K_CLASSES] = {
+      3 * D * D * 2 + 3 * D * 2 + M * D * 8 + M * 3 * D * 2,  // qkv: W, b, r in, x out, q/k/v out
+      self_kv + active * D * 4,                               // self attention: K, V, q in, out
+      D * D * 2 + D * 2 + M * D * (2 + 4 + 4),                // self out-proj: W, b, a in, x in, r out
+      D * D * 2 + D * 2 + M * D * (4 + 4 + 2),                // cross q
+      cross_kv + active * D * 4,                              // cross attention
+      D * D * 2 + D * 2 + M * D * (2 + 4 + 4),                // cross out-proj
+      FFN * D * 2 + FFN * 2 + M * D * 8 + M * FFN * 2,        // fc1
+      D * FFN * 2 + D * 2 + M * FFN * 2 + M * D * 8,          // fc2
+      V * D * 2 + M * D * 4 + V,                              // logits: E, r in, grammar column
+  };
+  for (int b = 0; b < c->B; ++b) {
+    if (!c->loaded[b]) continue;
+    c->bound[b] = std::min(c->bound[b] + 1, c->T - 1);
+    bool changed = false;
+    TRY(grow_pages(c, b, c->bound[b], &changed));
+    if (changed) TRY(upload_page_row(c, b, s));
+  }
+  // The step is captured into a graph with an event node after every kernel
+  // (no programmatic overlap, so each interval holds one kernel and no host
+  // launch time) and replayed once.
+  std::vector<std::pair<int, cudaEvent_t>> ev;
+  cudaEvent_t start;
+  CK(cudaEventCreate(&start));
+  const bool pdl = c->pdl;
+  c->pdl = false;
+  c->prof = &ev;
+  if (!c->use_graph) {  // plain launches: the events also hold the host's launch time
+    CK(cudaEventRecord(start, s));
+    int rc0 = enqueue_step(c, s, nullptr, nullptr, nullptr);
+    c->prof = nullptr;
+    c->pdl = pdl;
+    if (rc0 != S2R_OK) return rc0;
+    CK(cudaStreamSynchronize(s));
+  } else {
+  CK(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e0 = cudaEventRecordWithFlags(start, c->cap_stream, cudaEventRecordExternal);
+  int rc = e0 == cudaSuccess ? enqueue_step(c, c->cap_stream, nullptr, nullptr, nullptr) : S2R_ECUDA;
+  cudaGraph_t graph = nullptr;
+  cudaError_t e1 = cudaStreamEndCapture(c->cap_stream, &graph);
+  c->prof = nullptr;
+  c->pdl = pdl;
+  if (rc != S2R_OK || e0 != cudaSuccess || e1 != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc != S2R_OK ? rc : fail(S2R_ECUDA, "profile capture failed");
+  }
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e2 = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e2 != cudaSuccess) return fail(S2R_ECUDA, "profile graph: %s", cudaGetErrorString(e2));
+  CK(cudaGraphLaunch(exec, s));
+  CK(cudaStreamSynchronize(s));
+  cudaGraphExecDestroy(exec);
+  }
+  for (int k = 0; k < K_CLASSES; ++k) {
+    ms[k] = 0.f;
+    bytes[k] = per[k];
+    launches[k] = 0;
+  }
+  cudaEvent_t prev = start;
+  for (auto& [cls, e] : ev) {
+    float t = 0.f;
+    CK(cudaEventElapsedTime(&t, prev, e));
+    ms[cls] += t;
+    launches[cls] += 1;
+    prev = e;
+  }
+  cudaEventDestroy(start);
+  for (auto& pe : ev) cudaEventDestroy(pe.second);
+  return S2R_OK;
+}
+
+int32_t s2r_step_launches(s2r_ctx* c) { return c ? 8 * c->L + 1 : 0; }
+
+int32_t s2r_free_pages(s2r_ctx* c) { return c ? (int32_t)c->free_pages.size() : 0; }
+
+}  // extern "C"

@@ -1,0 +1,246 @@
+// Fused tied-logits projection, grammar mask, greedy argmax and slot commit.
+//
+// Replaces engine.py:315-357 (+ grammar.py:114-180): the final LayerNorm of
+// the last layer, logits = bf16(x . E_v) widened to float32, plus an optional
+// additive bias (mode_bias, engine.py:316-317), masked by the grammar, argmax
+// with the lowest index winning ties (torch.argmax), then for every live slot:
+// write the token to out[slot, position+1], advance the grammar, stop on
+// EOS / stop time / context limit.
+//
+// Every CTA scores an interleaved subset of the vocabulary for all rows and
+// publishes its best (value, index) per row with one 64-bit atomicMax on a key
+// whose high word orders the float value and whose low word is ~index, so the
+// maximum is the largest logit and, among equal logits, the lowest index.  The
+// last CTA to finish (a ticket counter) commits the step and resets the keys
+// and the counter for the next step.  The grammar mask is never materialised:
+// the class grammar evaluates its 13 class predicates once per row and reads
+// bit token_class[v]; the table grammar reads table[state, v].
+#pragma once
+
+#include "common.cuh"
+#include "proj.cuh"
+
+namespace s2r {
+
+struct Grammar {
+  int kind;  // 0 class, 1 table
+  const int8_t* token_class;
+  const int32_t* field_of_class;
+  const double* time_seconds;
+  int states;
+  int multiplier;
+  const uint8_t* table;
+};
+
+struct LogitsArgs {
+  int M, V, D, max_tokens;
+  SlotState st;
+  Grammar gr;
+  const float* r;  // [M, D] residual sums before the last final_norm
+  const float* gamma;
+  const float* beta;
+  const bf16* emb;    // tied output embedding [V, D], bfloat16
+  const float* bias;  // [V] or null
+  unsigned long long* keys;  // [M], zero between steps
+  unsigned int* counter;     // zero between steps
+  const int64_t* forced;     // [M] or null: commit forced[m] >= 0 instead of the greedy token
+  float* logits_out;         // [M, V] or null: raw logits
+  int64_t* greedy_out;       // [M] or null
+};
+
+// Class grammar constants (grammar.py:19-55).
+constexpr int kEosT = 0, kShiftT = 1, kTimeT = 2, kMeterT = 3, kPitchT = 8, kBassT = 10;
+constexpr int kNone = 0, kAfterMeter = 1, kAfterPitch = 2, kAfterBass = 3, kMaxShiftRun = 4;
+
+// The 13 class predicates of grammar.py:117-137 as a bit mask.
+__device__ __forceinline__ uint32_t class_mask(const SlotState& st, int s) {
+  const int64_t last = st.last_field[s], inc = st.incomplete[s], payload = st.payload[s], run = st.shift_run[s];
+  const bool in_shift = st.in_shift[s] != 0;
+  const bool free_ = inc == kNone, open_chord = inc == kAfterBass;
+  uint32_t m = 0;
+  m |= (uint32_t)((payload > 0) && !open_chord) << 0;
+  m |= (uint32_t)(((payload > 0) || in_shift) && (run < kMaxShiftRun) && !open_chord) << 1;
+  m |= (uint32_t)(free_ && last < 0) << 2;
+  m |= (uint32_t)(free_ && last < 1) << 3;
+  m |= (uint32_t)((inc == kAfterMeter) || (free_ && last < 1)) << 4;
+  m |= (uint32_t)(free_ && last < 2) << 5;
+  m |= (uint32_t)(free_ && last < 3) << 6;
+  m |= (uint32_t)(free_ && last < 4) << 7;
+  m |= (uint32_t)((inc == kAfterPitch) || (free_ && last <= 5)) << 8;
+  m |= (uint32_t)(inc == kAfterPitch) << 9;
+  m |= (uint32_t)(free_ && last < 4) << 10;
+  m |= (uint32_t)open_chord << 11;
+  return m;  // bit 12 (other) is never set
+}
+
+// grammar.py:140-180 for one slot (class grammar) or the table rule.
+__device__ __forceinline__ void grammar_update(const Grammar& gr, const SlotState& st, int s, int64_t tok, bool active,
+                                               bool at_limit) {
+  if (gr.kind == 1) {
+    const int64_t g = (gr.multiplier * st.g[s] + tok) % gr.states;
+    const int64_t count = st.count[s] + 1;
+    const bool done = count >= st.target[s];
+    const bool fin = done || at_limit;
+    if (active) {
+      st.g[s] = g;
+      st.count[s] = count;
+      if (fin) {
+        st.ended[s] = done ? 1 : 3;
+        st.finished[s] = 1;
+      }
+    }
+    return;
+  }
+  const int kind = gr.token_class[tok];
+  const bool is_shift = kind == kShiftT;
+  const bool is_field = kind != kShiftT && kind != kEosT;
+  const bool in_shift = st.in_shift[s] != 0;
+  const bool new_event = is_shift && !in_shift && st.payload[s] > 0;
+  int64_t payload = new_event ? 0 : st.payload[s];
+  if (is_field) payload += 1;
+  int64_t last = new_event ? -1 : st.last_field[s];
+  if (is_field) last = gr.field_of_class[kind];
+  int64_t inc = new_event ? kNone : st.incomplete[s];
+  if (is_field) inc = kind == kMeterT ? kAfterMeter : kind == kPitchT ? kAfterPitch : kind == kBassT ? kAfterBass : kNone;
+  const bool new_in_shift = is_shift ? true : (is_field ? false : in_shift);
+  const int64_t run = is_shift ? st.shift_run[s] + 1 : (is_field ? 0 : st.shift_run[s]);
+  const bool eos = kind == kEosT;
+  const bool stopped = kind == kTimeT && gr.time_seconds[tok] >= st.stop[s];
+  const bool fin = eos || stopped || at_limit;
+  if (active) {
+    st.payload[s] = payload;
+    st.last_field[s] = last;
+    st.incomplete[s] = inc;
+    st.in_shift[s] = new_in_shift;
+    st.shift_run[s] = run;
+    if (fin) {
+      st.ended[s] = eos ? 1 : stopped ? 2 : 3;
+      st.finished[s] = 1;
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+
+constexpr int kLogitsThreads = 256;
+
+template <int KCH, int MC>
+__global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int KP = KCH * 256;
+  constexpr int NW = kLogitsThreads / 32;
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MC][KP]
+  __shared__ uint32_t rule[MC];                   // class mask or table state per row
+  __shared__ unsigned long long wbest[NW][MC];
+  __shared__ int is_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int D = a.D;
+  const int stride = gridDim.x * NW;
+  const int first = blockIdx.x * NW + warp;
+
+  uint4 w[KCH];
+#pragma unroll
+  for (int c = 0; c < KCH; ++c) {
+    const int col = c * 256 + lane * 8;
+    w[c] = (first < a.V && col < D) ? ld_stream(a.emb + (size_t)first * D + col) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // LayerNorm staging shares the projection kernel's code path.
+  ProjArgs pa{};
+  pa.M = a.M;
+  pa.K = D;
+  pa.r = a.r;
+  pa.gamma = a.gamma;
+  pa.beta = a.beta;
+  pa.x_out = nullptr;
+
+  for (int m0 = 0; m0 < a.M; m0 += MC) {
+    const int mc = min(MC, a.M - m0);
+    if (m0 > 0) __syncthreads();
+    stage_ln_rows<KCH, IN_LN>(pa, xs, m0, mc, warp, lane, NW);
+    for (int idx = threadIdx.x; idx < (MC - mc) * (KP / 8); idx += blockDim.x) {
+      const int i = mc + idx / (KP / 8), col = (idx % (KP / 8)) * 8;
+      *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = make_uint4(0, 0, 0, 0);
+    }
+    if (threadIdx.x < MC) {
+      const int s = m0 + threadIdx.x;
+      rule[threadIdx.x] = threadIdx.x < mc ? (a.gr.kind == 1 ? (uint32_t)a.st.g[s] : class_mask(a.st, s)) : 0u;
+    }
+    __syncthreads();
+
+    unsigned long long best[MC];
+#pragma unroll
+    for (int i = 0; i < MC; ++i) best[i] = 0ull;
+    for (int v = first; v < a.V; v += stride) {
+      if (v != first || m0 > 0) {
+#pragma unroll
+        for (int c = 0; c < KCH; ++c) {
+          const int col = c * 256 + lane * 8;
+          w[c] = col < D ? ld_stream(a.emb + (size_t)v * D + col) : make_uint4(0, 0, 0, 0);
+        }
+      }
+      const float bias = a.bias ? a.bias[v] : 0.f;
+      const int cls = a.gr.kind == 1 ? 0 : a.gr.token_class[v];
+#pragma unroll
+      for (int i = 0; i < MC; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < KCH; ++c)
+          acc += dot8(w[c], *reinterpret_cast<const uint4*>(xs + (size_t)i * KP + c * 256 + lane * 8));
+        acc = warp_sum(acc);
+        if (i < mc) {
+          const float logit = round_bf16(acc);
+          if (a.logits_out && lane == 0) a.logits_out[(size_t)(m0 + i) * a.V + v] = logit;
+          const bool ok = a.gr.kind == 1 ? a.gr.table[(size_t)rule[i] * a.V + v] != 0 : ((rule[i] >> cls) & 1u) != 0;
+          if (ok) {
+            const unsigned long long k = argmax_key(logit + bias, v);
+            best[i] = k > best[i] ? k : best[i];
+          }
+        }
+      }
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < MC; ++i) wbest[warp][i] = best[i];
+    }
+    __syncthreads();
+    if (threadIdx.x < mc) {
+      unsigned long long k = 0ull;
+      for (int ww = 0; ww < NW; ++ww) k = wbest[ww][threadIdx.x] > k ? wbest[ww][threadIdx.x] : k;
+      if (k) atomicMax(a.keys + m0 + threadIdx.x, k);
+    }
+  }
+
+  // ---- the last CTA commits the step
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int s = threadIdx.x; s < a.M; s += blockDim.x) {
+    const unsigned long long k = atomicExch(a.keys + s, 0ull);
+    // all tokens masked: torch.argmax over a row of -inf returns index 0
+    const int64_t greedy = k ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
+    if (a.greedy_out) a.greedy_out[s] = greedy;
+    const bool active = a.st.finished[s] == 0;
+    const int64_t tok = a.st.token[s], pos = a.st.position[s];
+    int64_t choice = greedy;
+    if (a.forced && a.forced[s] >= 0) choice = a.forced[s];
+    if (!active) choice = tok;
+    const int64_t new_pos = active ? pos + 1 : pos;
+    if (active && new_pos < a.max_tokens) a.st.out[(size_t)s * a.max_tokens + new_pos] = choice;
+    grammar_update(a.gr, a.st, s, choice, active, new_pos >= a.max_tokens - 1);
+    a.st.token[s] = choice;
+    a.st.position[s] = new_pos;
+  }
+  if (threadIdx.x == 0) *a.counter = 0u;
+}
+
+}  // namespace s2r

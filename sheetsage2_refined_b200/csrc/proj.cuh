@@ -1,0 +1,266 @@
+// Streaming projection kernel: y = x W^T + b for a handful of rows, weights
+// read once from HBM at full width.
+//
+// One warp owns one output feature at a time and reads that feature's weight
+// row with 16-byte loads (lane l holds columns c*256 + 8l .. 8l+7 of every
+// 256-column chunk c), multiplies it against up to MC input rows staged in
+// shared memory as bfloat16, and reduces across the warp.  The input rows are
+// produced in the prologue, fused with what precedes the projection in the
+// reference step (engine.py:298-314):
+//   IN_EMBED  token + position embedding, then LayerNorm   (engine.py:298-302)
+//   IN_LN     LayerNorm of the residual sum r              (decoder.py:78,81,84)
+//   IN_BF16   bfloat16 rows (attention output, GELU hidden, encoder memory)
+//   IN_F32    float32 rows rounded to bfloat16 (float32 encoder memory)
+// and the epilogue applies what follows it:
+//   EPI_QKV     q to a buffer, k/v appended to the paged self K/V cache (engine.py:310-311)
+//   EPI_RESID   r = x + bf16(acc + b): the residual sum before the next LayerNorm
+//   EPI_BF16    bf16(acc + b)
+//   EPI_GELU    bf16(gelu(bf16(acc + b)))  (exact erf GELU on the bfloat16 value, decoder.py:83)
+//   EPI_CROSSKV cross K/V of one slot's encoder frames (decoder.py:108-113)
+// Rounding follows the reference's CUDA autocast: the Linear input is the
+// bfloat16 rounding of the float32 activation, accumulation is float32 and the
+// output is rounded once after the bias is added.
+#pragma once
+
+#include "common.cuh"
+
+namespace s2r {
+
+enum InMode { IN_LN = 0, IN_EMBED = 1, IN_BF16 = 2, IN_F32 = 3 };
+enum EpiMode { EPI_QKV = 0, EPI_RESID = 1, EPI_BF16 = 2, EPI_GELU = 3, EPI_CROSSKV = 4 };
+
+struct ProjArgs {
+  int M, K, N;
+  RowMap rm;
+  SlotState st;
+  // input
+  const float* r;      // IN_LN: [M, K] residual sums
+  const float* gamma;  // IN_LN / IN_EMBED: LayerNorm weight [K]
+  const float* beta;   //                   LayerNorm bias [K]
+  const float* tok_emb;
+  const float* pos_emb;
+  const void* xin;  // IN_BF16 / IN_F32: [M, ldx]
+  int ldx;
+  float* x_out;  // IN_LN / IN_EMBED: the normalised float32 rows [M, K] (null: not kept)
+  // weights [N, K] row-major and bias [N]
+  const bf16* W;
+  const bf16* bias;
+  // epilogue
+  bf16* out;
+  int ldo;
+  float* r_out;        // EPI_RESID [M, N]
+  const float* x_res;  // EPI_RESID [M, N]
+  bf16* k_dst;         // EPI_QKV: paged K pool; EPI_CROSSKV: cross K [batch, heads, frames_cap, 64]
+  bf16* v_dst;
+  int heads;
+  int pages_per_slot;
+  int frames_cap;
+  int cross_slot;
+};
+
+__device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
+  float s = bf_lo(w.x) * bf_lo(x.x);
+  s = fmaf(bf_hi(w.x), bf_hi(x.x), s);
+  s = fmaf(bf_lo(w.y), bf_lo(x.y), s);
+  s = fmaf(bf_hi(w.y), bf_hi(x.y), s);
+  s = fmaf(bf_lo(w.z), bf_lo(x.z), s);
+  s = fmaf(bf_hi(w.z), bf_hi(x.z), s);
+  s = fmaf(bf_lo(w.w), bf_lo(x.w), s);
+  s = fmaf(bf_hi(w.w), bf_hi(x.w), s);
+  return s;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f)); }
+
+template <int EPI>
+__device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, float acc) {
+  const float v = acc + __bfloat162float(a.bias[n]);
+  if constexpr (EPI == EPI_RESID) {
+    a.r_out[(size_t)m * a.N + n] = a.x_res[(size_t)m * a.N + n] + round_bf16(v);
+  } else if constexpr (EPI == EPI_BF16) {
+    a.out[(size_t)m * a.ldo + n] = __float2bfloat16_rn(v);
+  } else if constexpr (EPI == EPI_GELU) {
+    a.out[(size_t)m * a.ldo + n] = __float2bfloat16_rn(gelu_erf(round_bf16(v)));
+  } else if constexpr (EPI == EPI_QKV) {
+    const int D = a.heads * kHeadDim;
+    if (n < D) {
+      a.out[(size_t)m * a.ldo + n] = __float2bfloat16_rn(v);
+    } else if (row_active(a.rm, a.st, m)) {
+      const int c = n - D;
+      const int which = c >= D;
+      const int cc = which ? c - D : c;
+      const int slot = row_slot(a.rm, m), pos = row_pos(a.rm, a.st, m);
+      bf16* dst = which ? a.v_dst : a.k_dst;
+      dst[paged_offset(a.st.page_table, a.pages_per_slot, a.heads, slot, cc / kHeadDim, pos) + (cc % kHeadDim)] =
+          __float2bfloat16_rn(v);
+    }
+  } else {  // EPI_CROSSKV: row m is encoder frame m of slot cross_slot
+    const int D = a.heads * kHeadDim;
+    const int which = n >= D;
+    const int c = which ? n - D : n;
+    bf16* dst = which ? a.v_dst : a.k_dst;
+    dst[(((size_t)a.cross_slot * a.heads + c / kHeadDim) * a.frames_cap + m) * kHeadDim + (c % kHeadDim)] =
+        __float2bfloat16_rn(v);
+  }
+}
+
+// Normalise rows [m0, m0+mc) into xs (bfloat16, KP columns per row, zero
+// padded) and keep the float32 result in x_out.  One warp per row; each lane
+// holds its 8*KCH columns in registers (two-pass mean / variance).
+template <int KCH, int IN>
+__device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m0, int mc, int warp, int lane,
+                                              int nwarps) {
+  constexpr int KP = KCH * 256;
+  const int K = a.K;
+  for (int i = warp; i < mc; i += nwarps) {
+    const int m = m0 + i;
+    float v[KCH * 8];
+    const float* src0 = nullptr;
+    const float* src1 = nullptr;
+    if constexpr (IN == IN_EMBED) {
+      src0 = a.tok_emb + (size_t)row_token(a.rm, a.st, m) * K;
+      src1 = a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * K;  // POSITION_OFFSET, decoder.py:24-25
+    } else {
+      src0 = a.r + (size_t)m * K;
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < KCH; ++c) {
+      const int col = c * 256 + lane * 8;
+      if (col < K) {
+        float4 p0 = *reinterpret_cast<const float4*>(src0 + col);
+        float4 p1 = *reinterpret_cast<const float4*>(src0 + col + 4);
+        if constexpr (IN == IN_EMBED) {
+          float4 q0 = *reinterpret_cast<const float4*>(src1 + col);
+          float4 q1 = *reinterpret_cast<const float4*>(src1 + col + 4);
+          p0.x += q0.x; p0.y += q0.y; p0.z += q0.z; p0.w += q0.w;
+          p1.x += q1.x; p1.y += q1.y; p1.z += q1.z; p1.w += q1.w;
+        }
+        v[c * 8 + 0] = p0.x; v[c * 8 + 1] = p0.y; v[c * 8 + 2] = p0.z; v[c * 8 + 3] = p0.w;
+        v[c * 8 + 4] = p1.x; v[c * 8 + 5] = p1.y; v[c * 8 + 6] = p1.z; v[c * 8 + 7] = p1.w;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum += v[c * 8 + j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[c * 8 + j] = 0.f;
+      }
+    }
+    const float mean = warp_sum(sum) / (float)K;
+    float sq = 0.f;
+#pragma unroll
+    for (int c = 0; c < KCH; ++c) {
+      if (c * 256 + lane * 8 < K) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = v[c * 8 + j] - mean;
+          sq = fmaf(d, d, sq);
+        }
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(sq) / (float)K + kLnEps);
+    const bool keep = a.x_out != nullptr && (m % gridDim.x) == blockIdx.x;
+#pragma unroll
+    for (int c = 0; c < KCH; ++c) {
+      const int col = c * 256 + lane * 8;
+      uint4 packed = make_uint4(0, 0, 0, 0);
+      if (col < K) {
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = (v[c * 8 + j] - mean) * rstd * a.gamma[col + j] + a.beta[col + j];
+        packed = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+        if (keep) {
+          float* dst = a.x_out + (size_t)m * K + col;
+          *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+        }
+      }
+      *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = packed;
+    }
+  }
+}
+
+template <int KCH, int MC, int IN, int EPI>
+__global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MC][KP]
+  constexpr int KP = KCH * 256;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int K = a.K;
+  const int stride = gridDim.x * 4;
+  const int first = blockIdx.x * 4 + warp;
+
+  // The weights do not depend on earlier kernels: start streaming this warp's
+  // first row before waiting for them.
+  uint4 w[KCH];
+#pragma unroll
+  for (int c = 0; c < KCH; ++c) {
+    const int col = c * 256 + lane * 8;
+    w[c] = (first < a.N && col < K) ? ld_stream(a.W + (size_t)first * K + col) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
+  for (int m0 = 0; m0 < a.M; m0 += MC) {
+    const int mc = min(MC, a.M - m0);
+    if (m0 > 0) __syncthreads();
+    if constexpr (IN == IN_LN || IN == IN_EMBED) {
+      stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4);
+    } else {
+      for (int idx = threadIdx.x; idx < MC * (KP / 8); idx += blockDim.x) {
+        const int i = idx / (KP / 8), col = (idx % (KP / 8)) * 8;
+        uint4 packed = make_uint4(0, 0, 0, 0);
+        if (i < mc && col < K) {
+          if constexpr (IN == IN_BF16) {
+            packed = *reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.xin) + (size_t)(m0 + i) * a.ldx + col);
+          } else {
+            const float* s = static_cast<const float*>(a.xin) + (size_t)(m0 + i) * a.ldx + col;
+            float4 p0 = *reinterpret_cast<const float4*>(s), p1 = *reinterpret_cast<const float4*>(s + 4);
+            packed = make_uint4(pack_bf16(p0.x, p0.y), pack_bf16(p0.z, p0.w), pack_bf16(p1.x, p1.y), pack_bf16(p1.z, p1.w));
+          }
+        }
+        *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = packed;
+      }
+    }
+    if constexpr (IN == IN_LN || IN == IN_EMBED) {
+      // rows mc..MC-1 of the last chunk are not staged: zero them
+      for (int idx = threadIdx.x; idx < (MC - mc) * (KP / 8); idx += blockDim.x) {
+        const int i = mc + idx / (KP / 8), col = (idx % (KP / 8)) * 8;
+        *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    __syncthreads();
+
+    for (int n = first; n < a.N; n += stride) {
+      if (n != first || m0 > 0) {
+#pragma unroll
+        for (int c = 0; c < KCH; ++c) {
+          const int col = c * 256 + lane * 8;
+          w[c] = col < K ? ld_stream(a.W + (size_t)n * K + col) : make_uint4(0, 0, 0, 0);
+        }
+      }
+      float acc[MC];
+#pragma unroll
+      for (int i = 0; i < MC; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int c = 0; c < KCH; ++c) {
+#pragma unroll
+        for (int i = 0; i < MC; ++i) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)i * KP + c * 256 + lane * 8);
+          acc[i] += dot8(w[c], xv);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < MC; ++i) {
+        acc[i] = warp_sum(acc[i]);
+        if (lane == i && i < mc) proj_epilogue<EPI>(a, m0 + i, n, acc[i]);
+      }
+    }
+  }
+}
+
+}  // namespace s2r
