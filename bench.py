@@ -141,39 +141,47 @@ def reduce_sum(value: float, world: int, device) -> float:
 
 
 # ---------------------------------------------------------------- CPU arm
-def cpu_decode_sample(seconds: float = 10.0, min_tokens: int = 8):
-    """The reference's CPU decode path (the oracle's float32 mode) on the single-song workload.
+def single_config(world: int) -> dict:
+    return {"workload": "single-song decode, 12L d1024 h16 ffn4096 V2048, bf16 memory [1,1500,1024], "
+                        "2048 greedy tokens per song, batch 1 per GPU",
+            "global_batch": world, "seq_len": SINGLE_TOKENS, "parallelism": f"song-sharded x{world}",
+            "l2": "inputs larger than L2 (352 MB of weights streamed per token)"}
 
-    Loads the window (cross K/V of 1500 frames), then decodes greedily until
-    ``seconds`` of decode time have passed.  Returns (tokens/s, tokens, cores).
-    """
 
-    from oracle.engine import OracleEngine
-    from sheetsage2_refined_b200.weights import memory_array
+class CpuDecoder:
+    """The reference's CPU decode path (the oracle's float32 mode) on the single-song workload."""
 
-    grammar = TableGrammar(CONFIG.vocab_size, states=8, density=0.25, seed=GRAMMAR_SEED)
-    eng = OracleEngine(CONFIG, synthetic_state_dict(CONFIG, WEIGHT_SEED), grammar, batch=1, frames=SINGLE_FRAMES,
-                       mode="fp32")
-    eng.load(0, memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED), [SOS, OUT], None, SINGLE_FRAMES,
-             target=SINGLE_TOKENS)
-    eng.step()  # warm-up
-    n, t0 = 0, time.perf_counter()
-    while n < min_tokens or time.perf_counter() - t0 < seconds:
-        eng.step()
-        n += 1
-    dt = time.perf_counter() - t0
-    return n / dt, n, os.cpu_count() or 1
+    def __init__(self):
+        from oracle.engine import OracleEngine
+        from sheetsage2_refined_b200.weights import memory_array
+
+        grammar = TableGrammar(CONFIG.vocab_size, states=8, density=0.25, seed=GRAMMAR_SEED)
+        self.eng = OracleEngine(CONFIG, synthetic_state_dict(CONFIG, WEIGHT_SEED), grammar, batch=1,
+                                frames=SINGLE_FRAMES, mode="fp32")
+        self.eng.load(0, memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED), [SOS, OUT], None, SINGLE_FRAMES,
+                      target=SINGLE_TOKENS)
+        self.eng.step()  # warm-up
+
+    def sample(self, seconds: float, min_tokens: int = 4):
+        """Greedy tokens for ``seconds`` of decode; returns (tokens/s, tokens, cores)."""
+
+        n, t0 = 0, time.perf_counter()
+        while n < min_tokens or time.perf_counter() - t0 < seconds:
+            self.eng.step()
+            n += 1
+        return n / (time.perf_counter() - t0), n, os.cpu_count() or 1
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
+    cpu = CpuDecoder()
     values = []
     tokens = 0
     for _ in range(args.warmup):
-        cpu_decode_sample(seconds=1.0, min_tokens=2)
+        cpu.sample(seconds=0.5, min_tokens=2)
     for _ in range(args.steps):
-        v, n, cores = cpu_decode_sample(seconds=args.cpu_seconds / max(args.steps, 1), min_tokens=4)
+        v, n, cores = cpu.sample(seconds=args.cpu_seconds / max(args.steps, 1), min_tokens=4)
         values.append(v)
         tokens += n
     value = statistics.mean(values)
@@ -183,8 +191,7 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "single-song decode, 12L d1024 h16 ffn4096 V2048, F=1500, batch 1",
-                   "global_batch": 1, "seq_len": SINGLE_TOKENS, "parallelism": "cpu"},
+        "config": single_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -231,8 +238,7 @@ def run_b200(args, world, rank, local):
 
         h2d = SINGLE_FRAMES * CONFIG.width * 2 + 2 * 8
         d2h = (SINGLE_TOKENS + 3) * 8 + 1
-        workload = "single-song decode, 12L d1024 h16 ffn4096 V2048, bf16 memory [1,1500,1024], 2048 tokens, batch 1"
-        global_batch, seq_len = 1, SINGLE_TOKENS
+        config = single_config(world)
     else:
         raise SystemExit("batched workload: not implemented yet")
 
@@ -289,7 +295,7 @@ def run_b200(args, world, rank, local):
 
     cpu = None
     if world == 1 and not args.no_cpu:
-        v, n, cores = cpu_decode_sample(seconds=args.cpu_seconds)
+        v, n, cores = CpuDecoder().sample(seconds=args.cpu_seconds)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} greedy tokens of the single-song workload from position 1 (load excluded), "
                          "float32 numpy restatement of the reference CPU path, all host cores"}
@@ -300,9 +306,7 @@ def run_b200(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": workload, "global_batch": global_batch * world, "seq_len": seq_len,
-                       "parallelism": f"song-sharded x{world}",
-                       "l2": "inputs larger than L2 (352 MB of weights streamed per token)"},
+            "config": config,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             # per step: cross K/V projection (one per layer), the 1-row prefill of the
             # prefix (8 per layer but only the K/V projection in the last), then the decode
@@ -357,7 +361,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--workload", default="single", choices=("single", "batched"))
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     world, rank, local = dist_env()
