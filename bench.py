@@ -46,7 +46,7 @@ CONFIG = DecoderConfig(vocab_size=2048, width=1024, layers=12, heads=16, ffn_wid
 WEIGHT_SEED, MEMORY_SEED, GRAMMAR_SEED = 1, 101, 8
 SINGLE_FRAMES, SINGLE_TOKENS = 1500, 2048
 BATCH, BATCH_FRAMES = 64, 3000
-CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits")
+CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits", "step")
 
 
 def peaks():
@@ -334,13 +334,15 @@ def profile(eng):
 
     from sheetsage2_refined_b200 import _lib
 
-    ms = (C.c_float * 9)()
-    by = (C.c_double * 9)()
-    n = (C.c_int32 * 9)()
+    k = len(CLASS_NAMES)
+    ms = (C.c_float * k)()
+    by = (C.c_double * k)()
+    n = (C.c_int32 * k)()
     _lib.check(eng._lib.s2r_profile_step(eng._ctx, ms, by, n, eng._stream()))
-    classes = {name: {"ms": ms[i], "launches": n[i], "bytes_per_launch": by[i]} for i, name in enumerate(CLASS_NAMES)}
-    total_ms = sum(ms[i] for i in range(9))
-    total_bytes = sum(by[i] * n[i] for i in range(9))
+    classes = {name: {"ms": ms[i], "launches": n[i], "bytes_per_launch": by[i]} for i, name in enumerate(CLASS_NAMES)
+               if n[i] > 0}
+    total_ms = sum(ms[i] for i in range(k))
+    total_bytes = sum(by[i] * n[i] for i in range(k))
     return {"classes": classes, "step": {"ms_kernels": total_ms, "bytes": total_bytes,
                                          "gbs": total_bytes / (total_ms * 1e-3) / 1e9}}
 

@@ -68,6 +68,9 @@ typedef struct s2r_config {
 
 #define S2R_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
 #define S2R_FLAG_NO_GRAPH 2u /* issue steps as plain launches, no CUDA graph */
+#define S2R_FLAG_ONE_KERNEL_STEP 4u /* batch <= 8: run a step as one persistent kernel */
+#define S2R_FLAG_TRACE 8u          /* one-kernel step records clock64 marks per phase ("trace" buffer) */
+#define S2R_FLAG_NO_PREFETCH 16u   /* one-kernel step without next-phase L2 prefetches */
 
 /* One decoder layer's float32 parameters, named as in
  * TokenDecoder.state_dict() (decoder.py:28-84).  Linear weights are
@@ -173,16 +176,17 @@ int32_t s2r_take(s2r_ctx* ctx, int32_t slot, int64_t* tokens, int32_t capacity, 
  * 4 f64, 5 i32) of a named engine buffer, for zero-copy views: "token",
  * "position", "finished", "ended", "in_shift", "shift_run", "payload",
  * "last_field", "incomplete", "g", "count", "target", "stop", "out",
- * "frames". Replaces reads of BatchDecoder.state / .out (engine.py:138-144). */
+ * "frames", "trace" (with S2R_FLAG_TRACE). Replaces reads of BatchDecoder.state / .out (engine.py:138-144). */
 int32_t s2r_get_buffer(s2r_ctx* ctx, const char* name, void** ptr, int64_t* numel, int32_t* dtype);
 
 /* Run one decode step (it advances the slots like s2r_step) as a CUDA graph
  * with an event node after every kernel and no overlap between kernels, and
  * report per kernel
  * class — 0 qkv, 1 self attention, 2 self out-projection, 3 cross q,
- * 4 cross attention, 5 cross out-projection, 6 fc1, 7 fc2, 8 logits — the
+ * 4 cross attention, 5 cross out-projection, 6 fc1, 7 fc2, 8 logits,
+ * 9 the persistent one-kernel step — the
  * summed device time in ms, the algorithmic bytes of one launch and the
- * launch count (host arrays of 9).  Synchronises `stream`.  Measurement only;
+ * launch count (host arrays of 10).  Synchronises `stream`.  Measurement only;
  * no counterpart in the reference. */
 int32_t s2r_profile_step(s2r_ctx* ctx, float* ms, double* bytes, int32_t* launches, void* stream);
 

@@ -23,6 +23,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "logits.cuh"
+#include "persistent.cuh"
 #include "proj.cuh"
 
 using namespace s2r;
@@ -147,6 +148,7 @@ struct LayerBufs {
   bf16 *wqkv, *bqkv, *wo, *bo, *wcq, *bcq, *wckv, *bckv, *wco, *bco, *w1, *b1, *w2, *b2;
   float *ln_self_g, *ln_self_b, *ln_cross_g, *ln_cross_b, *ln_final_g, *ln_final_b;
   bf16 *kpool, *vpool, *ck, *cv;
+  bf16 *woT, *wcoT, *w2T;  // transposed copies for the persistent step kernel
 };
 
 struct s2r_ctx {
@@ -188,6 +190,13 @@ struct s2r_ctx {
   cudaGraphExec_t graph = nullptr;
   bool graph_dirty = true;
   cudaStream_t cap_stream = nullptr;
+  // persistent step kernel (live rows <= 8)
+  bool persistent = false;
+  int nclusters = 0, units = 0, chunk_cap = 0;
+  PLayer* d_layers = nullptr;
+  float *part_o = nullptr, *part_c = nullptr, *part_f = nullptr;
+  unsigned* bar = nullptr;
+  long long* trace = nullptr;  // S2R_FLAG_TRACE: clock64 marks of the persistent step
   // profiling: when set, an event is recorded after every launch of a step
   std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 };
@@ -210,7 +219,7 @@ int dalloc(s2r_ctx* c, T** p, size_t count) {
     if (rc_ != S2R_OK) return rc_; \
   } while (0)
 
-enum KernelClass { K_QKV = 0, K_SELF_ATTN, K_SELF_OUT, K_CROSS_Q, K_CROSS_ATTN, K_CROSS_OUT, K_FC1, K_FC2, K_LOGITS, K_CLASSES };
+enum KernelClass { K_QKV = 0, K_SELF_ATTN, K_SELF_OUT, K_CROSS_Q, K_CROSS_ATTN, K_CROSS_OUT, K_FC1, K_FC2, K_LOGITS, K_STEP, K_CLASSES };
 
 int mark(s2r_ctx* c, int cls, cudaStream_t s) {
   if (!c->prof) return S2R_OK;
@@ -229,6 +238,28 @@ int mark(s2r_ctx* c, int cls, cudaStream_t s) {
 __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restrict__ dst, size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+// out[j][i] = in[i][j] for a [rows, cols] bf16 matrix.
+__global__ void transpose_bf16_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int rows, int cols) {
+  __shared__ bf16 tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = r0 + k, col = c0 + threadIdx.x;
+    if (r < rows && col < cols) tile[k][threadIdx.x] = in[(size_t)r * cols + col];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int col = c0 + k, r = r0 + threadIdx.x;
+    if (r < rows && col < cols) out[(size_t)col * rows + r] = tile[threadIdx.x][k];
+  }
+}
+
+int transpose_bf16(const bf16* in, bf16* out, int rows, int cols) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+  transpose_bf16_kernel<<<grid, block>>>(in, out, rows, cols);
+  CK(cudaGetLastError());
+  return S2R_OK;
 }
 
 // Copy float32 weights (host or device) into `dst` as bfloat16, through a
@@ -416,8 +447,121 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   return S2R_OK;
 }
 
+typedef void (*StepFn)(const PArgs);
+
+template <int KCH>
+StepFn pick_step_mr(int mr) {
+  switch (mr) {
+    case 1: return step_persistent_kernel<KCH, 1>;
+    case 2: return step_persistent_kernel<KCH, 2>;
+    case 4: return step_persistent_kernel<KCH, 4>;
+    default: return step_persistent_kernel<KCH, 8>;
+  }
+}
+
+StepFn step_fn(int kch, int mr) {
+  switch (kch) {
+    case 1: return pick_step_mr<1>(mr);
+    case 2: return pick_step_mr<2>(mr);
+    default: return pick_step_mr<4>(mr);
+  }
+}
+
+size_t persistent_smem(const s2r_ctx* c, int mr) {
+  auto r = [](size_t b) { return (b + 15) & ~size_t(15); };
+  const size_t D = c->D, KP = (size_t)kch_for(c->D) * 256;
+  size_t bytes = r(4 * mr * D) + r(2 * mr * KP) + r(4 * mr * D) + r(4 * (size_t)mr * c->chunk_cap) +
+                 3 * r(4 * mr * kHeadDim) + r(4 * mr * kQkvLocal) + r(4 * mr * kHeadDim) + r(4 * mr * 2) +
+                 r(4 * mr * kDimsLocal) + r(4 * (size_t)mr * c->units) + r(4 * kPWarps * kHeadDim);
+  // at least 116 KB so that one CTA holds its SM (two would not fit the 228 KB)
+  return std::max<size_t>(bytes, 116 * 1024);
+}
+
+int launch_persistent(s2r_ctx* c, RowMap rm, int M, bool logits, const int64_t* forced, float* logits_out,
+                      int64_t* greedy_out, cudaStream_t s) {
+  PArgs a{};
+  a.M = M;
+  a.rm = rm;
+  a.st = c->st;
+  a.gr = c->gr;
+  a.D = c->D;
+  a.H = c->H;
+  a.FFN = c->FFN;
+  a.V = c->V;
+  a.L = c->L;
+  a.T = c->T;
+  a.F = c->F;
+  a.pps = c->pps;
+  a.units = c->units;
+  a.chunk_cap = c->chunk_cap;
+  a.logits = logits ? 1 : 0;
+  a.layers = c->d_layers;
+  a.tok_emb = c->tok_emb;
+  a.pos_emb = c->pos_emb;
+  a.emb_g = c->emb_ln_g;
+  a.emb_b = c->emb_ln_b;
+  a.emb = c->emb_bf16;
+  a.bias = c->has_bias ? c->bias : nullptr;
+  a.part_o = c->part_o;
+  a.part_c = c->part_c;
+  a.part_f = c->part_f;
+  a.bar = c->bar;
+  a.keys = c->keys;
+  a.counter = c->counter;
+  a.err = c->dev_error;
+  a.forced = forced;
+  a.logits_out = logits_out;
+  a.greedy_out = greedy_out;
+  a.trace = c->trace;
+  a.prefetch = (c->cfg.flags & S2R_FLAG_NO_PREFETCH) ? 0 : 1;
+  const int mr = mc_for(M);
+  StepFn fn = step_fn(kch_for(c->D), mr);
+  const size_t smem = persistent_smem(c, mr);
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(launch_ex(fn, dim3(c->nclusters * kPClus), dim3(kPThreads), smem, s, false, kPClus, a));
+  return S2R_OK;
+}
+
+// Decide whether the persistent kernel can run: rows <= 8, width <= 1024 and
+// at least one cluster of 8 CTAs resident.  Sets nclusters / units / chunk_cap.
+int setup_persistent(s2r_ctx* c) {
+  c->persistent = false;
+  if (!(c->cfg.flags & S2R_FLAG_ONE_KERNEL_STEP) || c->B > kPMaxRows || c->D > 1024 || c->D % 16) return S2R_OK;
+  c->chunk_cap = std::max((c->T + kPClus - 1) / kPClus, (c->F + kPClus - 1) / kPClus);
+  c->units = 64;  // upper bound for the occupancy query
+  StepFn fn = step_fn(kch_for(c->D), 8);
+  const size_t smem = persistent_smem(c, 8);
+  if (smem > 227 * 1024) return S2R_OK;
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kPClus * 64);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = kPClus;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  CK(cudaOccupancyMaxActiveClusters(&n, fn, &cfg));
+  if (n < 1) return S2R_OK;
+  c->nclusters = std::min(n, 64);
+  const int G = c->nclusters * kPClus;
+  c->units = (c->FFN + G - 1) / G;
+  if (c->units > 64) return S2R_OK;
+  c->persistent = true;
+  return S2R_OK;
+}
+
 int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logits, int64_t* greedy) {
   RowMap rm{0, 0, 0, nullptr};
+  if (c->persistent) {
+    TRY(launch_persistent(c, rm, c->B, true, forced, logits, greedy, s));
+    TRY(mark(c, K_STEP, s));
+    return S2R_OK;
+  }
   for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, c->B, l, false, s));
   LogitsArgs a{};
   a.M = c->B;
@@ -525,9 +669,13 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   CK(cudaStreamSynchronize(s));
   if (err == 0) return S2R_OK;
   CK(cudaMemsetAsync(c->dev_error, 0, sizeof(int), s));
+  if (c->bar) CK(cudaMemsetAsync(c->bar, 0, 2 * sizeof(unsigned), s));
+  CK(cudaMemsetAsync(c->counter, 0, sizeof(unsigned), s));
+  CK(cudaMemsetAsync(c->keys, 0, c->B * sizeof(unsigned long long), s));
   return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
               err == kErrAttnCluster ? "attention launched without its cluster shape"
-                                     : "attention keys exceed the score buffer");
+              : err == kErrAttnChunk ? "attention keys exceed the score buffer"
+                                     : "a grid barrier of the persistent step timed out");
 }
 
 template <typename T>
@@ -668,6 +816,36 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     CK(cudaMemset(b.vpool, 0, pool * sizeof(bf16)));
     CK(cudaMemset(b.ck, 0, cross * sizeof(bf16)));
     CK(cudaMemset(b.cv, 0, cross * sizeof(bf16)));
+  }
+  TRYC(setup_persistent(c));
+  if (c->persistent) {
+    std::vector<PLayer> pl(c->L);
+    for (int l = 0; l < c->L; ++l) {
+      LayerBufs& b = c->layers[l];
+      TRYC(dalloc(c, &b.woT, D * D));
+      TRYC(dalloc(c, &b.wcoT, D * D));
+      TRYC(dalloc(c, &b.w2T, FFN * D));
+      TRYC(transpose_bf16(b.wo, b.woT, (int)D, (int)D));
+      TRYC(transpose_bf16(b.wco, b.wcoT, (int)D, (int)D));
+      TRYC(transpose_bf16(b.w2, b.w2T, (int)D, (int)FFN));
+      PLayer& p = pl[l];
+      p.wqkv = b.wqkv; p.bqkv = b.bqkv; p.woT = b.woT; p.bo = b.bo; p.wcq = b.wcq; p.bcq = b.bcq;
+      p.wcoT = b.wcoT; p.bco = b.bco; p.w1 = b.w1; p.b1 = b.b1; p.w2T = b.w2T; p.b2 = b.b2;
+      p.ln_self_g = b.ln_self_g; p.ln_self_b = b.ln_self_b; p.ln_cross_g = b.ln_cross_g;
+      p.ln_cross_b = b.ln_cross_b; p.ln_final_g = b.ln_final_g; p.ln_final_b = b.ln_final_b;
+      p.kpool = b.kpool; p.vpool = b.vpool; p.ck = b.ck; p.cv = b.cv;
+    }
+    TRYC(dalloc(c, &c->d_layers, c->L));
+    CK(cudaMemcpy(c->d_layers, pl.data(), c->L * sizeof(PLayer), cudaMemcpyHostToDevice));
+    TRYC(dalloc(c, &c->part_o, (size_t)c->H * kPMaxRows * D));
+    TRYC(dalloc(c, &c->part_c, (size_t)c->H * kPMaxRows * D));
+    TRYC(dalloc(c, &c->part_f, (size_t)c->nclusters * kPMaxRows * D));
+    TRYC(dalloc(c, &c->bar, 2));
+    CK(cudaMemset(c->bar, 0, 2 * sizeof(unsigned)));
+    if (c->cfg.flags & S2R_FLAG_TRACE) {
+      TRYC(dalloc(c, &c->trace, (size_t)kTraceCtas * kTraceSlots));
+      CK(cudaMemset(c->trace, 0, (size_t)kTraceCtas * kTraceSlots * sizeof(long long)));
+    }
   }
   // activations
   const size_t M = c->maxM;
@@ -876,13 +1054,21 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
     TRY(launch_proj(c, a, memory_dtype == S2R_F32 ? IN_F32 : IN_BF16, EPI_CROSSKV, s));
   }
   // prefix prefill: K/V of prefix[0 .. n-2] at positions 0 .. n-2 (engine.py:199-205)
+  // With the persistent kernel the prefill runs through it too, 8 rows at a
+  // time, so that prefilled K/V are bit-identical to token-by-token decoding.
+  const int chunk_rows = c->persistent ? kPMaxRows : kPrefillRows;
   std::vector<int32_t> toks(kPrefillRows);
-  for (int p0 = 0; p0 < n_prefix - 1; p0 += kPrefillRows) {
-    const int rows = std::min(kPrefillRows, n_prefix - 1 - p0);
+  for (int p0 = 0; p0 < n_prefix - 1; p0 += chunk_rows) {
+    const int rows = std::min(chunk_rows, n_prefix - 1 - p0);
     for (int i = 0; i < rows; ++i) toks[i] = (int32_t)prefix[p0 + i];
-    CK(cudaMemcpyAsync(c->prefill_tokens, toks.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    RowMap rm{1, slot, p0, c->prefill_tokens};
-    for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
+    int32_t* dst = c->prefill_tokens + (c->persistent ? (p0 / chunk_rows) % (kPrefillRows / kPMaxRows) * kPMaxRows : 0);
+    CK(cudaMemcpyAsync(dst, toks.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    RowMap rm{1, slot, p0, dst};
+    if (c->persistent) {
+      TRY(launch_persistent(c, rm, rows, false, nullptr, nullptr, nullptr, s));
+    } else {
+      for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
+    }
   }
   CK(cudaGetLastError());
   c->loaded[slot] = 1;
@@ -986,9 +1172,10 @@ int32_t s2r_get_buffer(s2r_ctx* c, const char* name, void** ptr, int64_t* numel,
       {"payload", st.payload, B, 2},      {"last_field", st.last_field, B, 2}, {"incomplete", st.incomplete, B, 2},
       {"g", st.g, B, 2},                  {"count", st.count, B, 2},         {"target", st.target, B, 2},
       {"stop", st.stop, B, 4},            {"out", st.out, B * c->T, 2},      {"frames", st.frames, B, 5},
+      {"trace", c->trace, c->trace ? kTraceCtas * kTraceSlots : 0, 2},
   };
   for (const Entry& e : table)
-    if (std::strcmp(e.name, name) == 0) {
+    if (std::strcmp(e.name, name) == 0 && e.p != nullptr) {
       *ptr = e.p;
       *numel = e.n;
       *dtype = e.t;
@@ -1028,7 +1215,10 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
       FFN * D * 2 + FFN * 2 + M * D * 8 + M * FFN * 2,        // fc1
       D * FFN * 2 + D * 2 + M * FFN * 2 + M * D * 8,          // fc2
       V * D * 2 + M * D * 4 + V,                              // logits: E, r in, grammar column
+      0.0,                                                    // persistent step: filled below
   };
+  double step_bytes = 0.0;
+  for (int k = 0; k < K_STEP; ++k) step_bytes += per[k] * (k == K_LOGITS ? 1 : c->L);
   for (int b = 0; b < c->B; ++b) {
     if (!c->loaded[b]) continue;
     c->bound[b] = std::min(c->bound[b] + 1, c->T - 1);
@@ -1074,7 +1264,7 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
   }
   for (int k = 0; k < K_CLASSES; ++k) {
     ms[k] = 0.f;
-    bytes[k] = per[k];
+    bytes[k] = k == K_STEP ? step_bytes : per[k];
     launches[k] = 0;
   }
   cudaEvent_t prev = start;
@@ -1090,7 +1280,7 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
   return S2R_OK;
 }
 
-int32_t s2r_step_launches(s2r_ctx* c) { return c ? 8 * c->L + 1 : 0; }
+int32_t s2r_step_launches(s2r_ctx* c) { return c ? (c->persistent ? 1 : 8 * c->L + 1) : 0; }
 
 int32_t s2r_free_pages(s2r_ctx* c) { return c ? (int32_t)c->free_pages.size() : 0; }
 

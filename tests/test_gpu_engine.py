@@ -77,10 +77,14 @@ def test_c1_free_running_greedy():
         assert near_tie(ml, tokens[k], ref[k]), k
 
 
-def test_c1_vs_oracle_bf16():
+STEP_PATHS = pytest.mark.parametrize("flags", [0, 4], ids=["multi-kernel-step", "one-kernel-step"])
+
+
+@STEP_PATHS
+def test_c1_vs_oracle_bf16(flags):
     g = np.load(GOLDEN / "c1_table.npz")
     tokens = g["tokens"].tolist()
-    eng = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 1, sc.C1_FRAMES)
+    eng = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 1, sc.C1_FRAMES, flags=flags)
     ora = oracle_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 1, sc.C1_FRAMES)
     for e in (eng, ora):
         loader(e, sc.C1.width, sc.C1_FRAMES)(0, sc.C1_MEMORY_SEED, tokens[:2], None, sc.C1_FRAMES, sc.C1_STEPS)
@@ -106,6 +110,24 @@ def test_c2_head_vs_reference_golden():
     assert err <= 1.0 and within / count >= LOGIT_WITHIN_FRACTION, (worst, err, within / count)
     assert same >= 23, same
     print(f"c2 vs reference fp32: max |dlogit| {worst:.2e}, within 2e-2 {within}/{count}, agreement {same}/24")
+
+
+def test_one_kernel_and_multi_kernel_steps_agree():
+    """The two step implementations differ only in float32 summation order."""
+
+    g = np.load(GOLDEN / "c2_head.npz")
+    tokens = g["tokens"].tolist()
+    engines = [cuda_engine(sc.C2, sc.C2_SEED, sc.c2_grammar(), 1, sc.C2_FRAMES, flags=f) for f in (4, 0)]
+    assert engines[0].step_launches == 1 and engines[1].step_launches == 8 * sc.C2.layers + 1
+    for e in engines:
+        loader(e, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, 24)
+    err, same = 0.0, 0
+    for k in range(24):
+        (la, ga), (lb, gb) = (e.step_debug(np.array([tokens[2 + k]])) for e in engines)
+        err = max(err, logit_error(la[0], lb[0]))
+        same += int(ga[0] == gb[0])
+    print(f"one-kernel vs multi-kernel step: logit error {err:.3f}, agreement {same}/24")
+    assert err <= 1.0 and same >= 23
 
 
 def test_c2_long_context_vs_oracle():
@@ -175,8 +197,9 @@ def test_continuous_batch_vs_reference_golden():
     assert same / total >= 0.9
 
 
-def test_continuous_batch_vs_oracle_bf16():
-    eng = cuda_engine(sc.C1_SHORT, sc.BATCH_SEED, sc.batch_grammar(), 3, sc.BATCH_FRAMES)
+@STEP_PATHS
+def test_continuous_batch_vs_oracle_bf16(flags):
+    eng = cuda_engine(sc.C1_SHORT, sc.BATCH_SEED, sc.batch_grammar(), 3, sc.BATCH_FRAMES, flags=flags)
     ora = oracle_engine(sc.C1_SHORT, sc.BATCH_SEED, sc.batch_grammar(), 3, sc.BATCH_FRAMES)
     te = sc.continuous_batch(eng, loader(eng, sc.C1_SHORT.width, sc.BATCH_FRAMES))
     to = sc.continuous_batch(ora, loader(ora, sc.C1_SHORT.width, sc.BATCH_FRAMES))
@@ -187,14 +210,15 @@ def test_continuous_batch_vs_oracle_bf16():
     assert same / total >= TOKEN_AGREEMENT
 
 
-def test_prefill_equals_token_by_token():
-    """A 150-token prefix (three prefill chunks) gives bit-identical K/V to forcing it one token at a time."""
+@STEP_PATHS
+def test_prefill_equals_token_by_token(flags):
+    """A 150-token prefix (several prefill chunks) gives bit-identical K/V to forcing it one token at a time."""
 
     rng = np.random.default_rng(11)
     grammar = sc.c1_grammar()
     seq = [SOS, OUT] + rng.integers(4, sc.C1.vocab_size, 160).tolist()
-    a = cuda_engine(sc.C1, sc.C1_SEED, grammar, 1, sc.C1_FRAMES)
-    b = cuda_engine(sc.C1, sc.C1_SEED, grammar, 1, sc.C1_FRAMES)
+    a = cuda_engine(sc.C1, sc.C1_SEED, grammar, 1, sc.C1_FRAMES, flags=flags)
+    b = cuda_engine(sc.C1, sc.C1_SEED, grammar, 1, sc.C1_FRAMES, flags=flags)
     loader(a, sc.C1.width, sc.C1_FRAMES)(0, 3, seq[:152], None, 200, 10_000)
     loader(b, sc.C1.width, sc.C1_FRAMES)(0, 3, seq[:2], None, 200, 10_000)
     for k in range(150):
@@ -205,11 +229,12 @@ def test_prefill_equals_token_by_token():
         assert np.array_equal(la, lb) and ga[0] == gb[0], k
 
 
-def test_slot_independence_bit_exact():
+@STEP_PATHS
+def test_slot_independence_bit_exact(flags):
     """A window decodes to the same tokens alone (batch 1) or in slot 2 of a busy batch of 4."""
 
-    alone = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 1, sc.C1_FRAMES)
-    busy = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 4, sc.C1_FRAMES)
+    alone = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 1, sc.C1_FRAMES, flags=flags)
+    busy = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), 4, sc.C1_FRAMES, flags=flags)
     la = loader(alone, sc.C1.width, sc.C1_FRAMES)
     lb = loader(busy, sc.C1.width, sc.C1_FRAMES)
     la(0, 21, [SOS, OUT, 77], None, 180, 96)
