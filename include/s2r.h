@@ -196,6 +196,24 @@ int32_t s2r_step_launches(s2r_ctx* ctx);
 /* K/V pages of the pool that no slot holds. */
 int32_t s2r_free_pages(s2r_ctx* ctx);
 
+/* Grammar-masked greedy argmax over caller-provided device arrays, with no
+ * device allocation: out[r] = argmax over v of (allowed[r][v] ?
+ * logits[r][v] + bias[v] : -inf), lowest index on ties, 0 for a row with
+ * nothing allowed.  `logits` [rows, vocab] float32, `bias` [vocab] float32 or
+ * NULL, `allowed` [rows, vocab] uint8, `out` [rows] int64, all device memory.
+ * For callers that must not allocate while decoding: code that records a
+ * CUDA graph (an allocation cannot be captured) or a host that gives all
+ * device memory to its own pool allocator up front.  Its cross-CTA scratch is
+ * a static device array of 1024 rows + 1 counter, one copy per GPU that loads
+ * the library; rows > 1024 fail with S2R_EINVAL.  Every call shares that
+ * array, so calls that overlap on the GPU race; each call clears it first.
+ * The first call on a device looks up the array's address and should come
+ * before any stream capture on that device.  Asynchronous on `stream`.
+ * No counterpart in the reference (it computes this step with torch ops,
+ * engine.py:316-317,349-350, inside its engine). */
+int32_t s2r_masked_argmax_noalloc(const float* logits, const float* bias, const uint8_t* allowed, int32_t rows,
+                                  int32_t vocab, int64_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

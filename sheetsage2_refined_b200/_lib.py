@@ -81,6 +81,8 @@ SIGNATURES = {
     "s2r_profile_step": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "s2r_step_launches": (C.c_int32, [C.c_void_p]),
     "s2r_free_pages": (C.c_int32, [C.c_void_p]),
+    "s2r_masked_argmax_noalloc": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
+                                              C.c_void_p]),
 }
 
 _lib = None

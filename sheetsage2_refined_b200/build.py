@@ -19,7 +19,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libs2r.so"
-SOURCES = [CSRC / "engine.cu"]
+SOURCES = [CSRC / "engine.cu", CSRC / "noalloc.cu"]
 HEADERS = sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "s2r.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

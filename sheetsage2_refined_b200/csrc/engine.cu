@@ -686,6 +686,10 @@ int put(T* dev, int slot, T value, cudaStream_t s) {
 
 }  // namespace
 
+__attribute__((visibility("hidden"))) int s2r_record_error(int code, const char* msg) {
+  return fail(code, "%s", msg);
+}
+
 extern "C" {
 
 int32_t s2r_abi_version(void) { return S2R_ABI_VERSION; }
