@@ -199,6 +199,140 @@ def run_reference(args, world, rank):
 
 
 # ---------------------------------------------------------------- GPU arm
+class SingleSong:
+    """One song at batch 1: load its window and decode 2048 greedy tokens (one bench step)."""
+
+    def __init__(self, eng, torch, device, rank):
+        from sheetsage2_refined_b200.weights import memory_array
+
+        self.eng, self.torch, self.device = eng, torch, device
+        mem = torch.from_numpy(memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED + rank)).to(torch.bfloat16)
+        self.mem_dev = mem.to(device)
+        self.mem_pinned = mem.pin_memory()
+        self.h2d = SINGLE_FRAMES * CONFIG.width * 2 + 2 * 8
+        self.d2h = (SINGLE_TOKENS + 3) * 8 + 1
+        self.launches = 0
+
+    def config(self, world):
+        return single_config(world)
+
+    def _count(self):
+        # cross K/V projection (one per layer), the 1-row prefill of the prefix (8 per
+        # layer but only the K/V projection in the last), then the decode steps
+        self.launches += CONFIG.layers + 8 * (CONFIG.layers - 1) + 1 + self.eng.step_launches * SINGLE_TOKENS
+
+    def step_device(self):
+        self.eng.load(0, self.mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+        self.eng.run(SINGLE_TOKENS)
+        self._count()
+        return SINGLE_TOKENS
+
+    def step_e2e(self):
+        self.eng.load(0, self.mem_pinned, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+        self.eng.run(SINGLE_TOKENS)
+        done = self.eng.finished()
+        tokens, _ = self.eng.take(0)
+        assert done == [0] and len(tokens) == SINGLE_TOKENS + 3
+        return SINGLE_TOKENS
+
+    def prepare_profile(self):
+        self.eng.load(0, self.mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+        self.eng.run(SINGLE_TOKENS // 2)
+
+    def finish_profile(self):
+        self.eng.run(SINGLE_TOKENS)
+
+
+class Batched:
+    """64 slots with continuous refill: songs of U[600, 3000] frames and U[512, 4096] tokens.
+
+    One bench step = 64 decode steps of the whole batch (two polls of 32, the
+    reference scheduler's poll interval, transcribe.py:233,360) plus the
+    take / load refills they trigger.  Tokens = position increments of the
+    live slots during the step.
+    """
+
+    POLL = 32
+
+    def __init__(self, eng, torch, device, rank):
+        self.eng, self.torch, self.device = eng, torch, device
+        self.rng = np.random.default_rng(1000 + rank)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(MEMORY_SEED + rank)
+        self.pool = [torch.randn(BATCH_FRAMES, CONFIG.width, generator=gen, device=device).to(torch.bfloat16)
+                     for _ in range(4)]
+        self.pool_pinned = [m.cpu().pin_memory() for m in self.pool]
+        self.k = 0
+        self.launches = 0
+        self.h2d_total = 0
+        self.steps_done = 0
+        self.start_pos = [0] * BATCH
+        for slot in range(BATCH):
+            self._refill(slot, pinned=False)
+
+    def config(self, world):
+        return {"workload": "64-slot continuous batching, 12L d1024 h16 ffn4096 V2048, bf16 memory, frames "
+                            "U[600,3000], targets U[512,4096], refill on finish",
+                "global_batch": BATCH * world, "seq_len": 4096, "parallelism": f"song-sharded x{world}",
+                "l2": "inputs larger than L2 (weights and K/V streamed every step)"}
+
+    def _refill(self, slot, pinned):
+        frames = int(self.rng.integers(600, BATCH_FRAMES + 1))
+        target = int(self.rng.integers(512, 4097))
+        mem = (self.pool_pinned if pinned else self.pool)[self.k % len(self.pool)][:frames]
+        self.k += 1
+        self.eng.load(slot, mem, [SOS, OUT], None, frames, target=target)
+        self.start_pos[slot] = 1
+        self.launches += CONFIG.layers + 8 * (CONFIG.layers - 1) + 1
+        if pinned:
+            self.h2d_total += frames * CONFIG.width * 2 + 16
+
+    def _positions(self):
+        return self.eng.state["position"].cpu().tolist()
+
+    def _step(self, pinned):
+        tokens = 0
+        for _ in range(2):
+            self.eng.run(self.POLL)
+            self.launches += self.eng.step_launches * self.POLL
+            done = self.eng.finished()
+            if done:
+                pos = self._positions()
+                for slot in done:
+                    tokens += pos[slot] - self.start_pos[slot]
+                    self.eng.take(slot)
+                    self._refill(slot, pinned)
+        self.steps_done += 1
+        return tokens
+
+    def step_device(self):
+        return self._measure(False)
+
+    def step_e2e(self):
+        return self._measure(True)
+
+    def _measure(self, pinned):
+        tokens = self._step(pinned)
+        pos = self._positions()
+        tokens += sum(p - s for p, s in zip(pos, self.start_pos))
+        self.start_pos = pos
+        return tokens
+
+    @property
+    def h2d(self):
+        return int(self.h2d_total / max(self.steps_done, 1))
+
+    @property
+    def d2h(self):
+        return BATCH * 8 * 4
+
+    def prepare_profile(self):
+        pass
+
+    def finish_profile(self):
+        pass
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -211,7 +345,6 @@ def run_b200(args, world, rank, local):
 
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     from sheetsage2_refined_b200 import BatchDecoder
-    from sheetsage2_refined_b200.weights import memory_array
 
     grammar = TableGrammar(CONFIG.vocab_size, states=8, density=0.25, seed=GRAMMAR_SEED)
     dec = DecoderWeights(CONFIG, synthetic_state_dict(CONFIG, WEIGHT_SEED))
@@ -219,40 +352,20 @@ def run_b200(args, world, rank, local):
     flags = int(os.environ.get("S2R_ENGINE_FLAGS", "0"))
     if args.workload == "single":
         eng = BatchDecoder(dec, None, batch=1, frames=SINGLE_FRAMES, grammar=grammar, device=device, flags=flags)
-        mem_host = torch.from_numpy(memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED + rank)).to(torch.bfloat16)
-        mem_dev = mem_host.to(device)
-        mem_pinned = mem_host.pin_memory()
-
-        def step_device():
-            eng.load(0, mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
-            eng.run(SINGLE_TOKENS)
-            return SINGLE_TOKENS
-
-        def step_e2e():
-            eng.load(0, mem_pinned, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
-            eng.run(SINGLE_TOKENS)
-            done = eng.finished()
-            tokens, _ = eng.take(0)
-            assert done == [0] and len(tokens) == SINGLE_TOKENS + 3
-            return SINGLE_TOKENS
-
-        h2d = SINGLE_FRAMES * CONFIG.width * 2 + 2 * 8
-        d2h = (SINGLE_TOKENS + 3) * 8 + 1
-        config = single_config(world)
+        work = SingleSong(eng, torch, device, rank)
     else:
-        raise SystemExit("batched workload: not implemented yet")
+        eng = BatchDecoder(dec, None, batch=BATCH, frames=BATCH_FRAMES, grammar=grammar, device=device, flags=flags)
+        work = Batched(eng, torch, device, rank)
 
     stream = torch.cuda.current_stream(device)
-    # warm-up (also captures the step graph)
-    for _ in range(args.warmup):
-        step_device()
+    for _ in range(args.warmup):  # warm-up (also captures the step graph)
+        work.step_device()
     torch.cuda.synchronize(device)
 
-    # roofline: per-kernel times of one profiled step in the middle of a decode
-    eng.load(0, mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
-    eng.run(SINGLE_TOKENS // 2)
+    # roofline: per-kernel times of one profiled step at a representative position
+    work.prepare_profile()
     prof = profile(eng)
-    eng.run(SINGLE_TOKENS)
+    work.finish_profile()
     torch.cuda.synchronize(device)
 
     def timed(fn, k):
@@ -281,10 +394,12 @@ def run_b200(args, world, rank, local):
             gpu_index = int(visible.split(",")[local])
         except (ValueError, IndexError):
             pass
+    launches0 = work.launches
     with ClockSampler(gpu_index) as clocks:
-        ms, tokens = timed(step_device, args.steps)
+        ms, tokens = timed(work.step_device, args.steps)
+    launches = work.launches - launches0
     clock_summary = clocks.summary()
-    ms_e2e, tokens_e2e = timed(step_e2e, max(1, args.steps // 2))
+    ms_e2e, tokens_e2e = timed(work.step_e2e, max(1, args.steps // 2))
 
     ms_max = reduce_max(ms, world, device)
     ms_e2e_max = reduce_max(ms_e2e, world, device)
@@ -306,12 +421,9 @@ def run_b200(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": config,
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            # per step: cross K/V projection (one per layer), the 1-row prefill of the
-            # prefix (8 per layer but only the K/V projection in the last), then the decode
-            "gpu_launches": args.steps * (CONFIG.layers + 8 * (CONFIG.layers - 1) + 1
-                                          + eng.step_launches * SINGLE_TOKENS),
+            "config": work.config(world),
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": work.h2d, "d2h_bytes_per_step": work.d2h},
+            "gpu_launches": launches,
             "clocks": clock_summary,
             "roofline": roofline(prof, peak, peak_kind),
             "step_roofline": prof["step"],
