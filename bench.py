@@ -23,6 +23,7 @@ cores), on a bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -46,6 +47,7 @@ CONFIG = DecoderConfig(vocab_size=2048, width=1024, layers=12, heads=16, ffn_wid
 WEIGHT_SEED, MEMORY_SEED, GRAMMAR_SEED = 1, 101, 8
 SINGLE_FRAMES, SINGLE_TOKENS = 1500, 2048
 BATCH, BATCH_FRAMES = 64, 3000
+OVERRIDES: dict = {}  # profiling-case overrides of the workload, reported in "config"
 CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits", "step")
 
 
@@ -199,6 +201,23 @@ def run_reference(args, world, rank):
 
 
 # ---------------------------------------------------------------- GPU arm
+def load_launches(eng) -> int:
+    """Kernel launches of one ``load`` with the prefix [SOS, OUT] and bfloat16 memory.
+
+    The cross K/V projection (one launch per layer), then the one-row prefill
+    of position 0: a full layer but only the K/V projection in the last one,
+    each LayerNorm'd projection with its own LayerNorm launch on tensor-core
+    engines; the one-kernel step engine prefills with one launch.
+    """
+
+    L, per_step = CONFIG.layers, eng.step_launches
+    if per_step == 1:
+        return L + 1
+    if per_step == 11 * L + 2:
+        return L + 11 * (L - 1) + 2
+    return L + 8 * (L - 1) + 1
+
+
 class SingleSong:
     """One song at batch 1: load its window and decode 2048 greedy tokens (one bench step)."""
 
@@ -217,9 +236,7 @@ class SingleSong:
         return single_config(world)
 
     def _count(self):
-        # cross K/V projection (one per layer), the 1-row prefill of the prefix (8 per
-        # layer but only the K/V projection in the last), then the decode steps
-        self.launches += CONFIG.layers + 8 * (CONFIG.layers - 1) + 1 + self.eng.step_launches * SINGLE_TOKENS
+        self.launches += load_launches(self.eng) + self.eng.step_launches * SINGLE_TOKENS
 
     def step_device(self):
         self.eng.load(0, self.mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
@@ -283,7 +300,7 @@ class Batched:
         self.k += 1
         self.eng.load(slot, mem, [SOS, OUT], None, frames, target=target)
         self.start_pos[slot] = 1
-        self.launches += CONFIG.layers + 8 * (CONFIG.layers - 1) + 1
+        self.launches += load_launches(self.eng)
         if pinned:
             self.h2d_total += frames * CONFIG.width * 2 + 16
 
@@ -421,7 +438,7 @@ def run_b200(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": work.config(world),
+            "config": {**work.config(world), **({"profiling_overrides": OVERRIDES} if OVERRIDES else {})},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": work.h2d, "d2h_bytes_per_step": work.d2h},
             "gpu_launches": launches,
             "clocks": clock_summary,
@@ -477,7 +494,19 @@ def main():
     ap.add_argument("--workload", default="single", choices=("single", "batched"))
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    # smaller cases of the same kernels for ncu captures that must fit a few GB (not bench lines)
+    ap.add_argument("--layers", type=int, default=None, help="override the decoder depth (profiling cases)")
+    ap.add_argument("--max-tokens", type=int, default=None, help="override the context length (profiling cases)")
+    ap.add_argument("--batch-frames", type=int, default=None, help="override the batched frames cap (profiling cases)")
     args = ap.parse_args()
+    global CONFIG, BATCH_FRAMES, OVERRIDES
+    if args.layers or args.max_tokens:
+        CONFIG = dataclasses.replace(CONFIG, layers=args.layers or CONFIG.layers,
+                                     max_tokens=args.max_tokens or CONFIG.max_tokens)
+        OVERRIDES.update(layers=CONFIG.layers, max_tokens=CONFIG.max_tokens)
+    if args.batch_frames:
+        BATCH_FRAMES = args.batch_frames
+        OVERRIDES.update(batch_frames=BATCH_FRAMES)
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)

@@ -71,6 +71,9 @@ typedef struct s2r_config {
 #define S2R_FLAG_ONE_KERNEL_STEP 4u /* batch <= 8: run a step as one persistent kernel */
 #define S2R_FLAG_TRACE 8u          /* one-kernel step records clock64 marks per phase ("trace" buffer) */
 #define S2R_FLAG_NO_PREFETCH 16u   /* one-kernel step without next-phase L2 prefetches */
+#define S2R_FLAG_NO_TENSOR_CORE 32u /* every projection on the CUDA-core kernel (by default the cross K/V
+                                       projection at load, and with batch >= 16 the step and prefill
+                                       projections, run on tcgen05 tensor cores) */
 
 /* One decoder layer's float32 parameters, named as in
  * TokenDecoder.state_dict() (decoder.py:28-84).  Linear weights are
@@ -176,7 +179,9 @@ int32_t s2r_take(s2r_ctx* ctx, int32_t slot, int64_t* tokens, int32_t capacity, 
  * 4 f64, 5 i32) of a named engine buffer, for zero-copy views: "token",
  * "position", "finished", "ended", "in_shift", "shift_run", "payload",
  * "last_field", "incomplete", "g", "count", "target", "stop", "out",
- * "frames", "trace" (with S2R_FLAG_TRACE). Replaces reads of BatchDecoder.state / .out (engine.py:138-144). */
+ * "frames", "trace" (with S2R_FLAG_TRACE), "cross_k" / "cross_v" (layer 0's cross K/V, bf16
+ * [batch][heads][frames][64], for inspection). Replaces reads of BatchDecoder.state / .out
+ * (engine.py:138-144). */
 int32_t s2r_get_buffer(s2r_ctx* ctx, const char* name, void** ptr, int64_t* numel, int32_t* dtype);
 
 /* Run one decode step (it advances the slots like s2r_step) as a CUDA graph

@@ -19,8 +19,10 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libs2r.so"
-SOURCES = [CSRC / "engine.cu", CSRC / "noalloc.cu"]
-HEADERS = sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "s2r.h"]
+SOURCES = [CSRC / "engine.cu", CSRC / "noalloc.cu", CSRC / "kernels_select.cu", CSRC / "kernels_tc.cu",
+           CSRC / "kernels_proj_ln.cu", CSRC / "kernels_proj_rows.cu", CSRC / "kernels_step_1.cu",
+           CSRC / "kernels_step_2.cu", CSRC / "kernels_step_4.cu"]
+HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "s2r.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -39,18 +41,31 @@ def stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every translation unit in parallel, then link the shared library."""
+
     if not force and not stale():
         return LIB
-    cmd = [
-        nvcc(), *ARCH, "-O3", "-std=c++17", "-lineinfo", "-shared", "-Xcompiler", "-fPIC",
-        "-Xptxas", "-v" if verbose else "-O3",
-        "-I", str(ROOT / "include"), *map(str, SOURCES), "-o", str(LIB) + ".tmp",
-    ]
-    res = subprocess.run(cmd, capture_output=True, text=True)
+    objdir = PKG / "_build"
+    objdir.mkdir(exist_ok=True)
+    flags = [*ARCH, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", str(ROOT / "include")]
+    procs = []
+    for src in SOURCES:
+        obj = objdir / (src.stem + ".o")
+        cmd = [nvcc(), *flags, "-Xptxas", "-v" if verbose else "-O3", "-c", str(src), "-o", str(obj)]
+        procs.append((src, obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    failed = []
+    for src, obj, proc in procs:
+        out, err = proc.communicate()
+        if proc.returncode != 0:
+            failed.append(f"{src.name} ({proc.returncode}):\n{out}\n{err}")
+        elif verbose:
+            sys.stderr.write(err)
+    if failed:
+        raise RuntimeError("nvcc failed: " + "\n".join(failed))
+    link = [nvcc(), *ARCH, "-shared", *[str(obj) for _, obj, _ in procs], "-o", str(LIB) + ".tmp"]
+    res = subprocess.run(link, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError(f"link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     os.replace(str(LIB) + ".tmp", LIB)
     return LIB
 

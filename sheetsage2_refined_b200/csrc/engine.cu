@@ -9,6 +9,8 @@
 // captured once serves every step, whatever the slots' lengths; consecutive
 // kernels are chained with programmatic dependent launch so that each one
 // starts streaming its weights while the previous one finishes.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -16,12 +18,16 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/s2r.h"
 #include "attention.cuh"
 #include "common.cuh"
+#include "gemm_tc.cuh"
+#include "kernels.h"
 #include "logits.cuh"
 #include "persistent.cuh"
 #include "proj.cuh"
@@ -54,9 +60,9 @@ int kch_for(int k) { return k <= 256 ? 1 : k <= 512 ? 2 : k <= 1024 ? 4 : k <= 2
 int mc_for(int m) { return m >= 5 ? 8 : m >= 3 ? 4 : m; }
 
 // Launch with optional programmatic dependent launch and cluster shape.
-template <typename Arg>
-cudaError_t launch_ex(void (*kernel)(Arg), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                      int cluster, const Arg& arg) {
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      int cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -78,62 +84,7 @@ cudaError_t launch_ex(void (*kernel)(Arg), dim3 grid, dim3 block, size_t smem, c
   }
   cfg.attrs = attrs;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kernel, arg);
-}
-
-typedef void (*ProjFn)(const ProjArgs);
-typedef void (*LogitsFn)(const LogitsArgs);
-
-template <int IN, int EPI, int KCH>
-ProjFn pick_mc(int mc) {
-  switch (mc) {
-    case 1: return proj_kernel<KCH, 1, IN, EPI>;
-    case 2: return proj_kernel<KCH, 2, IN, EPI>;
-    case 4: return proj_kernel<KCH, 4, IN, EPI>;
-    default: return proj_kernel<KCH, 8, IN, EPI>;
-  }
-}
-
-template <int IN, int EPI>
-ProjFn pick_proj(int kch, int mc) {
-  switch (kch) {
-    case 1: return pick_mc<IN, EPI, 1>(mc);
-    case 2: return pick_mc<IN, EPI, 2>(mc);
-    case 4: return pick_mc<IN, EPI, 4>(mc);
-    case 8: return pick_mc<IN, EPI, 8>(mc);
-    default: return pick_mc<IN, EPI, 16>(mc);
-  }
-}
-
-ProjFn proj_fn(int in, int epi, int kch, int mc) {
-  if (in == IN_EMBED && epi == EPI_QKV) return pick_proj<IN_EMBED, EPI_QKV>(kch, mc);
-  if (in == IN_LN && epi == EPI_QKV) return pick_proj<IN_LN, EPI_QKV>(kch, mc);
-  if (in == IN_LN && epi == EPI_BF16) return pick_proj<IN_LN, EPI_BF16>(kch, mc);
-  if (in == IN_LN && epi == EPI_GELU) return pick_proj<IN_LN, EPI_GELU>(kch, mc);
-  if (in == IN_BF16 && epi == EPI_RESID) return pick_proj<IN_BF16, EPI_RESID>(kch, mc);
-  if (in == IN_BF16 && epi == EPI_CROSSKV) return pick_proj<IN_BF16, EPI_CROSSKV>(kch, mc);
-  if (in == IN_F32 && epi == EPI_CROSSKV) return pick_proj<IN_F32, EPI_CROSSKV>(kch, mc);
-  return nullptr;
-}
-
-template <int KCH>
-LogitsFn pick_logits_mc(int mc) {
-  switch (mc) {
-    case 1: return logits_kernel<KCH, 1>;
-    case 2: return logits_kernel<KCH, 2>;
-    case 4: return logits_kernel<KCH, 4>;
-    default: return logits_kernel<KCH, 8>;
-  }
-}
-
-LogitsFn logits_fn(int kch, int mc) {
-  switch (kch) {
-    case 1: return pick_logits_mc<1>(mc);
-    case 2: return pick_logits_mc<2>(mc);
-    case 4: return pick_logits_mc<4>(mc);
-    case 8: return pick_logits_mc<8>(mc);
-    default: return pick_logits_mc<16>(mc);
-  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Host replay of the class grammar (grammar.py:140-180), used for prefixes.
@@ -197,6 +148,13 @@ struct s2r_ctx {
   float *part_o = nullptr, *part_c = nullptr, *part_f = nullptr;
   unsigned* bar = nullptr;
   long long* trace = nullptr;  // S2R_FLAG_TRACE: clock64 marks of the persistent step
+  // tensor-core projections (tcgen05 GEMM): the step and prefill projections
+  // when `tc` (16 or more slots), the cross K/V projection at load when `tc_cross`
+  bool tc = false, tc_cross = false;
+  int tc_nb = 64;                  // rows per MMA tile of the step and prefill projections
+  int attn_splits = 8;             // CTAs (one cluster) per (row, head) of the attention
+  bf16* xln = nullptr;             // [maxM][KP] LayerNorm'd rows, the X operand of LN'd projections
+  bf16* mem_bf16 = nullptr;        // [F][D] float32 encoder memory rounded to bf16
   // profiling: when set, an event is recorded after every launch of a step
   std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 };
@@ -287,7 +245,101 @@ ProjArgs proj_base(s2r_ctx* c) {
   return a;
 }
 
+// ---- tensor-core projections --------------------------------------------
+
+constexpr int kTcMinBatch = 16;     // engines with this many slots run step projections on tensor cores
+constexpr int kTcMinKPerSplit = 2;  // K tiles (of 64) per split-K slice, at least
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major bf16 matrix [rows][inner] with `row_bytes` between rows, read in
+// boxes of 64 columns x box_rows rows with the 128-byte swizzle; reads outside
+// the matrix return zeros.
+int encode_rows(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(S2R_ECUDA, "the driver has no cuTensorMapEncodeTiled");
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 || row_bytes % 16 || rows == 0 || inner == 0)
+    return fail(S2R_EINVAL, "tensor map: pointer or row stride not 16-byte aligned, or an empty matrix");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)kTcBlockK, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(S2R_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return S2R_OK;
+}
+
+// Split-K cluster size (1, 2, 4 or 8) for `tiles` output tiles of k_tiles K
+// tiles each: enough CTAs to cover the SMs, at least kTcMinKPerSplit K tiles
+// per slice.  The step and prefill projections pass the feature tiles only,
+// so that the split, and with it a row's result, does not depend on how many
+// rows share the launch.
+void tc_split(int tiles, int k_tiles, int sms, int* splits, int* per) {
+  int sp = 1;
+  while (sp < kTcMaxSplits && tiles * sp * 2 <= sms && k_tiles / (sp * 2) >= kTcMinKPerSplit) sp *= 2;
+  *per = (k_tiles + sp - 1) / sp;
+  *splits = sp;
+}
+
+// One projection on tensor cores: the LayerNorm or float32 conversion that
+// produces its bf16 rows (when the input is not bf16 already), then the GEMM
+// with the projection's epilogue.  `lg` is the logits epilogue's state.
+int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, const LogitsArgs* lg = nullptr) {
+  const bool cross = epi == EPI_CROSSKV;
+  const int nb = cross ? 128 : c->tc_nb;
+  const void* x = a.xin;
+  int ldx = a.ldx;
+  if (in == IN_LN || in == IN_EMBED) {
+    const int kch = kch_for(a.K);
+    LnFn fn = ln_fn(in, kch);
+    CK(launch_ex(fn, dim3((a.M + 3) / 4), dim3(128), 0, s, c->pdl, 0, a, c->xln));
+    x = c->xln;
+    ldx = kch * 256;
+  } else if (in == IN_F32) {
+    if (a.ldx != a.K || a.K % 8) return fail(S2R_ENOTSUP, "float32 rows must be dense with K a multiple of 8");
+    const size_t n = (size_t)a.M * a.K;
+    f32_to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4 * (size_t)c->num_sms), 256, 0, s>>>(
+        static_cast<const float*>(a.xin), c->mem_bf16, n);
+    CK(cudaGetLastError());
+    x = c->mem_bf16;
+  }
+  const int n_tiles = (a.N + kTcBlockN - 1) / kTcBlockN, m_tiles = (a.M + nb - 1) / nb;
+  const int k_tiles = (a.K + kTcBlockK - 1) / kTcBlockK;
+  int splits = 1, per = k_tiles;
+  tc_split(cross ? n_tiles * m_tiles : n_tiles, k_tiles, c->num_sms, &splits, &per);
+  GemmFn fn = gemm_fn(nb, epi);
+  if (!fn) return fail(S2R_ENOTSUP, "no tensor-core projection for epilogue %d with %d-row tiles", epi, nb);
+  CUtensorMap map_w, map_x;
+  TRY(encode_rows(&map_w, a.W, a.K, a.N, (uint64_t)a.K * sizeof(bf16), kTcBlockN));
+  TRY(encode_rows(&map_x, x, a.K, a.M, (uint64_t)ldx * sizeof(bf16), nb));
+  TcArgs t{};
+  t.p = a;
+  t.k_tiles_per_split = per;
+  t.err = c->dev_error;
+  if (lg) t.lg = *lg;
+  const size_t smem = tc_smem_bytes(nb);
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(launch_ex(fn, dim3(splits, n_tiles, m_tiles), dim3(kTcThreads), smem, s, c->pdl, splits > 1 ? splits : 0, map_w,
+               map_x, t));
+  return S2R_OK;
+}
+
 int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
+  if (epi == EPI_CROSSKV ? c->tc_cross : c->tc) return launch_proj_tc(c, a, in, epi, s);
   const int kch = kch_for(a.K), mc = mc_for(std::min(a.M, 8));
   ProjFn fn = proj_fn(in, epi, kch, mc);
   if (!fn) return fail(S2R_ENOTSUP, "no projection kernel for in=%d epi=%d", in, epi);
@@ -298,10 +350,20 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
   return S2R_OK;
 }
 
-// Every (row, head) is split over the same number of CTAs whatever the batch,
-// so a row's result never depends on how many rows share the launch (decode
-// at any batch and prefill chunks give bit-identical K/V and outputs).
+// Every (row, head) of an engine is split over the same number of CTAs
+// (attn_splits) whatever the rows of the launch, so a row's result never
+// depends on how many rows share it (decode with any slots live and prefill
+// chunks give bit-identical K/V and outputs).  Engines of fewer than 16 slots
+// split 8 ways; tensor-core engines split so that the (row, head) pairs of a
+// full batch cover the SMs about four times.
 constexpr int kAttnSplits = 8;
+
+int attn_splits_for(const s2r_ctx* c) {
+  if (!c->tc) return kAttnSplits;
+  int sp = 1;
+  while (sp < kAttnSplits && c->B * c->H * sp * 2 <= 4 * c->num_sms) sp *= 2;
+  return sp;
+}
 
 int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s) {
   AttnArgs a{};
@@ -318,9 +380,9 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   a.v = cross ? c->layers[layer].cv : c->layers[layer].vpool;
   a.pages_per_slot = c->pps;
   a.frames_cap = c->F;
-  a.splits = kAttnSplits;
+  a.splits = c->attn_splits;
   a.err = c->dev_error;
-  const int C = kAttnSplits;
+  const int C = c->attn_splits;
   const int maxlen = cross ? c->F : c->T;
   a.chunk_cap = (maxlen + C - 1) / C;
   const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
@@ -447,26 +509,6 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   return S2R_OK;
 }
 
-typedef void (*StepFn)(const PArgs);
-
-template <int KCH>
-StepFn pick_step_mr(int mr) {
-  switch (mr) {
-    case 1: return step_persistent_kernel<KCH, 1>;
-    case 2: return step_persistent_kernel<KCH, 2>;
-    case 4: return step_persistent_kernel<KCH, 4>;
-    default: return step_persistent_kernel<KCH, 8>;
-  }
-}
-
-StepFn step_fn(int kch, int mr) {
-  switch (kch) {
-    case 1: return pick_step_mr<1>(mr);
-    case 2: return pick_step_mr<2>(mr);
-    default: return pick_step_mr<4>(mr);
-  }
-}
-
 size_t persistent_smem(const s2r_ctx* c, int mr) {
   auto r = [](size_t b) { return (b + 15) & ~size_t(15); };
   const size_t D = c->D, KP = (size_t)kch_for(c->D) * 256;
@@ -580,6 +622,21 @@ int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logit
   a.forced = forced;
   a.logits_out = logits;
   a.greedy_out = greedy;
+  if (c->tc) {
+    ProjArgs p = proj_base(c);
+    p.rm = rm;
+    p.M = c->B;
+    p.K = c->D;
+    p.N = c->V;
+    p.r = c->r;
+    p.gamma = a.gamma;
+    p.beta = a.beta;
+    p.x_out = nullptr;
+    p.W = c->emb_bf16;
+    TRY(launch_proj_tc(c, p, IN_LN, EPI_LOGITS, s, &a));
+    TRY(mark(c, K_LOGITS, s));
+    return S2R_OK;
+  }
   const int kch = kch_for(c->D), mc = mc_for(std::min(c->B, 8));
   LogitsFn fn = logits_fn(kch, mc);
   const size_t smem = (size_t)mc * kch * 256 * sizeof(bf16);
@@ -662,6 +719,26 @@ void replay_class(const s2r_ctx* c, HostGrammarState& st, int64_t tok) {
   }
 }
 
+// Tensor-core projection buffers.  The step and prefill projections and the
+// logits run on tensor cores when the engine has kTcMinBatch or more slots
+// (fewer rows are faster on the CUDA-core kernels, which stream the weights
+// once at full width); the cross K/V projection at load always does.
+// S2R_FLAG_NO_TENSOR_CORE keeps every projection on the CUDA-core kernels.
+int setup_tensor_core(s2r_ctx* c) {
+  const bool allowed = !(c->cfg.flags & S2R_FLAG_NO_TENSOR_CORE);
+  if (allowed && !tensor_map_encoder()) return fail(S2R_ECUDA, "the driver has no cuTensorMapEncodeTiled");
+  c->tc_cross = allowed;
+  c->tc = allowed && !c->persistent && c->B >= kTcMinBatch && c->D >= kTcBlockN;
+  c->tc_nb = c->maxM <= 64 ? 64 : c->maxM <= 128 ? 128 : 256;
+  if (!allowed) return S2R_OK;
+  if (c->tc) {
+    TRY(dalloc(c, &c->xln, (size_t)c->maxM * kch_for(c->D) * 256));
+    CK(cudaMemset(c->xln, 0, (size_t)c->maxM * kch_for(c->D) * 256 * sizeof(bf16)));
+  }
+  TRY(dalloc(c, &c->mem_bf16, (size_t)c->F * c->D));
+  return S2R_OK;
+}
+
 // Read (and clear) the device error word after the stream's work has finished.
 int check_device_error(s2r_ctx* c, cudaStream_t s) {
   int err = 0;
@@ -675,6 +752,7 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
               err == kErrAttnCluster ? "attention launched without its cluster shape"
               : err == kErrAttnChunk ? "attention keys exceed the score buffer"
+              : err == kErrGemmWait  ? "a wait of the tensor-core projection timed out"
                                      : "a grid barrier of the persistent step timed out");
 }
 
@@ -862,6 +940,8 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   TRYC(dalloc(c, &mem_stage, (size_t)c->F * D));
   c->mem_stage = mem_stage;
   TRYC(dalloc(c, &c->prefill_tokens, kPrefillRows));
+  TRYC(setup_tensor_core(c));
+  c->attn_splits = attn_splits_for(c);
   TRYC(dalloc(c, &c->keys, c->B));
   TRYC(dalloc(c, &c->counter, 1));
   TRYC(dalloc(c, &c->dev_error, 1));
@@ -1177,6 +1257,8 @@ int32_t s2r_get_buffer(s2r_ctx* c, const char* name, void** ptr, int64_t* numel,
       {"g", st.g, B, 2},                  {"count", st.count, B, 2},         {"target", st.target, B, 2},
       {"stop", st.stop, B, 4},            {"out", st.out, B * c->T, 2},      {"frames", st.frames, B, 5},
       {"trace", c->trace, c->trace ? kTraceCtas * kTraceSlots : 0, 2},
+      {"cross_k", c->layers[0].ck, B * c->H * c->F * kHeadDim, 1},
+      {"cross_v", c->layers[0].cv, B * c->H * c->F * kHeadDim, 1},
   };
   for (const Entry& e : table)
     if (std::strcmp(e.name, name) == 0 && e.p != nullptr) {
@@ -1284,7 +1366,12 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
   return S2R_OK;
 }
 
-int32_t s2r_step_launches(s2r_ctx* c) { return c ? (c->persistent ? 1 : 8 * c->L + 1) : 0; }
+int32_t s2r_step_launches(s2r_ctx* c) {
+  if (!c) return 0;
+  if (c->persistent) return 1;
+  // tensor-core engines add a LayerNorm launch before each LayerNorm'd projection and the logits
+  return c->tc ? 11 * c->L + 2 : 8 * c->L + 1;
+}
 
 int32_t s2r_free_pages(s2r_ctx* c) { return c ? (int32_t)c->free_pages.size() : 0; }
 

@@ -1,0 +1,14 @@
+// CUDA-core projections of LayerNorm'd rows (QKV, cross q, fc1).
+#include "kernels.h"
+
+namespace s2r {
+
+ProjFn proj_fn_ln(int in, int epi, int kch, int mc) {
+  if (in == IN_EMBED && epi == EPI_QKV) return pick_proj<IN_EMBED, EPI_QKV>(kch, mc);
+  if (in == IN_LN && epi == EPI_QKV) return pick_proj<IN_LN, EPI_QKV>(kch, mc);
+  if (in == IN_LN && epi == EPI_BF16) return pick_proj<IN_LN, EPI_BF16>(kch, mc);
+  if (in == IN_LN && epi == EPI_GELU) return pick_proj<IN_LN, EPI_GELU>(kch, mc);
+  return nullptr;
+}
+
+}  // namespace s2r

@@ -126,6 +126,37 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
 }
 
+// Commit one step for rows [0, M) once every key is final: the greedy token
+// (or the forced one) is written to out[slot, position+1], the grammar
+// advances and the keys return to zero.  Run by one CTA.
+__device__ __forceinline__ void commit_rows(const LogitsArgs& a) {
+  for (int s = threadIdx.x; s < a.M; s += blockDim.x) {
+    const unsigned long long k = atomicExch(a.keys + s, 0ull);
+    // all tokens masked: torch.argmax over a row of -inf returns index 0
+    const int64_t greedy = k ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
+    if (a.greedy_out) a.greedy_out[s] = greedy;
+    const bool active = a.st.finished[s] == 0;
+    const int64_t tok = a.st.token[s], pos = a.st.position[s];
+    int64_t choice = greedy;
+    if (a.forced && a.forced[s] >= 0) choice = a.forced[s];
+    if (!active) choice = tok;
+    const int64_t new_pos = active ? pos + 1 : pos;
+    if (active && new_pos < a.max_tokens) a.st.out[(size_t)s * a.max_tokens + new_pos] = choice;
+    grammar_update(a.gr, a.st, s, choice, active, new_pos >= a.max_tokens - 1);
+    a.st.token[s] = choice;
+    a.st.position[s] = new_pos;
+  }
+}
+
+// The grammar rule of row s: its class mask (class grammar) or its state (table grammar).
+__device__ __forceinline__ uint32_t row_rule(const Grammar& gr, const SlotState& st, int s) {
+  return gr.kind == 1 ? (uint32_t)st.g[s] : class_mask(st, s);
+}
+
+__device__ __forceinline__ bool token_allowed(const Grammar& gr, uint32_t rule, int V, int v) {
+  return gr.kind == 1 ? gr.table[(size_t)rule * V + v] != 0 : ((rule >> gr.token_class[v]) & 1u) != 0;
+}
+
 constexpr int kLogitsThreads = 256;
 
 template <int KCH, int MC>
@@ -170,7 +201,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
     }
     if (threadIdx.x < MC) {
       const int s = m0 + threadIdx.x;
-      rule[threadIdx.x] = threadIdx.x < mc ? (a.gr.kind == 1 ? (uint32_t)a.st.g[s] : class_mask(a.st, s)) : 0u;
+      rule[threadIdx.x] = threadIdx.x < mc ? row_rule(a.gr, a.st, s) : 0u;
     }
     __syncthreads();
 
@@ -224,22 +255,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int s = threadIdx.x; s < a.M; s += blockDim.x) {
-    const unsigned long long k = atomicExch(a.keys + s, 0ull);
-    // all tokens masked: torch.argmax over a row of -inf returns index 0
-    const int64_t greedy = k ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
-    if (a.greedy_out) a.greedy_out[s] = greedy;
-    const bool active = a.st.finished[s] == 0;
-    const int64_t tok = a.st.token[s], pos = a.st.position[s];
-    int64_t choice = greedy;
-    if (a.forced && a.forced[s] >= 0) choice = a.forced[s];
-    if (!active) choice = tok;
-    const int64_t new_pos = active ? pos + 1 : pos;
-    if (active && new_pos < a.max_tokens) a.st.out[(size_t)s * a.max_tokens + new_pos] = choice;
-    grammar_update(a.gr, a.st, s, choice, active, new_pos >= a.max_tokens - 1);
-    a.st.token[s] = choice;
-    a.st.position[s] = new_pos;
-  }
+  commit_rows(a);
   if (threadIdx.x == 0) *a.counter = 0u;
 }
 

@@ -97,12 +97,6 @@ __device__ __forceinline__ void trace_mark(const PArgs& a, int idx) {
   if (which >= 0) a.trace[which * kTraceSlots + idx] = clock64();
 }
 
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // L2-coherent loads (data written earlier in this launch by other SMs) and
 // read-only weight loads.
 __device__ __forceinline__ uint4 ld_cg(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
@@ -541,7 +535,7 @@ __device__ void cluster_attention(const PArgs& a, cg::cluster_group& cluster, PS
 // L2 prefetches for what this CTA reads in its next phase (weights and the
 // K/V of positions already cached), so that HBM streams them while the grid
 // barrier resolves.  phase: 0 = A of `layer`, 1 = B, 2 = C, 3 = logits.
-__device__ void prefetch_phase(const PArgs& a, int phase, int layer, int rank, int ci, unsigned nclusters) {
+static __device__ void prefetch_phase(const PArgs& a, int phase, int layer, int rank, int ci, unsigned nclusters) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane != 0 || !a.prefetch) return;
   const int D = a.D, H = a.H;

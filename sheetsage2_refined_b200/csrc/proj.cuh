@@ -114,7 +114,7 @@ __device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, f
 // holds its 8*KCH columns in registers (two-pass mean / variance).
 template <int KCH, int IN>
 __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m0, int mc, int warp, int lane,
-                                              int nwarps) {
+                                              int nwarps, bool own_rows = false) {
   constexpr int KP = KCH * 256;
   const int K = a.K;
   for (int i = warp; i < mc; i += nwarps) {
@@ -163,7 +163,9 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
       }
     }
     const float rstd = rsqrtf(warp_sum(sq) / (float)K + kLnEps);
-    const bool keep = a.x_out != nullptr && (m % gridDim.x) == blockIdx.x;
+    // x_out is written once per row: by this CTA when it owns the rows it
+    // stages, else by CTA m % gridDim.x (every CTA stages every row)
+    const bool keep = a.x_out != nullptr && (own_rows || (m % gridDim.x) == blockIdx.x);
 #pragma unroll
     for (int c = 0; c < KCH; ++c) {
       const int col = c * 256 + lane * 8;
