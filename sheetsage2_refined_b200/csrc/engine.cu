@@ -108,6 +108,7 @@ struct s2r_ctx {
   int D = 0, H = 0, F = 0, FFN = 0, V = 0, L = 0, B = 0, T = 0, maxM = 0, pps = 0, n_pages = 0;
   int num_sms = 148;
   bool pdl = true, use_graph = true;
+  bool fence_next = false;  // the next launch starts a decode step or prefill chunk: no programmatic overlap
   std::vector<void*> allocs;
   // weights
   float *tok_emb = nullptr, *pos_emb = nullptr, *emb_ln_g = nullptr, *emb_ln_b = nullptr;
@@ -236,6 +237,17 @@ int upload_f32(float* dst, const float* src, size_t n) {
   return S2R_OK;
 }
 
+// Programmatic dependent launch for the next kernel, except for the first
+// kernel of a decode step or prefill chunk (fence_next): that one starts after
+// everything before it has completed, so the step's kernels may read data
+// written before the step (cross K/V, earlier positions' K/V) ahead of their
+// griddepcontrol.wait.
+bool next_pdl(s2r_ctx* c) {
+  const bool fenced = c->fence_next;
+  c->fence_next = false;
+  return c->pdl && !fenced;
+}
+
 ProjArgs proj_base(s2r_ctx* c) {
   ProjArgs a{};
   a.st = c->st;
@@ -306,7 +318,7 @@ int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, cons
   if (in == IN_LN || in == IN_EMBED) {
     const int kch = kch_for(a.K);
     LnFn fn = ln_fn(in, kch);
-    CK(launch_ex(fn, dim3((a.M + 3) / 4), dim3(128), 0, s, c->pdl, 0, a, c->xln));
+    CK(launch_ex(fn, dim3((a.M + 3) / 4), dim3(128), 0, s, next_pdl(c), 0, a, c->xln));
     x = c->xln;
     ldx = kch * 256;
   } else if (in == IN_F32) {
@@ -333,7 +345,7 @@ int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, cons
   if (lg) t.lg = *lg;
   const size_t smem = tc_smem_bytes(nb);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  CK(launch_ex(fn, dim3(splits, n_tiles, m_tiles), dim3(kTcThreads), smem, s, c->pdl, splits > 1 ? splits : 0, map_w,
+  CK(launch_ex(fn, dim3(splits, n_tiles, m_tiles), dim3(kTcThreads), smem, s, next_pdl(c), splits > 1 ? splits : 0, map_w,
                map_x, t));
   return S2R_OK;
 }
@@ -346,7 +358,7 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
   const size_t smem = (size_t)(mc == 8 ? 8 : mc) * kch * 256 * sizeof(bf16);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int blocks = (a.N + 3) / 4;
-  CK(launch_ex(fn, dim3(blocks), dim3(128), smem, s, c->pdl, 0, a));
+  CK(launch_ex(fn, dim3(blocks), dim3(128), smem, s, next_pdl(c), 0, a));
   return S2R_OK;
 }
 
@@ -387,7 +399,7 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   a.chunk_cap = (maxlen + C - 1) / C;
   const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
   CK(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  CK(launch_ex(attn_kernel, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, c->pdl, C, a));
+  CK(launch_ex(attn_kernel, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
   return S2R_OK;
 }
 
@@ -599,6 +611,7 @@ int setup_persistent(s2r_ctx* c) {
 
 int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logits, int64_t* greedy) {
   RowMap rm{0, 0, 0, nullptr};
+  c->fence_next = true;
   if (c->persistent) {
     TRY(launch_persistent(c, rm, c->B, true, forced, logits, greedy, s));
     TRY(mark(c, K_STEP, s));
@@ -642,7 +655,7 @@ int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logit
   const size_t smem = (size_t)mc * kch * 256 * sizeof(bf16);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int blocks = std::max(1, std::min((c->V + 7) / 8, 2 * c->num_sms));
-  CK(launch_ex(fn, dim3(blocks), dim3(kLogitsThreads), smem, s, c->pdl, 0, a));
+  CK(launch_ex(fn, dim3(blocks), dim3(kLogitsThreads), smem, s, next_pdl(c), 0, a));
   TRY(mark(c, K_LOGITS, s));
   return S2R_OK;
 }
@@ -1151,6 +1164,7 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
     if (c->persistent) {
       TRY(launch_persistent(c, rm, rows, false, nullptr, nullptr, nullptr, s));
     } else {
+      c->fence_next = true;
       for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
     }
   }

@@ -22,7 +22,7 @@
 // writes its fp32 partial tile to its own shared memory; after a cluster
 // barrier CTA s adds rows [s*NB/S, (s+1)*NB/S) of all S partials, in slice
 // order, through distributed shared memory and runs the epilogue on them.  No
-// partial leaves the SM cluster and the sum order is fixed.
+// partial leaves the cluster and the sum order is fixed.
 //
 // Epilogues: those of proj.cuh (bias, bf16 rounding, residual, GELU, paged K/V
 // append, cross K/V scatter; the same function the CUDA-core kernel runs) and
@@ -41,6 +41,7 @@
 
 #include "common.cuh"
 #include "logits.cuh"
+#include "mbarrier.cuh"
 #include "proj.cuh"
 
 namespace s2r {
@@ -50,7 +51,6 @@ constexpr int kTcBlockN = 128;  // output features per CTA (MMA M)
 constexpr int kTcBlockK = 64;   // K per stage: 128 bytes of bf16, one swizzle row
 constexpr int kTcStages = 4;
 constexpr int kErrGemmWait = 4;                          // an mbarrier wait of the tensor-core GEMM timed out
-constexpr unsigned long long kTcWaitNs = 1000000000ull;  // 1 s
 
 constexpr int EPI_LOGITS = 5;  // tied-embedding logits + grammar mask + greedy argmax (+ commit)
 constexpr int kTcMaxSplits = 8;
@@ -64,43 +64,6 @@ struct TcArgs {
 
 __host__ __device__ constexpr size_t tc_smem_bytes(int nb) {
   return (size_t)kTcStages * (kTcBlockN + nb) * kTcBlockK * 2 + 1024;  // + slack for 1024-byte alignment
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint32_t addr, unsigned parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Wait until the phase with parity `parity` of an mbarrier has completed, for
-// at most kTcWaitNs.  Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-  const uint32_t addr = smem_u32(bar);
-  if (mbar_try(addr, parity)) return true;
-  const unsigned long long t0 = global_ns();
-  for (;;) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try(addr, parity)) return true;
-    if (global_ns() - t0 > kTcWaitNs) return false;
-  }
 }
 
 // 2-D tiled TMA load of the box at (x, y) into shared memory (x in elements, a
@@ -148,24 +111,30 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 16 consecutive fp32 columns of this thread's tensor-memory lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// 32 consecutive fp32 columns of this thread's tensor-memory lane; complete
+// after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Epilogue of one accumulator value for row m, feature n (both in range).
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Split cluster barrier: arrive (release) now, wait (acquire) later.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// Epilogue of one output (m, n) (both in range) given accumulator + bias.
 template <int EPI>
 __device__ __forceinline__ void tc_store(const TcArgs& t, int m, int n, float v) {
-  if constexpr (EPI != EPI_LOGITS) proj_epilogue<EPI>(t.p, m, n, v);
+  if constexpr (EPI != EPI_LOGITS) proj_epilogue_biased<EPI>(t.p, m, n, v);
 }
 
 // EPI_LOGITS: the logit of token n for row m (stored when requested) and its
@@ -205,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint32_t tmem_base;
   __shared__ int aborted, good, is_last;
   __shared__ uint32_t rule[EPI == EPI_LOGITS ? NB : 1];
+  __shared__ float sbias[kTcBlockN];  // bias of this CTA's features (weights: read before the wait)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, splits = gridDim.x, n_tile = blockIdx.y, m_tile = blockIdx.z;
@@ -214,6 +184,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int kt0 = split * t.k_tiles_per_split;
   const int nk = max(0, min(k_tiles, kt0 + t.k_tiles_per_split) - kt0);
 
+  if constexpr (EPI != EPI_LOGITS)
+    sbias[threadIdx.x] = n0 + (int)threadIdx.x < N ? __bfloat162float(t.p.bias[n0 + threadIdx.x]) : 0.f;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full[s], 1);
@@ -294,27 +266,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int f_own = warp * 32 + lane;  // the feature (tensor-memory lane) this thread reads
   const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+  const bool have = good && nk > 0;
   if (splits == 1) {
     // ---- the accumulator is the result: epilogue straight from tensor memory
     const int n = n0 + f_own;
 #pragma unroll 1
-    for (int c = 0; c < NB; c += 16) {
-      float v[16];
-      if (good && nk > 0) {
-        tmem_ld16(taddr + c, v);
+    for (int c = 0; c < NB; c += 32) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
       }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 32; ++j) {
         const int m = m0 + c + j;
+        const float v = __uint_as_float(r[j]);
         if constexpr (EPI == EPI_LOGITS) {
-          unsigned long long key = (m < M && n < N) ? tc_logit_key(t, rule[c + j], m, n, v[j]) : 0ull;
+          unsigned long long key = (m < M && n < N) ? tc_logit_key(t, rule[c + j], m, n, v) : 0ull;
           key = warp_max_u64(key);
           if (lane == 0 && key) atomicMax(t.lg.keys + m, key);
         } else {
-          if (m < M && n < N) tc_store<EPI>(t, m, n, v[j]);
+          if (m < M && n < N) tc_store<EPI>(t, m, n, v + sbias[f_own]);
         }
       }
     }
@@ -323,65 +298,81 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0)
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
   } else {
-    // ---- split-K over the cluster: partial tile to shared memory, then each
-    // CTA reduces its share of the rows across the cluster in slice order
+    // ---- split-K over the cluster: every CTA writes its partial tile to its
+    // own shared memory; after a cluster barrier CTA s adds rows
+    // [s*R, (s+1)*R), R = NB/S, of the S partials in slice order through
+    // distributed shared memory and runs the epilogue on them.
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
 #pragma unroll 1
-    for (int c = 0; c < NB; c += 16) {
-      float v[16];
-      if (good && nk > 0) {
-        tmem_ld16(taddr + c, v);
+    for (int c = 0; c < NB; c += 32) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
       }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part[(c + j) * kTcBlockN + f_own] = v[j];
+      for (int j = 0; j < 32; ++j) part[(c + j) * kTcBlockN + f_own] = __uint_as_float(r[j]);
     }
     tmem_fence_before();
     __syncthreads();
     if (warp == 0)
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
-    cluster.sync();  // every partial tile of the cluster is in shared memory
+    cluster_arrive();
+    cluster_wait();  // every partial tile of the cluster is in shared memory
     const int rows = NB / splits, r0 = split * rows;
-    const float* peer[kTcMaxSplits];
-#pragma unroll
-    for (int sp = 0; sp < kTcMaxSplits; ++sp) peer[sp] = sp < splits ? cluster.map_shared_rank(part, sp) : part;
     // 32 threads per row (4 features each): warp w takes rows r0 + w, r0 + w + 4, ...
-    for (int idx = threadIdx.x; idx < rows * (kTcBlockN / 4); idx += kTcThreads) {
-      const int r = r0 + idx / (kTcBlockN / 4), f = (idx % (kTcBlockN / 4)) * 4;
-      float4 acc = *reinterpret_cast<const float4*>(peer[0] + r * kTcBlockN + f);
+    constexpr int kMaxIters = NB / 2 * (kTcBlockN / 4) / kTcThreads;  // rows <= NB/2 with 2+ slices
+    float4 sums[kMaxIters];
 #pragma unroll
-      for (int sp = 1; sp < kTcMaxSplits; ++sp) {
-        if (sp < splits) {
-          const float4 x = *reinterpret_cast<const float4*>(peer[sp] + r * kTcBlockN + f);
-          acc.x += x.x;
-          acc.y += x.y;
-          acc.z += x.z;
-          acc.w += x.w;
-        }
-      }
-      const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-      const int m = m0 + r;
-      if constexpr (EPI == EPI_LOGITS) {
-        unsigned long long key = 0ull;
+    for (int it = 0; it < kMaxIters; ++it) {
+      const int idx = threadIdx.x + it * kTcThreads;
+      if (idx < rows * (kTcBlockN / 4)) {
+        const int r = r0 + idx / (kTcBlockN / 4), f = (idx % (kTcBlockN / 4)) * 4;
+        float4 acc = *reinterpret_cast<const float4*>(cluster.map_shared_rank(part, 0) + r * kTcBlockN + f);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (m < M && n0 + f + j < N) {
-            const unsigned long long kj = tc_logit_key(t, rule[r], m, n0 + f + j, a4[j]);
-            key = kj > key ? kj : key;
+        for (int sp = 1; sp < kTcMaxSplits; ++sp) {
+          if (sp < splits) {
+            const float4 x = *reinterpret_cast<const float4*>(cluster.map_shared_rank(part, sp) + r * kTcBlockN + f);
+            acc.x += x.x;
+            acc.y += x.y;
+            acc.z += x.z;
+            acc.w += x.w;
           }
         }
-        key = warp_max_u64(key);  // the warp covers the row's 128 features
-        if (lane == 0 && key) atomicMax(t.lg.keys + m, key);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (m < M && n0 + f + j < N) tc_store<EPI>(t, m, n0 + f + j, a4[j]);
+        sums[it] = acc;
       }
     }
-    cluster.sync();  // peers keep their shared memory until every CTA has read it
+    cluster_arrive();  // done reading the peers' shared memory; the epilogue overlaps the barrier
+#pragma unroll
+    for (int it = 0; it < kMaxIters; ++it) {
+      const int idx = threadIdx.x + it * kTcThreads;
+      if (idx < rows * (kTcBlockN / 4)) {
+        const int r = r0 + idx / (kTcBlockN / 4), f = (idx % (kTcBlockN / 4)) * 4;
+        const float a4[4] = {sums[it].x, sums[it].y, sums[it].z, sums[it].w};
+        const int m = m0 + r;
+        if constexpr (EPI == EPI_LOGITS) {
+          unsigned long long key = 0ull;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (m < M && n0 + f + j < N) {
+              const unsigned long long kj = tc_logit_key(t, rule[r], m, n0 + f + j, a4[j]);
+              key = kj > key ? kj : key;
+            }
+          }
+          key = warp_max_u64(key);  // the warp covers the row's 128 features
+          if (lane == 0 && key) atomicMax(t.lg.keys + m, key);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (m < M && n0 + f + j < N) tc_store<EPI>(t, m, n0 + f + j, a4[j] + sbias[f + j]);
+        }
+      }
+    }
+    cluster_wait();  // peers keep their shared memory until every CTA has read it
   }
 
   if constexpr (EPI == EPI_LOGITS) {

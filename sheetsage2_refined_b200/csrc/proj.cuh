@@ -77,9 +77,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 __device__ __forceinline__ float gelu_erf(float x) { return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f)); }
 
+// Epilogue of output (m, n) given v = accumulator + bias.
 template <int EPI>
-__device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, float acc) {
-  const float v = acc + __bfloat162float(a.bias[n]);
+__device__ __forceinline__ void proj_epilogue_biased(const ProjArgs& a, int m, int n, float v) {
   if constexpr (EPI == EPI_RESID) {
     a.r_out[(size_t)m * a.N + n] = a.x_res[(size_t)m * a.N + n] + round_bf16(v);
   } else if constexpr (EPI == EPI_BF16) {
@@ -107,6 +107,11 @@ __device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, f
     dst[(((size_t)a.cross_slot * a.heads + c / kHeadDim) * a.frames_cap + m) * kHeadDim + (c % kHeadDim)] =
         __float2bfloat16_rn(v);
   }
+}
+
+template <int EPI>
+__device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, float acc) {
+  proj_epilogue_biased<EPI>(a, m, n, acc + __bfloat162float(a.bias[n]));
 }
 
 // Normalise rows [m0, m0+mc) into xs (bfloat16, KP columns per row, zero
