@@ -69,8 +69,8 @@ typedef struct s2r_config {
 #define S2R_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
 #define S2R_FLAG_NO_GRAPH 2u /* issue steps as plain launches, no CUDA graph */
 #define S2R_FLAG_ONE_KERNEL_STEP 4u /* batch <= 8: run a step as one persistent kernel */
-#define S2R_FLAG_TRACE 8u          /* one-kernel step records clock64 marks per phase ("trace" buffer) */
-#define S2R_FLAG_NO_PREFETCH 16u   /* one-kernel step without next-phase L2 prefetches */
+#define S2R_FLAG_TRACE 8u          /* one-kernel step records globaltimer marks (ns) per phase ("trace" buffer) */
+#define S2R_FLAG_NO_PREFETCH 16u   /* accepted for compatibility; no effect */
 #define S2R_FLAG_NO_TENSOR_CORE 32u /* every projection on the CUDA-core kernel (by default the cross K/V
                                        projection at load, and with batch >= 16 the step and prefill
                                        projections, run on tcgen05 tensor cores) */
@@ -135,6 +135,43 @@ int32_t s2r_destroy(s2r_ctx* ctx);
  * applied after the bfloat16 logits are widened and before the grammar mask.
  * Replaces the `mode_bias` term (engine.py:77-80,316-317). */
 int32_t s2r_set_logit_bias(s2r_ctx* ctx, const float* bias);
+
+/* Frame-head rescoring terms, in the reference's FRAME_TERMS order
+ * (engine.py:29-38): root, bass, detail, quality, key, key_boundary,
+ * downbeat, meter. */
+#define S2R_FRAME_TERMS 8
+
+/* Frame-head rescoring configuration (engine.py:81-116): one weight per term
+ * (0 disables the term), the vocabulary spans [start, end) it moves, the
+ * meter tables and the vocabulary's time resolution.  Host pointers. */
+typedef struct s2r_rescore {
+  float weight[S2R_FRAME_TERMS];
+  int32_t bass_span[2];    /* chord_bass block */
+  int32_t detail_span[2];  /* chord_detail start, start + NO_CHORD */
+  int32_t key_span[2];     /* key block */
+  int32_t eighth_span[2];  /* eighth_position block */
+  int32_t meter_span[2];   /* meter block */
+  const int32_t* meter_beats; /* [meter block size] min(numerator, 16) - 1 of each meter */
+  const int32_t* meter_unit;  /* [meter block size] denominator of each meter */
+  int32_t time_hz;            /* time tokens per second of the vocabulary */
+} s2r_rescore;
+
+/* Enable frame-head rescoring with `rs` (NULL or all-zero weights: off).
+ * Needs the class grammar.  Allocates the per-slot frame tables (float32
+ * [batch][frames][width]: 12 root, 12 bass, NO_CHORD detail, NO_CHORD
+ * quality, 24 key, 1 key_boundary, 1 downbeat, 16 meter).  Synchronises the
+ * device.  Replaces the `frame_weight` argument of BatchDecoder
+ * (engine.py:81-116); the terms are added to the logits as engine.py:318-347
+ * does and the state they read advances as engine.py:358-369 does. */
+int32_t s2r_set_rescore(s2r_ctx* ctx, const s2r_rescore* rs);
+
+/* The window's per-frame tables of `slot` for frame-head rescoring
+ * (engine.py:218-224): tables[t] holds rows[t] rows of the term's width
+ * (float32, host or device; NULL or 0 rows: the term's table is zero); rows
+ * beyond the engine's frames are ignored.  Call before s2r_load_slot of the
+ * same window.  Replaces the `frame_logp` argument of BatchDecoder.load. */
+int32_t s2r_load_frame_tables(s2r_ctx* ctx, int32_t slot, const float* const* tables, const int32_t* rows,
+                              void* stream);
 
 /* Start `slot` on a window.  `memory` is the encoder memory
  * [memory_frames, width] (float32 or bfloat16); cross-attention sees its

@@ -1,9 +1,9 @@
 """The batched greedy decode engine restated in numpy (test infrastructure).
 
-``OracleEngine`` mirrors ``sheetsage2_refined/engine.py:52-369`` without the
-rescoring terms: construction (55-149), ``load`` (180-232), ``run`` (234-246),
-``finished`` (248-252), ``take`` (254-262) and the step ``_forward``
-(294-357).  ``step(forced=...)`` additionally lets a test force the
+``OracleEngine`` mirrors ``sheetsage2_refined/engine.py:52-369``:
+construction (55-149), ``load`` (180-232), ``run`` (234-246), ``finished``
+(248-252), ``take`` (254-262), the step ``_forward`` (294-357) and the
+frame-head rescoring terms and state (81-116, 218-232, 318-347, 358-369).  ``step(forced=...)`` additionally lets a test force the
 committed token per slot (teacher forcing) and returns the raw logits.
 
 The decoder forward is ``TokenDecoder`` (decoder.py:58-151) evaluated one
@@ -18,16 +18,21 @@ from __future__ import annotations
 import numpy as np
 
 from sheetsage2_refined_b200.grammar import ENDED
-from sheetsage2_refined_b200.vocab_table import EOS, OUT
+from sheetsage2_refined_b200.vocab_table import EOS, NO_CHORD, OUT, meter_tables
 from sheetsage2_refined_b200.weights import POSITION_OFFSET
 
 from .grammar import make_grammar_oracle
 from .numerics import bf16, gelu, layer_norm, softmax
 
 
+# FRAME_TERMS order (engine.py:29-38)
+FRAME_TERM_NAMES = ("root", "bass", "detail", "quality", "key", "key_boundary", "downbeat", "meter")
+AFTER_METER = 1  # incomplete-field state after a meter token (grammar.py, AFTER_METER)
+
+
 class OracleEngine:
     def __init__(self, config, state_dict: dict, grammar, *, batch: int, frames: int, mode: str = "bf16",
-                 logit_bias: np.ndarray | None = None):
+                 logit_bias: np.ndarray | None = None, frame_weight: tuple | None = None, vocab=None):
         if mode not in ("fp32", "bf16"):
             raise ValueError(mode)
         self.config, self.mode, self.batch, self.frames = config, mode, batch, frames
@@ -66,6 +71,27 @@ class OracleEngine:
         self.state["position"] = np.zeros(batch, np.int64)
         self.stop = np.full(batch, np.inf, np.float64)
         self.loaded = [False] * batch
+        # frame-head rescoring (engine.py:81-116): weights in FRAME_TERMS order
+        self.frame_weight = tuple(frame_weight) if frame_weight is not None else (0.0,) * 8
+        self.rescore = any(self.frame_weight)
+        if self.rescore:
+            sizes = {"root": 12, "bass": 12, "detail": NO_CHORD, "quality": NO_CHORD, "key": 24, "meter": 16}
+            self.frame = {name: np.zeros((batch, frames) + ((sizes[name],) if name in sizes else ()), np.float32)
+                          for name in FRAME_TERM_NAMES}
+            self.frame_now = np.zeros(batch, np.int64)
+            self.key_seen = np.zeros(batch, bool)
+            self.root_of_detail = np.arange(NO_CHORD) % 12
+            self.key_span = (vocab.start["key"], vocab.end["key"])
+            self.eighth_span = (vocab.start["eighth_position"], vocab.end["eighth_position"])
+            self.meter_span = (vocab.start["meter"], vocab.end["meter"])
+            beats, units = meter_tables()
+            self.meter_beats, self.meter_unit = np.array(beats), np.array(units)
+            self.active_meter = np.full(batch, -1, np.int64)
+            self.meter_changed = np.zeros(batch, bool)
+            self.meter_index = np.arange(len(beats))
+            self.time_hz = vocab.time_hz
+            self.bass_span = (vocab.start["chord_bass"], vocab.end["chord_bass"])
+            self.detail_span = (vocab.start["chord_detail"], vocab.start["chord_detail"] + NO_CHORD)
 
     # ------------------------------------------------------------ numerics
     def _linear(self, layer: int, name: str, x: np.ndarray) -> np.ndarray:
@@ -112,8 +138,8 @@ class OracleEngine:
         return [s for s in range(self.batch) if not self.loaded[s]]
 
     def load(self, slot: int, memory, prefix: list[int], stop_seconds, frames: int | None = None,
-             target: int | None = None) -> None:
-        """engine.py:180-232 (without the rescoring tables); ``target`` feeds the table grammar."""
+             target: int | None = None, frame_logp: dict | None = None) -> None:
+        """engine.py:180-232; ``target`` feeds the table grammar."""
 
         memory = np.asarray(memory, np.float32).reshape(-1, self.config.width)
         frames = self.frames if frames is None else frames
@@ -139,6 +165,72 @@ class OracleEngine:
         self.state["position"][slot] = n - 1
         self.stop[slot] = np.inf if stop_seconds is None else stop_seconds
         self.loaded[slot] = True
+        if self.rescore:  # engine.py:218-232
+            frame_logp = frame_logp or {}
+            for name, table in self.frame.items():
+                table[slot] = 0.0
+                if name in frame_logp:
+                    count = min(len(frame_logp[name]), self.frames)
+                    table[slot, :count] = np.asarray(frame_logp[name], np.float32)[:count]
+            seconds = self.grammar.time_seconds
+            times = [float(seconds[t]) for t in prefix if seconds[t] > float("-inf")]
+            self.frame_now[slot] = (min(int(times[-1] * self.time_hz) * 25 // self.time_hz, self.frames - 1)
+                                    if times else 0)
+            self.key_seen[slot] = any(self.key_span[0] <= t < self.key_span[1] for t in prefix)
+            m0, m1 = self.meter_span
+            meters = [t - m0 for t in prefix if m0 <= t < m1]
+            self.active_meter[slot] = meters[-1] if meters else -1
+            self.meter_changed[slot] = False
+
+    def _rescore_logits(self, logits: np.ndarray) -> None:
+        """engine.py:318-347 in place: the frame-head terms of every row."""
+
+        st, rows = self.state, np.arange(self.batch)
+        (b0, b1), (d0, d1), (k0, k1) = self.bass_span, self.detail_span, self.key_span
+        w, now, frame = dict(zip(FRAME_TERM_NAMES, self.frame_weight)), self.frame_now, self.frame
+        if w["root"]:
+            logits[:, d0:d1] += w["root"] * frame["root"][rows, now][:, self.root_of_detail]
+        if w["detail"]:
+            logits[:, d0:d1] += w["detail"] * frame["detail"][rows, now]
+        if w["quality"]:
+            logits[:, d0:d1] += w["quality"] * frame["quality"][rows, now]
+        if w["bass"]:
+            logits[:, b0:b1] += w["bass"] * frame["bass"][rows, now]
+        if w["key"]:
+            logits[:, k0:k1] += w["key"] * frame["key"][rows, now]
+        if w["key_boundary"]:
+            stated = self.key_seen.astype(np.float32)
+            logits[:, k0:k1] += (w["key_boundary"] * frame["key_boundary"][rows, now] * stated)[:, None]
+        if w["downbeat"]:
+            logits[:, self.eighth_span[0]] += w["downbeat"] * frame["downbeat"][rows, now]
+        if w["meter"]:
+            (m0, m1), (e0, e1) = self.meter_span, self.eighth_span
+            table = frame["meter"][rows, now]
+            active = np.maximum(self.active_meter, 0)
+            change = (self.active_meter >= 0)[:, None] & (self.meter_index[None] != active[:, None])
+            current = np.take_along_axis(table, self.meter_beats[active][:, None], axis=1)
+            same_unit = self.meter_unit[None] == self.meter_unit[active][:, None]
+            logits[:, m0:m1] += w["meter"] * (table[:, self.meter_beats] - current) * (change & same_unit)
+            if w["downbeat"]:
+                logits[:, m0:m1] += w["downbeat"] * frame["downbeat"][rows, now][:, None] * change
+            after = (st["incomplete"] == AFTER_METER) & self.meter_changed
+            logits[:, e0 + 1: e1][after] = -np.inf
+
+    def _rescore_commit(self, choice: np.ndarray, active: np.ndarray) -> None:
+        """engine.py:358-369: the rescoring state after the step's tokens."""
+
+        seconds = self.grammar.time_seconds[choice]
+        with np.errstate(invalid="ignore"):
+            frame = np.clip(np.where(np.isfinite(seconds), seconds * 25, 0).astype(np.int64), 0, self.frames - 1)
+        self.frame_now[:] = np.where(active & (seconds > float("-inf")), frame, self.frame_now)
+        k0, k1 = self.key_span
+        self.key_seen |= active & (choice >= k0) & (choice < k1)
+        m0, m1 = self.meter_span
+        is_meter = active & (choice >= m0) & (choice < m1)
+        meter = np.clip(choice - m0, 0, m1 - m0 - 1)
+        changed = (self.active_meter >= 0) & (meter != self.active_meter)
+        self.meter_changed[:] = np.where(is_meter, changed, self.meter_changed)
+        self.active_meter[:] = np.where(is_meter, meter, self.active_meter)
 
     def step(self, forced: np.ndarray | None = None):
         """One step (engine.py:294-357). Returns ``(raw logits [B, V], greedy choice [B])``.
@@ -154,7 +246,9 @@ class OracleEngine:
         for slot in np.nonzero(active)[0]:
             x = self._row_forward(int(slot), int(token[slot]), int(position[slot]))
             logits[slot] = self._logits(x)
-        biased = logits if self.logit_bias is None else logits + self.logit_bias
+        biased = logits.copy() if self.logit_bias is None else logits + self.logit_bias
+        if self.rescore:
+            self._rescore_logits(biased)
         masked = np.where(self.grammar.allowed(st), biased, -np.inf)
         greedy = masked.argmax(axis=-1)
         choice = greedy.copy()
@@ -165,6 +259,8 @@ class OracleEngine:
         rows = np.arange(self.batch)
         self.out[rows, new_position] = np.where(active, choice, self.out[rows, new_position])
         self.grammar.update(st, choice, active, self.stop, new_position >= self.max_tokens - 1)
+        if self.rescore:
+            self._rescore_commit(choice, active)
         token[...] = choice
         position[...] = new_position
         return logits, greedy

@@ -62,6 +62,23 @@ class GrammarDesc(C.Structure):
     ]
 
 
+FRAME_TERM_COUNT = 8
+
+
+class Rescore(C.Structure):
+    _fields_ = [
+        ("weight", C.c_float * FRAME_TERM_COUNT),
+        ("bass_span", C.c_int32 * 2),
+        ("detail_span", C.c_int32 * 2),
+        ("key_span", C.c_int32 * 2),
+        ("eighth_span", C.c_int32 * 2),
+        ("meter_span", C.c_int32 * 2),
+        ("meter_beats", C.c_void_p),
+        ("meter_unit", C.c_void_p),
+        ("time_hz", C.c_int32),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/s2r.h declares.
 SIGNATURES = {
     "s2r_abi_version": (C.c_int32, []),
@@ -70,6 +87,8 @@ SIGNATURES = {
                                C.POINTER(C.c_void_p)]),
     "s2r_destroy": (C.c_int32, [C.c_void_p]),
     "s2r_set_logit_bias": (C.c_int32, [C.c_void_p, C.c_void_p]),
+    "s2r_set_rescore": (C.c_int32, [C.c_void_p, C.POINTER(Rescore)]),
+    "s2r_load_frame_tables": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     "s2r_load_slot": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                   C.POINTER(C.c_int64), C.c_int32, C.c_double, C.c_int64, C.c_void_p]),
     "s2r_step": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p]),

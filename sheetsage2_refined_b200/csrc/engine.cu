@@ -99,7 +99,7 @@ struct LayerBufs {
   bf16 *wqkv, *bqkv, *wo, *bo, *wcq, *bcq, *wckv, *bckv, *wco, *bco, *w1, *b1, *w2, *b2;
   float *ln_self_g, *ln_self_b, *ln_cross_g, *ln_cross_b, *ln_final_g, *ln_final_b;
   bf16 *kpool, *vpool, *ck, *cv;
-  bf16 *woT, *wcoT, *w2T;  // transposed copies for the persistent step kernel
+  bf16 *wo_hb, *wco_hb;  // out-projections by head for the persistent step kernel
 };
 
 struct s2r_ctx {
@@ -129,6 +129,8 @@ struct s2r_ctx {
   int64_t* dbg_greedy = nullptr;
   SlotState st{};
   Grammar gr{};
+  Rescore rs{};  // frame-head rescoring (device tables and state)
+  int rs_time_hz = 100;
   // host copies for prefix replay
   std::vector<int8_t> h_token_class;
   std::vector<int32_t> h_field;
@@ -144,9 +146,9 @@ struct s2r_ctx {
   cudaStream_t cap_stream = nullptr;
   // persistent step kernel (live rows <= 8)
   bool persistent = false;
-  int nclusters = 0, units = 0, chunk_cap = 0;
+  int nclusters = 0, chunk_cap = 0, stages = 0;
   PLayer* d_layers = nullptr;
-  float *part_o = nullptr, *part_c = nullptr, *part_f = nullptr;
+  float *part_o = nullptr, *part_c = nullptr;
   unsigned* bar = nullptr;
   long long* trace = nullptr;  // S2R_FLAG_TRACE: clock64 marks of the persistent step
   // tensor-core projections (tcgen05 GEMM): the step and prefill projections
@@ -199,24 +201,20 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restri
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-// out[j][i] = in[i][j] for a [rows, cols] bf16 matrix.
-__global__ void transpose_bf16_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int rows, int cols) {
-  __shared__ bf16 tile[32][33];
-  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int r = r0 + k, col = c0 + threadIdx.x;
-    if (r < rows && col < cols) tile[k][threadIdx.x] = in[(size_t)r * cols + col];
-  }
-  __syncthreads();
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int col = c0 + k, r = r0 + threadIdx.x;
-    if (r < rows && col < cols) out[(size_t)col * rows + r] = tile[threadIdx.x][k];
+// out[h][n][d] = in[n][64h + d] for a [D, D] bf16 matrix (an out-projection
+// regrouped so that head h's inputs of every output feature are contiguous).
+__global__ void head_block_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int D) {
+  const size_t n_total = (size_t)D * D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_total; i += (size_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % kHeadDim);
+    const size_t rest = i / kHeadDim;
+    const int n = (int)(rest % D), h = (int)(rest / D);
+    out[i] = in[(size_t)n * D + h * kHeadDim + d];
   }
 }
 
-int transpose_bf16(const bf16* in, bf16* out, int rows, int cols) {
-  dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
-  transpose_bf16_kernel<<<grid, block>>>(in, out, rows, cols);
+int head_block_bf16(const bf16* in, bf16* out, int D) {
+  head_block_kernel<<<1024, 256>>>(in, out, D);
   CK(cudaGetLastError());
   return S2R_OK;
 }
@@ -521,14 +519,14 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   return S2R_OK;
 }
 
-size_t persistent_smem(const s2r_ctx* c, int mr) {
-  auto r = [](size_t b) { return (b + 15) & ~size_t(15); };
-  const size_t D = c->D, KP = (size_t)kch_for(c->D) * 256;
-  size_t bytes = r(4 * mr * D) + r(2 * mr * KP) + r(4 * mr * D) + r(4 * (size_t)mr * c->chunk_cap) +
-                 3 * r(4 * mr * kHeadDim) + r(4 * mr * kQkvLocal) + r(4 * mr * kHeadDim) + r(4 * mr * 2) +
-                 r(4 * mr * kDimsLocal) + r(4 * (size_t)mr * c->units) + r(4 * kPWarps * kHeadDim);
-  // at least 116 KB so that one CTA holds its SM (two would not fit the 228 KB)
-  return std::max<size_t>(bytes, 116 * 1024);
+// Dynamic shared memory of the persistent kernel for mr rows (the ring not
+// included): it mirrors the carve-up at the top of step_persistent_kernel.
+size_t persistent_smem_fixed(const s2r_ctx* c, int mr) {
+  auto r = [](size_t b) { return (b + 127) & ~size_t(127); };
+  const size_t D = c->D, KP = (size_t)kch_for(c->D) * 256, FP = (size_t)(c->FFN + 255) / 256 * 256;
+  return r(4 * mr * D) + r(2 * mr * KP) + r(std::max(4 * (size_t)mr * c->chunk_cap, 2 * (size_t)mr * FP)) +
+         2 * r(4 * mr * kHeadDim) + r(4 * 2 * kPClus * mr * 2) + r(4 * 2 * kPClus * mr * kHeadDim) +
+         r(4 * kPWarps * kHeadDim);
 }
 
 int launch_persistent(s2r_ctx* c, RowMap rm, int M, bool logits, const int64_t* forced, float* logits_out,
@@ -546,8 +544,8 @@ int launch_persistent(s2r_ctx* c, RowMap rm, int M, bool logits, const int64_t* 
   a.T = c->T;
   a.F = c->F;
   a.pps = c->pps;
-  a.units = c->units;
   a.chunk_cap = c->chunk_cap;
+  a.stages = c->stages;
   a.logits = logits ? 1 : 0;
   a.layers = c->d_layers;
   a.tok_emb = c->tok_emb;
@@ -558,7 +556,9 @@ int launch_persistent(s2r_ctx* c, RowMap rm, int M, bool logits, const int64_t* 
   a.bias = c->has_bias ? c->bias : nullptr;
   a.part_o = c->part_o;
   a.part_c = c->part_c;
-  a.part_f = c->part_f;
+  a.r = c->r;
+  a.q = c->q;
+  a.hid = c->hid;
   a.bar = c->bar;
   a.keys = c->keys;
   a.counter = c->counter;
@@ -567,25 +567,28 @@ int launch_persistent(s2r_ctx* c, RowMap rm, int M, bool logits, const int64_t* 
   a.logits_out = logits_out;
   a.greedy_out = greedy_out;
   a.trace = c->trace;
-  a.prefetch = (c->cfg.flags & S2R_FLAG_NO_PREFETCH) ? 0 : 1;
+  a.rs = c->rs;
   const int mr = mc_for(M);
   StepFn fn = step_fn(kch_for(c->D), mr);
-  const size_t smem = persistent_smem(c, mr);
+  const size_t smem = persistent_smem_fixed(c, mr) + (size_t)c->stages * kPStage;
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CK(launch_ex(fn, dim3(c->nclusters * kPClus), dim3(kPThreads), smem, s, false, kPClus, a));
   return S2R_OK;
 }
 
-// Decide whether the persistent kernel can run: rows <= 8, width <= 1024 and
-// at least one cluster of 8 CTAs resident.  Sets nclusters / units / chunk_cap.
+// Decide whether the persistent kernel can run: rows <= 8, width <= 1024, a ring of at least 3 stages next to the kernel's other
+// shared memory, and at least one cluster of 4 CTAs resident.  Sets
+// nclusters, chunk_cap and stages.
 int setup_persistent(s2r_ctx* c) {
   c->persistent = false;
-  if (!(c->cfg.flags & S2R_FLAG_ONE_KERNEL_STEP) || c->B > kPMaxRows || c->D > 1024 || c->D % 16) return S2R_OK;
+  if (!(c->cfg.flags & S2R_FLAG_ONE_KERNEL_STEP) || c->B > kPMaxRows || c->D > 1024) return S2R_OK;
   c->chunk_cap = std::max((c->T + kPClus - 1) / kPClus, (c->F + kPClus - 1) / kPClus);
-  c->units = 64;  // upper bound for the occupancy query
+  const size_t fixed = persistent_smem_fixed(c, 8);
+  const size_t budget = 227 * 1024 - 2048;  // less the kernel's static shared memory
+  if (fixed + 3 * (size_t)kPStage > budget) return S2R_OK;
+  c->stages = (int)std::min<size_t>(kPMaxStages, (budget - fixed) / kPStage);
   StepFn fn = step_fn(kch_for(c->D), 8);
-  const size_t smem = persistent_smem(c, 8);
-  if (smem > 227 * 1024) return S2R_OK;
+  const size_t smem = fixed + (size_t)c->stages * kPStage;
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kPClus * 64);
@@ -602,9 +605,6 @@ int setup_persistent(s2r_ctx* c) {
   CK(cudaOccupancyMaxActiveClusters(&n, fn, &cfg));
   if (n < 1) return S2R_OK;
   c->nclusters = std::min(n, 64);
-  const int G = c->nclusters * kPClus;
-  c->units = (c->FFN + G - 1) / G;
-  if (c->units > 64) return S2R_OK;
   c->persistent = true;
   return S2R_OK;
 }
@@ -635,6 +635,7 @@ int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logit
   a.forced = forced;
   a.logits_out = logits;
   a.greedy_out = greedy;
+  a.rs = c->rs;
   if (c->tc) {
     ProjArgs p = proj_base(c);
     p.rm = rm;
@@ -917,15 +918,13 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     std::vector<PLayer> pl(c->L);
     for (int l = 0; l < c->L; ++l) {
       LayerBufs& b = c->layers[l];
-      TRYC(dalloc(c, &b.woT, D * D));
-      TRYC(dalloc(c, &b.wcoT, D * D));
-      TRYC(dalloc(c, &b.w2T, FFN * D));
-      TRYC(transpose_bf16(b.wo, b.woT, (int)D, (int)D));
-      TRYC(transpose_bf16(b.wco, b.wcoT, (int)D, (int)D));
-      TRYC(transpose_bf16(b.w2, b.w2T, (int)D, (int)FFN));
+      TRYC(dalloc(c, &b.wo_hb, D * D));
+      TRYC(dalloc(c, &b.wco_hb, D * D));
+      TRYC(head_block_bf16(b.wo, b.wo_hb, (int)D));
+      TRYC(head_block_bf16(b.wco, b.wco_hb, (int)D));
       PLayer& p = pl[l];
-      p.wqkv = b.wqkv; p.bqkv = b.bqkv; p.woT = b.woT; p.bo = b.bo; p.wcq = b.wcq; p.bcq = b.bcq;
-      p.wcoT = b.wcoT; p.bco = b.bco; p.w1 = b.w1; p.b1 = b.b1; p.w2T = b.w2T; p.b2 = b.b2;
+      p.wqkv = b.wqkv; p.bqkv = b.bqkv; p.wo_hb = b.wo_hb; p.bo = b.bo; p.wcq = b.wcq; p.bcq = b.bcq;
+      p.wco_hb = b.wco_hb; p.bco = b.bco; p.w1 = b.w1; p.b1 = b.b1; p.w2 = b.w2; p.b2 = b.b2;
       p.ln_self_g = b.ln_self_g; p.ln_self_b = b.ln_self_b; p.ln_cross_g = b.ln_cross_g;
       p.ln_cross_b = b.ln_cross_b; p.ln_final_g = b.ln_final_g; p.ln_final_b = b.ln_final_b;
       p.kpool = b.kpool; p.vpool = b.vpool; p.ck = b.ck; p.cv = b.cv;
@@ -934,7 +933,6 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     CK(cudaMemcpy(c->d_layers, pl.data(), c->L * sizeof(PLayer), cudaMemcpyHostToDevice));
     TRYC(dalloc(c, &c->part_o, (size_t)c->H * kPMaxRows * D));
     TRYC(dalloc(c, &c->part_c, (size_t)c->H * kPMaxRows * D));
-    TRYC(dalloc(c, &c->part_f, (size_t)c->nclusters * kPMaxRows * D));
     TRYC(dalloc(c, &c->bar, 2));
     CK(cudaMemset(c->bar, 0, 2 * sizeof(unsigned)));
     if (c->cfg.flags & S2R_FLAG_TRACE) {
@@ -1080,6 +1078,84 @@ int32_t s2r_set_logit_bias(s2r_ctx* c, const float* bias) {
   return S2R_OK;
 }
 
+int32_t s2r_set_rescore(s2r_ctx* c, const s2r_rescore* in) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  CK(cudaSetDevice(c->device));
+  CK(cudaDeviceSynchronize());
+  bool on = false;
+  if (in)
+    for (int t = 0; t < S2R_FRAME_TERMS; ++t) on = on || in->weight[t] != 0.f;
+  c->graph_dirty = true;
+  if (!on) {
+    c->rs.on = 0;
+    return S2R_OK;
+  }
+  if (c->gr.kind != S2R_GRAMMAR_CLASS) return fail(S2R_ENOTSUP, "frame-head rescoring needs the class grammar");
+  const int32_t* spans[5] = {in->bass_span, in->detail_span, in->key_span, in->eighth_span, in->meter_span};
+  for (const int32_t* sp : spans)
+    if (sp[0] < 0 || sp[1] <= sp[0] || sp[1] > c->V) return fail(S2R_EINVAL, "rescoring span [%d, %d) outside the vocabulary", sp[0], sp[1]);
+  if (in->bass_span[1] - in->bass_span[0] != 12 || in->key_span[1] - in->key_span[0] != 24)
+    return fail(S2R_EINVAL, "rescoring: the bass span must hold 12 tokens and the key span 24");
+  if (!in->meter_beats || !in->meter_unit || in->time_hz <= 0) return fail(S2R_EINVAL, "rescoring: meter tables and time_hz needed");
+  const int n_meters = in->meter_span[1] - in->meter_span[0];
+  for (int i = 0; i < n_meters; ++i)
+    if (in->meter_beats[i] < 0 || in->meter_beats[i] > 15) return fail(S2R_EINVAL, "meter_beats[%d] = %d not in [0, 15]", i, in->meter_beats[i]);
+  Rescore& r = c->rs;
+  const int no_chord = in->detail_span[1] - in->detail_span[0];
+  if (r.frame_now && no_chord != r.d1 - r.d0) return fail(S2R_EINVAL, "rescoring: the detail span width cannot change");
+  if (!r.frame_now) {  // first call: tables and state
+    for (int t = 0; t < FT_COUNT; ++t) {
+      float* tab = nullptr;
+      const size_t n = (size_t)c->B * c->F * frame_term_width(t, no_chord);
+      TRY(dalloc(c, &tab, n));
+      CK(cudaMemset(tab, 0, n * sizeof(float)));
+      r.table[t] = tab;
+    }
+    int32_t *beats = nullptr, *unit = nullptr;
+    TRY(dalloc(c, &beats, n_meters));
+    TRY(dalloc(c, &unit, n_meters));
+    r.meter_beats = beats;
+    r.meter_unit = unit;
+    TRY(dalloc(c, &r.frame_now, c->B));
+    TRY(dalloc(c, &r.key_seen, c->B));
+    TRY(dalloc(c, &r.active_meter, c->B));
+    TRY(dalloc(c, &r.meter_changed, c->B));
+    CK(cudaMemset(r.frame_now, 0, c->B * sizeof(int32_t)));
+    CK(cudaMemset(r.key_seen, 0, c->B));
+    CK(cudaMemset(r.active_meter, 0xff, c->B * sizeof(int32_t)));  // -1: no meter stated
+    CK(cudaMemset(r.meter_changed, 0, c->B));
+  }
+  CK(cudaMemcpy(const_cast<int32_t*>(r.meter_beats), in->meter_beats, n_meters * sizeof(int32_t), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(const_cast<int32_t*>(r.meter_unit), in->meter_unit, n_meters * sizeof(int32_t), cudaMemcpyHostToDevice));
+  for (int t = 0; t < FT_COUNT; ++t) r.w[t] = in->weight[t];
+  r.b0 = in->bass_span[0], r.b1 = in->bass_span[1];
+  r.d0 = in->detail_span[0], r.d1 = in->detail_span[1];
+  r.k0 = in->key_span[0], r.k1 = in->key_span[1];
+  r.e0 = in->eighth_span[0], r.e1 = in->eighth_span[1];
+  r.m0 = in->meter_span[0], r.m1 = in->meter_span[1];
+  r.frames = c->F;
+  c->rs_time_hz = in->time_hz;
+  r.on = 1;
+  return S2R_OK;
+}
+
+int32_t s2r_load_frame_tables(s2r_ctx* c, int32_t slot, const float* const* tables, const int32_t* rows, void* stream) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  if (!c->rs.on) return fail(S2R_ESTATE, "frame-head rescoring is not enabled (s2r_set_rescore)");
+  if (slot < 0 || slot >= c->B) return fail(S2R_EINVAL, "slot %d out of range [0, %d)", slot, c->B);
+  CK(cudaSetDevice(c->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int no_chord = c->rs.d1 - c->rs.d0;
+  for (int t = 0; t < FT_COUNT; ++t) {
+    const size_t width = frame_term_width(t, no_chord);
+    float* dst = const_cast<float*>(c->rs.table[t]) + (size_t)slot * c->F * width;
+    CK(cudaMemsetAsync(dst, 0, (size_t)c->F * width * sizeof(float), s));
+    const int n = (tables && rows && tables[t]) ? std::min<int>(std::max(rows[t], 0), c->F) : 0;
+    if (n > 0) CK(cudaMemcpyAsync(dst, tables[t], (size_t)n * width * sizeof(float), cudaMemcpyDefault, s));
+  }
+  return S2R_OK;
+}
+
 int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memory_dtype, int32_t memory_frames,
                       int32_t frames, const int64_t* prefix, int32_t n_prefix, double stop_seconds, int64_t target,
                       void* stream) {
@@ -1133,6 +1209,25 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
   TRY(put<int64_t>(st.position, slot, (int64_t)n_prefix - 1, s));
   CK(cudaMemcpyAsync(st.out + (size_t)slot * c->T, prefix, n_prefix * sizeof(int64_t), cudaMemcpyDefault, s));
 
+  if (c->rs.on) {  // rescoring state after the prefix (engine.py:225-232)
+    const Rescore& r = c->rs;
+    int32_t frame_now = 0, active = -1;
+    uint8_t key_seen = 0;
+    for (int i = 0; i < n_prefix; ++i) {
+      const int64_t t = prefix[i];
+      const double sec = c->h_time[(size_t)t];
+      if (sec > -INFINITY) {
+        const long long f = (long long)(sec * c->rs_time_hz) * 25 / c->rs_time_hz;
+        frame_now = (int32_t)std::min<long long>(f, c->F - 1);
+      }
+      if (t >= r.k0 && t < r.k1) key_seen = 1;
+      if (t >= r.m0 && t < r.m1) active = (int32_t)(t - r.m0);
+    }
+    TRY(put<int32_t>(r.frame_now, slot, frame_now, s));
+    TRY(put<uint8_t>(r.key_seen, slot, key_seen, s));
+    TRY(put<int32_t>(r.active_meter, slot, active, s));
+    TRY(put<uint8_t>(r.meter_changed, slot, (uint8_t)0, s));
+  }
   // cross K/V of the window (decoder.py:98-116), written straight into the slot
   const size_t elem = memory_dtype == S2R_F32 ? 4 : 2;
   CK(cudaMemcpyAsync(c->mem_stage, memory, (size_t)frames * D * elem, cudaMemcpyDefault, s));

@@ -143,7 +143,7 @@ __device__ __forceinline__ unsigned long long tc_logit_key(const TcArgs& t, uint
   const float logit = round_bf16(v);
   if (t.lg.logits_out) t.lg.logits_out[(size_t)m * t.lg.V + n] = logit;
   if (!token_allowed(t.lg.gr, rule, t.lg.V, n)) return 0ull;
-  return argmax_key(logit + (t.lg.bias ? t.lg.bias[n] : 0.f), n);
+  return argmax_key(rescore_logit(t.lg.rs, t.lg.st, m, n, logit + (t.lg.bias ? t.lg.bias[n] : 0.f)), n);
 }
 
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {

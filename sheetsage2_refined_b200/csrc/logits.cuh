@@ -32,6 +32,27 @@ struct Grammar {
   const uint8_t* table;
 };
 
+// Frame-head rescoring (engine.py:81-116,318-347,358-369): additive terms
+// from per-slot per-frame tables, looked up at the slot's current frame, on
+// the chord detail, bass, key, eighth-position and meter spans, and the state
+// they read (current frame, key stated, active meter, last meter a change).
+// Weights in the reference's FRAME_TERMS order.
+enum FrameTerm { FT_ROOT = 0, FT_BASS, FT_DETAIL, FT_QUALITY, FT_KEY, FT_KEY_BOUNDARY, FT_DOWNBEAT, FT_METER, FT_COUNT };
+
+struct Rescore {
+  int on;
+  float w[FT_COUNT];
+  int b0, b1, d0, d1, k0, k1, e0, e1, m0, m1;  // bass, detail, key, eighth-position and meter spans
+  int frames;                                  // table rows per slot
+  const float* table[FT_COUNT];                // [slots][frames][width of the term]
+  const int32_t* meter_beats;                  // [meters] min(numerator, 16) - 1
+  const int32_t* meter_unit;                   // [meters] denominator
+  int32_t* frame_now;                          // [slots]
+  uint8_t* key_seen;                           // [slots]
+  int32_t* active_meter;                       // [slots], -1 none
+  uint8_t* meter_changed;                      // [slots]
+};
+
 struct LogitsArgs {
   int M, V, D, max_tokens;
   SlotState st;
@@ -46,6 +67,7 @@ struct LogitsArgs {
   const int64_t* forced;     // [M] or null: commit forced[m] >= 0 instead of the greedy token
   float* logits_out;         // [M, V] or null: raw logits
   int64_t* greedy_out;       // [M] or null
+  Rescore rs;                // frame-head rescoring (rs.on == 0: none)
 };
 
 // Class grammar constants (grammar.py:19-55).
@@ -126,14 +148,80 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
 }
 
+__host__ __device__ constexpr int frame_term_width(int term, int no_chord) {
+  return term == FT_ROOT || term == FT_BASS ? 12
+         : term == FT_DETAIL || term == FT_QUALITY ? no_chord
+         : term == FT_KEY ? 24
+         : term == FT_METER ? 16
+                            : 1;
+}
+
+// x = logit + mode bias of token v for slot s, plus the rescoring terms in
+// the reference's order (engine.py:318-347); -inf for the eighth positions
+// after a meter change.  Terms with a zero weight are not added at all.
+__device__ __forceinline__ float rescore_logit(const Rescore& r, const SlotState& st, int s, int v, float x) {
+  if (!r.on) return x;
+  const int now = r.frame_now[s];
+  auto row = [&](int term) {
+    return r.table[term] + ((size_t)s * r.frames + now) * frame_term_width(term, r.d1 - r.d0);
+  };
+  if (v >= r.d0 && v < r.d1) {
+    const int i = v - r.d0;
+    if (r.w[FT_ROOT] != 0.f) x += r.w[FT_ROOT] * row(FT_ROOT)[i % 12];
+    if (r.w[FT_DETAIL] != 0.f) x += r.w[FT_DETAIL] * row(FT_DETAIL)[i];
+    if (r.w[FT_QUALITY] != 0.f) x += r.w[FT_QUALITY] * row(FT_QUALITY)[i];
+  }
+  if (v >= r.b0 && v < r.b1 && r.w[FT_BASS] != 0.f) x += r.w[FT_BASS] * row(FT_BASS)[v - r.b0];
+  if (v >= r.k0 && v < r.k1) {
+    if (r.w[FT_KEY] != 0.f) x += r.w[FT_KEY] * row(FT_KEY)[v - r.k0];
+    if (r.w[FT_KEY_BOUNDARY] != 0.f)
+      x += r.w[FT_KEY_BOUNDARY] * row(FT_KEY_BOUNDARY)[0] * (r.key_seen[s] ? 1.f : 0.f);
+  }
+  if (v == r.e0 && r.w[FT_DOWNBEAT] != 0.f) x += r.w[FT_DOWNBEAT] * row(FT_DOWNBEAT)[0];
+  if (r.w[FT_METER] != 0.f) {
+    if (v >= r.m0 && v < r.m1) {
+      const int m = v - r.m0, act = r.active_meter[s], a = act < 0 ? 0 : act;
+      const bool change = act >= 0 && m != a;
+      const bool same_unit = r.meter_unit[m] == r.meter_unit[a];
+      const float* t = row(FT_METER);
+      x += r.w[FT_METER] * (t[r.meter_beats[m]] - t[r.meter_beats[a]]) * ((change && same_unit) ? 1.f : 0.f);
+      if (r.w[FT_DOWNBEAT] != 0.f) x += r.w[FT_DOWNBEAT] * row(FT_DOWNBEAT)[0] * (change ? 1.f : 0.f);
+    }
+    if (v > r.e0 && v < r.e1 && st.incomplete[s] == kAfterMeter && r.meter_changed[s]) x = -INFINITY;
+  }
+  return x;
+}
+
+// Rescoring state after slot s committed `tok` (engine.py:358-369).
+__device__ __forceinline__ void rescore_commit(const Rescore& r, const Grammar& gr, int s, int64_t tok, bool active) {
+  if (!r.on || !active) return;
+  const double seconds = gr.time_seconds[tok];
+  if (seconds > -INFINITY) {
+    long long f = (long long)(seconds * 25.0);
+    f = f < 0 ? 0 : (f > r.frames - 1 ? r.frames - 1 : f);
+    r.frame_now[s] = (int32_t)f;
+  }
+  if (tok >= r.k0 && tok < r.k1) r.key_seen[s] = 1;
+  if (tok >= r.m0 && tok < r.m1) {
+    const int m = (int)(tok - r.m0);
+    r.meter_changed[s] = r.active_meter[s] >= 0 && m != r.active_meter[s];
+    r.active_meter[s] = m;
+  }
+}
+
+// torch.argmax over a row whose best value is -inf (every token masked or
+// pushed to -inf) returns index 0; otherwise the key's token.
+__device__ __forceinline__ int64_t key_token(unsigned long long k) {
+  return (k >> 32) > 0x007fffffull ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
+}
+
 // Commit one step for rows [0, M) once every key is final: the greedy token
 // (or the forced one) is written to out[slot, position+1], the grammar
 // advances and the keys return to zero.  Run by one CTA.
 __device__ __forceinline__ void commit_rows(const LogitsArgs& a) {
   for (int s = threadIdx.x; s < a.M; s += blockDim.x) {
     const unsigned long long k = atomicExch(a.keys + s, 0ull);
-    // all tokens masked: torch.argmax over a row of -inf returns index 0
-    const int64_t greedy = k ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
+    const int64_t greedy = key_token(k);
     if (a.greedy_out) a.greedy_out[s] = greedy;
     const bool active = a.st.finished[s] == 0;
     const int64_t tok = a.st.token[s], pos = a.st.position[s];
@@ -143,6 +231,7 @@ __device__ __forceinline__ void commit_rows(const LogitsArgs& a) {
     const int64_t new_pos = active ? pos + 1 : pos;
     if (active && new_pos < a.max_tokens) a.st.out[(size_t)s * a.max_tokens + new_pos] = choice;
     grammar_update(a.gr, a.st, s, choice, active, new_pos >= a.max_tokens - 1);
+    rescore_commit(a.rs, a.gr, s, choice, active);
     a.st.token[s] = choice;
     a.st.position[s] = new_pos;
   }
@@ -230,7 +319,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
           if (a.logits_out && lane == 0) a.logits_out[(size_t)(m0 + i) * a.V + v] = logit;
           const bool ok = a.gr.kind == 1 ? a.gr.table[(size_t)rule[i] * a.V + v] != 0 : ((rule[i] >> cls) & 1u) != 0;
           if (ok) {
-            const unsigned long long k = argmax_key(logit + bias, v);
+            const unsigned long long k = argmax_key(rescore_logit(a.rs, a.st, m0 + i, v, logit + bias), v);
             best[i] = k > best[i] ? k : best[i];
           }
         }

@@ -1,62 +1,75 @@
-// One decode step as ONE persistent kernel, for up to 8 live rows.
+// One decode step (or prefill chunk of up to 8 rows) as ONE persistent kernel
+// whose weights and K/V stream through a shared-memory ring.
 //
 // At batch 1 the multi-kernel step is bound by launch and dependency latency
-// (97 kernels that each move 2-8 MB).  Here a grid of clusters of 4 CTAs (one
-// CTA per SM) runs the whole step with three grid barriers per layer, the
-// minimum for this decoder: every LayerNorm and every projection input needs
-// the whole residual vector, and the residual needs every head or every FFN
-// unit.  Inside a phase the exchanges stay in a cluster (distributed shared
-// memory and cluster barriers):
+// (97 kernels that each move 2-8 MB).  Here one CTA per SM runs the whole
+// step.  Each CTA has a producer warp and eight consumer warps:
 //
-//   phase A (cluster per head h): combine the previous FFN partial sums into
-//     the residual, LayerNorm, the 192 q/k/v rows of head h, K/V append, self
-//     attention of head h split over the cluster, and head h's share of the
-//     out-projection, written as a partial sum over the head.
-//   phase B (cluster per head h): combine the out-projection partials,
-//     residual + self_attn_norm, cross q of head h, cross attention, cross
-//     out-projection partial.
-//   phase C (every CTA): combine, residual + cross_attn_norm, a slice of fc1
-//     units + GELU, their fc2 contribution, reduced inside the cluster.
-//   logits (every CTA): combine, residual + final_norm, a slice of the
-//     vocabulary, grammar mask, argmax keys; the last CTA commits the step.
+//   * the producer walks the CTA's fixed sequence of pieces for the whole
+//     step -- its slice of every weight matrix, and for attention CTAs the
+//     K/V blocks of its key range -- and copies each piece (at most 16 KB)
+//     into the next free stage of a ring in shared memory with 1-D bulk
+//     copies.  Nothing it copies is written during the step (weights, cross
+//     K/V, self K/V of earlier positions), so it runs ahead of the consumers
+//     by the ring's depth, across grid barriers, and HBM streams while the
+//     consumers wait;
+//   * the consumers run the step in six phases per layer separated by grid
+//     barriers, every matrix split by rows over all CTAs:
+//       P1  r -> LayerNorm -> QKV rows (q to global, K/V appended to the cache)
+//       P2  self-attention, one cluster of 4 CTAs per head (keys split over
+//           the cluster, softmax statistics and outputs exchanged through
+//           distributed shared memory), then the head's share of the
+//           out-projection as a partial sum over the head
+//       P3  r = x + bf16(sum over heads + bias) -> self_attn_norm -> cross q rows
+//       P4  cross-attention as P2, with the cross out-projection
+//       P5  r -> cross_attn_norm -> fc1 rows + GELU (to global)
+//       P6  fc2 rows -> r = x + bf16(fc2 + bias) (to global)
+//     then the logits phase: r -> final_norm -> a vocabulary slice, grammar
+//     mask, argmax keys; the last CTA commits the step.
 //
-// Rounding follows the reference's CUDA path (engine.py:286-315) exactly as
-// the multi-kernel path does; only float32 summation orders differ, and they
-// are fixed, so the step is deterministic and a row's result does not depend
-// on the other rows of the launch.
+// Rounding follows the reference's CUDA path (engine.py:286-315) as the
+// multi-kernel path does; float32 summation orders differ from it but are
+// fixed, so the step is deterministic and a row's result does not depend on
+// the other rows of the launch.
 //
-// Every wait is bounded.  A grid barrier that has not completed after 2 s
-// records an error word; from then on no barrier waits (each sees the error
-// word), the CTAs run the remaining phases without waiting and the commit is
-// skipped, so every CTA takes the same cluster barriers and the kernel ends.
+// Every wait is bounded.  A grid barrier, ring stage or cluster exchange that
+// has not completed in time records an error word; from then on no wait
+// blocks, the phases run on whatever data they have, the commit is skipped
+// and every CTA still takes the same barriers, so the kernel ends.
 #pragma once
 
 #include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "logits.cuh"
+#include "mbarrier.cuh"
 #include "proj.cuh"
 
 namespace s2r {
 
 namespace cg = cooperative_groups;
 
-constexpr int kPClus = 4;                      // CTAs per cluster (one head per cluster)
-constexpr int kPThreads = 256;
-constexpr int kPWarps = kPThreads / 32;
+constexpr int kPClus = 4;                        // CTAs per cluster: one head's attention per cluster
+constexpr int kPConsumers = 256;                 // eight consumer warps
+constexpr int kPWarps = kPConsumers / 32;
+constexpr int kPThreads = kPConsumers + 32;      // + the producer warp
 constexpr int kPMaxRows = 8;
-constexpr int kQkvLocal = 3 * kHeadDim / kPClus;  // q/k/v rows of a head per CTA (48)
-constexpr int kDimsLocal = kHeadDim / kPClus;     // head dims per CTA (16)
-constexpr int kErrBarrier = 3;                    // a grid barrier timed out
+constexpr int kPStage = 16384;                   // bytes per ring stage
+constexpr int kPKeys = kPStage / (kHeadDim * 2);  // K or V rows per stage (128)
+constexpr int kPMaxStages = 12;
+constexpr int kErrBarrier = 3;  // a grid barrier timed out
+constexpr int kErrRing = 8;     // a ring stage or cluster exchange timed out
 constexpr unsigned long long kSpinNs = 2000000000ull;
+constexpr int kTraceSlots = 512;
+constexpr int kTraceCtas = 16;
 
 struct PLayer {
-  const bf16 *wqkv, *bqkv;  // [3D, D], [3D]
-  const bf16 *woT, *bo;     // out-projection transposed [D_in, D_out]
-  const bf16 *wcq, *bcq;    // [D, D]
-  const bf16 *wcoT, *bco;   // cross out-projection transposed
-  const bf16 *w1, *b1;      // [F, D]
-  const bf16 *w2T, *b2;     // fc2 transposed [F, D]
+  const bf16 *wqkv, *bqkv;   // [3D, D], [3D]
+  const bf16 *wo_hb, *bo;    // out-projection by head: wo_hb[h][n][d] = Wo[n][64h + d]
+  const bf16 *wcq, *bcq;     // [D, D]
+  const bf16 *wco_hb, *bco;  // cross out-projection by head
+  const bf16 *w1, *b1;       // [F, D]
+  const bf16 *w2, *b2;       // [D, F]
   const float *ln_self_g, *ln_self_b, *ln_cross_g, *ln_cross_b, *ln_final_g, *ln_final_b;
   bf16 *kpool, *vpool;
   const bf16 *ck, *cv;
@@ -68,78 +81,181 @@ struct PArgs {
   SlotState st;
   Grammar gr;
   int D, H, FFN, V, L, T, F, pps;
-  int units;       // fc1 units per CTA (phase C)
-  int chunk_cap;   // attention scores per row per CTA
-  int logits;      // 1: decode step (logits + commit); 0: prefill (K/V only)
+  int chunk_cap;  // attention keys per row per CTA
+  int stages;     // ring stages
+  int logits;     // 1: decode step (logits + commit); 0: prefill (K/V only)
   const PLayer* layers;
   const float *tok_emb, *pos_emb, *emb_g, *emb_b;
   const bf16* emb;
   const float* bias;
-  float *part_o, *part_c, *part_f;  // [H][M][D], [H][M][D], [clusters][M][D]
-  unsigned* bar;                    // [0] arrivals, [1] exits
+  float* r;                // [M][D] residual sums between phases
+  bf16* q;                 // [M][D] queries (self, then cross)
+  bf16* hid;               // [M][FFN] GELU outputs
+  float *part_o, *part_c;  // [H][M][D] out-projection partial sums by head
+  unsigned* bar;           // [0] arrivals, [1] exits
   unsigned long long* keys;
   unsigned* counter;
   int* err;
   const int64_t* forced;
   float* logits_out;
   int64_t* greedy_out;
-  int prefetch;      // issue next-phase L2 prefetches
-  long long* trace;  // optional clock64 marks (rank 0 of the first kTraceCtas clusters)
+  long long* trace;  // optional globaltimer marks (rank 0 of the first kTraceCtas clusters)
+  Rescore rs;        // frame-head rescoring (rs.on == 0: none)
 };
 
-constexpr int kTraceSlots = 512;
-constexpr int kTraceCtas = 16;
+// ---------------------------------------------------------------- geometry
+// The producer and the consumers derive the same piece sequence from these.
+
+// Rows [r0, r1) of an N-row matrix owned by this CTA.
+__device__ __forceinline__ void row_slice(int N, int& r0, int& r1) {
+  r0 = (int)((long long)N * blockIdx.x / gridDim.x);
+  r1 = (int)((long long)N * (blockIdx.x + 1) / gridDim.x);
+}
+
+__device__ __forceinline__ int rows_per_stage(int K) { return max(1, kPStage / (K * 2)); }
+
+struct KeyRange {
+  int slot, L, j0, j1, js;  // keys [j0, j1) of this CTA; [j0, js) stream through the ring
+};
+
+__device__ __forceinline__ KeyRange key_range(const PArgs& a, int m, bool cross, int rank) {
+  KeyRange k{0, 0, 0, 0, 0};
+  if (!row_active(a.rm, a.st, m)) return k;
+  k.slot = row_slot(a.rm, m);
+  k.L = cross ? a.st.frames[k.slot] : row_pos(a.rm, a.st, m) + 1;
+  const int chunk = (k.L + kPClus - 1) / kPClus;
+  k.j0 = min(k.L, rank * chunk);
+  k.j1 = min(k.L, k.j0 + chunk);
+  // keys written during this launch (the rows' own positions) are read from global memory
+  const int fresh = cross ? k.L : (a.rm.prefill ? a.rm.pos0 : row_pos(a.rm, a.st, m));
+  k.js = max(k.j0, min(k.j1, fresh));
+  return k;
+}
+
+// Number of 128-key ring pieces of [j0, js).
+__device__ __forceinline__ int key_blocks(const KeyRange& k) {
+  return k.js > k.j0 ? (k.js - 1) / kPKeys - k.j0 / kPKeys + 1 : 0;
+}
+
+__device__ __forceinline__ void block_keys(const KeyRange& k, int b, int& lo, int& hi) {
+  const int base = (k.j0 / kPKeys + b) * kPKeys;
+  lo = max(k.j0, base);
+  hi = min(k.js, base + kPKeys);
+}
+
+__device__ __forceinline__ const bf16* key_row(const PArgs& a, const PLayer& W, bool cross, bool value, int slot, int h,
+                                               int j) {
+  if (cross) return (value ? W.cv : W.ck) + (((size_t)slot * a.H + h) * a.F + j) * kHeadDim;
+  return (value ? W.vpool : W.kpool) + paged_offset(a.st.page_table, a.pps, a.H, slot, h, j);
+}
+
+// ---------------------------------------------------------------- ring
+struct Ring {
+  unsigned char* buf;
+  uint64_t* full;
+  uint64_t* empty;
+  int stages;
+};
+
+// Producer: request one piece into the next stage (waits, bounded, for it to be free).
+struct Producer {
+  const PArgs* a;
+  Ring ring;
+  int seq = 0;
+  bool dead = false;
+  __device__ __forceinline__ unsigned char* begin(unsigned bytes) {
+    const int s = seq % ring.stages;
+    if (!dead && seq >= ring.stages) {
+      if (*(volatile int*)a->err != 0 || !mbar_wait(&ring.empty[s], ((seq / ring.stages) - 1) & 1)) {
+        if (*(volatile int*)a->err == 0) atomicExch(a->err, kErrRing);
+        dead = true;
+      }
+    }
+    if (!dead) mbar_expect_tx(&ring.full[s], bytes);
+    return ring.buf + (size_t)s * kPStage;
+  }
+  __device__ __forceinline__ void copy(unsigned char* dst, const void* src, unsigned bytes) {
+    if (!dead) bulk_load(dst, src, bytes, &ring.full[seq % ring.stages]);
+  }
+  __device__ __forceinline__ void end() { ++seq; }
+  // a run of rows [r0, r1) of a row-major [*, K] matrix, in pieces of rows_per_stage(K)
+  __device__ __forceinline__ void rows(const bf16* W, int K, int r0, int r1) {
+    const int rps = rows_per_stage(K);
+    for (int p = r0; p < r1; p += rps) {
+      const int n = min(rps, r1 - p);
+      unsigned char* dst = begin((unsigned)(n * K * 2));
+      copy(dst, W + (size_t)p * K, (unsigned)(n * K * 2));
+      end();
+    }
+  }
+  __device__ __forceinline__ void keys(const PLayer& W, bool cross, bool value, int h, const KeyRange& k) {
+    const int nb = key_blocks(k);
+    for (int b = 0; b < nb; ++b) {
+      int lo, hi;
+      block_keys(k, b, lo, hi);
+      unsigned char* dst = begin((unsigned)((hi - lo) * kHeadDim * 2));
+      for (int j = lo; j < hi;) {  // a self K/V page holds 64 consecutive keys of a head
+        const int n = cross ? hi - j : min(hi - j, kPageTokens - j % kPageTokens);
+        copy(dst + (size_t)(j - lo) * kHeadDim * 2, key_row(*a, W, cross, value, k.slot, h, j),
+             (unsigned)(n * kHeadDim * 2));
+        j += n;
+      }
+      end();
+    }
+  }
+  // the last stages' copies land before the CTA leaves
+  __device__ __forceinline__ void drain() {
+    for (int i = max(0, seq - ring.stages); i < seq; ++i) mbar_wait(&ring.full[i % ring.stages], (i / ring.stages) & 1);
+  }
+};
+
+// Consumers: wait (bounded) for the next piece, release it after use.
+struct Consumer {
+  const PArgs* a;
+  Ring ring;
+  int seq = 0;
+  int* failed;  // shared flag
+  __device__ __forceinline__ const unsigned char* wait() {
+    const int s = seq % ring.stages;
+    if (!*(volatile int*)failed && !mbar_wait(&ring.full[s], (seq / ring.stages) & 1)) {
+      *(volatile int*)failed = 1;
+      atomicExch(a->err, kErrRing);
+    }
+    return ring.buf + (size_t)s * kPStage;
+  }
+  __device__ __forceinline__ void release() {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&ring.empty[seq % ring.stages])) : "memory");
+    ++seq;
+  }
+};
+
+// ---------------------------------------------------------------- consumer helpers
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kPConsumers) : "memory"); }
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void trace_mark(const PArgs& a, int idx) {
   if (a.trace == nullptr || threadIdx.x != 0 || idx < 0 || idx >= kTraceSlots) return;
   const int b = blockIdx.x;
   const int which = (b % kPClus == 0 && b / kPClus < kTraceCtas) ? b / kPClus : -1;
-  if (which >= 0) a.trace[which * kTraceSlots + idx] = clock64();
+  if (which >= 0) a.trace[which * kTraceSlots + idx] = (long long)global_ns();
 }
 
-// L2-coherent loads (data written earlier in this launch by other SMs) and
-// read-only weight loads.
-__device__ __forceinline__ uint4 ld_cg(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
-__device__ __forceinline__ float4 ld_cg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ uint4 ld_w(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void prefetch_bulk_l2(const void* p, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// Shared memory of one CTA (dynamic); sizes mirror persistent_smem() on the host.
-struct PSmem {
-  float* xk;    // [MR][D]  residual-stream value after LayerNorm (fp32)
-  bf16* xs;     // [MR][KP] the same rounded to bf16, GEMV input
-  float* y;     // [MR][D]  partial sums exchanged inside the cluster
-  float* sc;    // [MR][chunk_cap] attention scores
-  float* qh;    // [MR][64] the head's query
-  float* kn;    // [MR][64] the head's new key (decode rows)
-  float* vn;    // [MR][64] the head's new value
-  float* loc;   // [MR][48] this CTA's q/k/v rows
-  float* ov;    // [MR][64] partial attention output
-  float* stat;  // [MR][2]  local max and sum
-  float* av;    // [MR][16] this CTA's dims of the attention output
-  float* hid;   // [MR][units] fc1 outputs
-  float* red;   // [8][64]  reduction scratch
-};
-
-// Grid barrier: every CTA arrives on one counter and waits for all (bounded).
-// Returns false once any CTA has recorded an error.
-__device__ __forceinline__ bool grid_barrier(const PArgs& a, unsigned& target) {
-  __shared__ int ok_s;
-  __syncthreads();
+// Grid barrier over the consumers of every CTA (bounded).  False once any
+// CTA has recorded an error: from then on nobody waits.
+__device__ __forceinline__ bool grid_barrier(const PArgs& a, unsigned& target, int* ok_s) {
+  csync();
   if (threadIdx.x == 0) {
     target += gridDim.x;
-    __threadfence();
-    atomicAdd(a.bar, 1u);
-    int ok = 1;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+    int ok = *(volatile int*)a.err == 0;
     const unsigned long long t0 = global_ns();
-    while (ld_acquire(a.bar) < target) {
+    while (ok && ld_acquire_u32(a.bar) < target) {
       if (*(volatile int*)a.err != 0) {
         ok = 0;
         break;
@@ -149,25 +265,23 @@ __device__ __forceinline__ bool grid_barrier(const PArgs& a, unsigned& target) {
         ok = 0;
         break;
       }
-      __nanosleep(20);
     }
-    if (ok && *(volatile int*)a.err != 0) ok = 0;
-    ok_s = ok;
+    *ok_s = ok;
   }
-  __syncthreads();
-  return ok_s != 0;
+  csync();
+  return *ok_s != 0;
 }
 
-// Sum v[m] over the block (fixed order: warps 0..7); every thread gets the totals.
+// Sum v[m] over the consumers (fixed order); every consumer gets the totals.
 template <int MR>
-__device__ __forceinline__ void block_sum(float (&v)[MR], float* red) {
+__device__ __forceinline__ void consumer_sum(float (&v)[MR], float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     const float t = warp_sum(v[m]);
     if (lane == 0) red[warp * MR + m] = t;
   }
-  __syncthreads();
+  csync();
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     float t = 0.f;
@@ -175,17 +289,28 @@ __device__ __forceinline__ void block_sum(float (&v)[MR], float* red) {
     for (int w = 0; w < kPWarps; ++w) t += red[w * MR + m];
     v[m] = t;
   }
-  __syncthreads();
+  csync();
 }
 
-// Residual stream update at the start of a phase, identically in every CTA:
-// r = xk + bf16(sum_p part[p][m][:] + bias) (the embedding for layer 0),
-// then x = LayerNorm(r) (two-pass, biased variance) into xk / xs.  Thread t
-// owns columns 4t..4t+3 (width <= 1024).
-template <int KCH, int MR>
-__device__ void combine_ln(const PArgs& a, PSmem& s, const float* part, int nparts, const bf16* pbias,
-                           const float* g, const float* b, bool embed) {
-  constexpr int KP = KCH * 256;
+struct PSmem {
+  float* x;     // [MR][D]  the LayerNorm output (float32): the residual input of the next sum
+  bf16* xs;     // [MR][KP] the same in bfloat16: GEMV input
+  bf16* hs;     // [MR][FP] GELU outputs (fc2 input), shares space with sc
+  float* sc;    // [MR][chunk_cap] attention scores
+  float* qh;    // [MR][64] the head's query
+  float* oh;    // [MR][64] the head's attention output (bf16-rounded)
+  float* xch0;  // [2][kPClus][MR][2]  exchanged (max, sum) by use parity and source rank
+  float* xch1;  // [2][kPClus][MR][64] exchanged partial outputs by use parity and source rank
+  float* red;   // [8][64] reduction scratch
+};
+
+// r (from global, or the embedding for layer 0) -> LayerNorm into x / xs.
+// with_part: r = x + bf16(sum_h part[h] + bias) first (the residual sum of an
+// attention block).  Thread t owns columns 4t..4t+3.
+template <int MR>
+__device__ void combine_ln(const PArgs& a, PSmem& s, int KP, int mode, const float* part, const bf16* pbias,
+                           const float* g, const float* b) {
+  // mode 0: embedding; 1: r from global; 2: x + bf16(sum of head partials + bias)
   const int D = a.D;
   const int col = threadIdx.x * 4;
   const bool own = col < D;
@@ -194,21 +319,22 @@ __device__ void combine_ln(const PArgs& a, PSmem& s, const float* part, int npar
   for (int m = 0; m < MR; ++m) {
     r[m] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (m >= a.M || !own) continue;
-    if (embed) {
+    if (mode == 0) {
       const float4 t = *reinterpret_cast<const float4*>(a.tok_emb + (size_t)row_token(a.rm, a.st, m) * D + col);
       const float4 p = *reinterpret_cast<const float4*>(a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * D + col);
       r[m] = make_float4(t.x + p.x, t.y + p.y, t.z + p.z, t.w + p.w);  // POSITION_OFFSET 2
+    } else if (mode == 1) {
+      r[m] = __ldcg(reinterpret_cast<const float4*>(a.r + (size_t)m * D + col));
     } else {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 16
-      for (int q = 0; q < nparts; ++q) {
-        const float4 p = ld_cg_f4(part + ((size_t)q * a.M + m) * D + col);
+      for (int h = 0; h < a.H; ++h) {
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)h * a.M + m) * D + col));
         acc.x += p.x;
         acc.y += p.y;
         acc.z += p.z;
         acc.w += p.w;
       }
-      const float4 x = *reinterpret_cast<const float4*>(s.xk + (size_t)m * D + col);
+      const float4 x = *reinterpret_cast<const float4*>(s.x + (size_t)m * D + col);
       const uint2 bb = *reinterpret_cast<const uint2*>(pbias + col);
       r[m].x = x.x + round_bf16(acc.x + bf_lo(bb.x));
       r[m].y = x.y + round_bf16(acc.y + bf_hi(bb.x));
@@ -219,7 +345,7 @@ __device__ void combine_ln(const PArgs& a, PSmem& s, const float* part, int npar
   float sum[MR];
 #pragma unroll
   for (int m = 0; m < MR; ++m) sum[m] = (r[m].x + r[m].y) + (r[m].z + r[m].w);
-  block_sum<MR>(sum, s.red);
+  consumer_sum<MR>(sum, s.red);
   float mean[MR], sq[MR];
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
@@ -231,7 +357,7 @@ __device__ void combine_ln(const PArgs& a, PSmem& s, const float* part, int npar
       sq[m] = 0.f;
     }
   }
-  block_sum<MR>(sq, s.red);
+  consumer_sum<MR>(sq, s.red);
   if (col < KP) {
     float4 gg = make_float4(0.f, 0.f, 0.f, 0.f), bb = gg;
     if (own) {
@@ -240,639 +366,536 @@ __device__ void combine_ln(const PArgs& a, PSmem& s, const float* part, int npar
     }
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
-      if (m >= a.M) continue;
       uint2 packed = make_uint2(0, 0);
-      if (own) {
+      if (own && m < a.M) {
         const float rstd = rsqrtf(sq[m] / (float)D + kLnEps);
         float4 y;
         y.x = (r[m].x - mean[m]) * rstd * gg.x + bb.x;
         y.y = (r[m].y - mean[m]) * rstd * gg.y + bb.y;
         y.z = (r[m].z - mean[m]) * rstd * gg.z + bb.z;
         y.w = (r[m].w - mean[m]) * rstd * gg.w + bb.w;
-        *reinterpret_cast<float4*>(s.xk + (size_t)m * D + col) = y;
+        *reinterpret_cast<float4*>(s.x + (size_t)m * D + col) = y;
         packed = make_uint2(pack_bf16(y.x, y.y), pack_bf16(y.z, y.w));
       }
       *reinterpret_cast<uint2*>(s.xs + (size_t)m * KP + col) = packed;
     }
   }
-  __syncthreads();
+  csync();
 }
 
-// Dot products of weight rows against the staged rows: warp w takes rows
-// r0 + w, r0 + w + 8, ... < r1 (four per pass, all loads in flight together)
-// and calls epi(m, row, acc) on lane m.
-template <int KCH, int MR, typename Epi>
-__device__ __forceinline__ void gemv_rows(const bf16* W, int K, int r0, int r1, const bf16* xs, int M, Epi epi) {
-  constexpr int KP = KCH * 256;
-  constexpr int RP = 4;
+// Rows [r0, r1) of a [*, K] weight streamed through the ring, against the
+// staged rows xs (stride KP, zero padded): warp w takes row w of every piece.
+// Lane l holds columns c*256 + 8l .. 8l+7 of every 256-column chunk c, as in
+// the multi-kernel projection.  epi(m, row, acc) runs on lane m.
+template <int MR, typename Epi>
+__device__ __forceinline__ void gemv_stream(Consumer& cs, int K, int r0, int r1, const bf16* xs, int KP, int M,
+                                            Epi epi) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int r = r0 + warp; r < r1; r += RP * kPWarps) {
-    uint4 w[RP][KCH];
+  const int rps = rows_per_stage(K);
+  const int nch = (K + 255) / 256;
+  for (int p = r0; p < r1; p += rps) {
+    const bf16* ws = reinterpret_cast<const bf16*>(cs.wait());
+    const int n = min(rps, r1 - p);
+    for (int i = warp; i < n; i += kPWarps) {
+      float acc[MR];
 #pragma unroll
-    for (int k = 0; k < RP; ++k) {
-      const int row = r + k * kPWarps;
-#pragma unroll
-      for (int c = 0; c < KCH; ++c) {
+      for (int m = 0; m < MR; ++m) acc[m] = 0.f;
+      for (int c = 0; c < nch; ++c) {
         const int col = c * 256 + lane * 8;
-        w[k][c] = (col < K && row < r1) ? ld_w(W + (size_t)row * K + col) : make_uint4(0, 0, 0, 0);
+        const uint4 w = col < K ? *reinterpret_cast<const uint4*>(ws + (size_t)i * K + col) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int m = 0; m < MR; ++m)
+          acc[m] += dot8(w, *reinterpret_cast<const uint4*>(xs + (size_t)m * KP + col));
+      }
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        acc[m] = warp_sum(acc[m]);
+        if (lane == m && m < M) epi(m, p + i, acc[m]);
       }
     }
-#pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      float acc[RP];
-#pragma unroll
-      for (int k = 0; k < RP; ++k) acc[k] = 0.f;
-#pragma unroll
-      for (int c = 0; c < KCH; ++c) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)m * KP + c * 256 + lane * 8);
-#pragma unroll
-        for (int k = 0; k < RP; ++k) acc[k] += dot8(w[k][c], xv);
-      }
-#pragma unroll
-      for (int k = 0; k < RP; ++k) {
-        acc[k] = warp_sum(acc[k]);
-        if (lane == m && m < M && r + k * kPWarps < r1) epi(m, r + k * kPWarps, acc[k]);
-      }
-    }
+    cs.release();
   }
 }
 
-// y[m][n] = sum_j s[m][j] * WT[j0 + j][n] for every n (rows of a transposed
-// weight).  Thread t owns 4 columns; the loads of 16 rows are issued before
-// any is used, and j is summed in order.
-template <int MR>
-__device__ __forceinline__ void axpy_rows(const bf16* WT, int D, int j0, int J, const float* sv, int lds, int M,
-                                          float* y) {
-  constexpr int JB = 32;
-  for (int n = threadIdx.x * 4; n < D; n += kPThreads * 4) {
-    float acc[MR][4];
-#pragma unroll
-    for (int m = 0; m < MR; ++m)
-#pragma unroll
-      for (int t = 0; t < 4; ++t) acc[m][t] = 0.f;
-    for (int jb = 0; jb < J; jb += JB) {
-      uint2 w[JB];
-#pragma unroll
-      for (int u = 0; u < JB; ++u)
-        w[u] = jb + u < J ? __ldg(reinterpret_cast<const uint2*>(WT + (size_t)(j0 + jb + u) * D + n)) : make_uint2(0, 0);
-#pragma unroll
-      for (int u = 0; u < JB; ++u) {
-        if (jb + u < J) {
-          const float w0 = bf_lo(w[u].x), w1 = bf_hi(w[u].x), w2 = bf_lo(w[u].y), w3 = bf_hi(w[u].y);
-#pragma unroll
-          for (int m = 0; m < MR; ++m) {
-            const float sj = m < M ? sv[m * lds + jb + u] : 0.f;
-            acc[m][0] = fmaf(sj, w0, acc[m][0]);
-            acc[m][1] = fmaf(sj, w1, acc[m][1]);
-            acc[m][2] = fmaf(sj, w2, acc[m][2]);
-            acc[m][3] = fmaf(sj, w3, acc[m][3]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < MR; ++m)
-      if (m < M) *reinterpret_cast<float4*>(y + (size_t)m * D + n) = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
-  }
-}
-
-// Sum the cluster's y[m][n] over this CTA's column range, in rank order, into dst[m][n].
-template <int MR>
-__device__ __forceinline__ void cluster_reduce_y(cg::cluster_group& cluster, PSmem& s, int D, int M, float* dst) {
+// Exchange `count` floats per source rank with the cluster: src (this CTA's
+// values) go to slot [rank] (of `cap` floats) of every peer's buffer; returns (bounded) once
+// every peer's values are in this CTA's buffer, which it returns.  xbar
+// counts one arrival per rank.  Buffers alternate by use, so a peer that is
+// one exchange ahead never overwrites values still being read.
+__device__ __forceinline__ const float* cluster_exchange(const PArgs& a, cg::cluster_group& cluster, float* bufs,
+                                                         const float* src, int count, int cap, uint64_t* xbar,
+                                                         int& uses, int* failed) {
   const int rank = (int)cluster.block_rank();
-  const int per = D / kPClus;
-  const int n0 = rank * per;
-  for (int idx = threadIdx.x * 4; idx < M * per; idx += kPThreads * 4) {
-    const int m = idx / per, n = n0 + idx % per;
-    float4 v[kPClus];
-#pragma unroll
-    for (int r = 0; r < kPClus; ++r)
-      v[r] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(s.y, r) + (size_t)m * D + n);
-    float4 acc = v[0];
-#pragma unroll
-    for (int r = 1; r < kPClus; ++r) {
-      acc.x += v[r].x;
-      acc.y += v[r].y;
-      acc.z += v[r].z;
-      acc.w += v[r].w;
+  float* buf = bufs + (size_t)(uses & 1) * kPClus * cap;
+  for (int idx = threadIdx.x; idx < kPClus * count; idx += kPConsumers) {
+    const int peer = idx / count, i = idx % count;
+    cluster.map_shared_rank(buf, peer)[rank * cap + i] = src[i];
+  }
+  csync();
+  if (threadIdx.x == 0) {  // the release of each arrival covers the consumers' stores (ordered by csync)
+    for (int peer = 0; peer < kPClus; ++peer) {
+      uint32_t remote;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(xbar)), "r"(peer));
+      asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
     }
-    *reinterpret_cast<float4*>(dst + (size_t)m * D + n) = acc;
   }
+  const unsigned parity = uses & 1;
+  ++uses;
+  if (*(volatile int*)failed) return buf;
+  const uint32_t addr = smem_u32(xbar);
+  bool done = false;
+  const unsigned long long t0 = global_ns();
+  while (!done) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    done = r != 0;
+    if (!done && global_ns() - t0 > kMbarWaitNs) {
+      *(volatile int*)failed = 1;
+      atomicExch(a.err, kErrRing);
+      break;
+    }
+  }
+  return buf;
 }
 
-struct KeySrc {
-  bool cross;
-  bool own_last;  // the last key/value of each row come from s.kn / s.vn
-  const bf16* k;
-  const bf16* v;
-  const int32_t* page_table;
-  int pps, H, F;
-  __device__ __forceinline__ const bf16* krow(int slot, int h, int j) const {
-    return cross ? k + (((size_t)slot * H + h) * F + j) * kHeadDim : k + paged_offset(page_table, pps, H, slot, h, j);
-  }
-  __device__ __forceinline__ const bf16* vrow(int slot, int h, int j) const {
-    return cross ? v + (((size_t)slot * H + h) * F + j) * kHeadDim : v + paged_offset(page_table, pps, H, slot, h, j);
-  }
-};
-
-__device__ __forceinline__ uint4 pack8(const float* p) {
-  return make_uint4(pack_bf16(p[0], p[1]), pack_bf16(p[2], p[3]), pack_bf16(p[4], p[5]), pack_bf16(p[6], p[7]));
-}
-
-// Attention of head h for every active row, keys split over the cluster.
-// Leaves this CTA's kDimsLocal output dims (bf16-rounded) in s.av.  Two
-// cluster barriers.
+// Attention of head h for every active row (keys split over the cluster),
+// then this CTA's quarter of the head's out-projection as a partial sum:
+// part[h][m][n] = sum_d Who[h][n][d] * o[m][d] for n in the CTA's quarter.
 template <int MR>
-__device__ void cluster_attention(const PArgs& a, cg::cluster_group& cluster, PSmem& s, const KeySrc& src, int h) {
+__device__ void head_attention(const PArgs& a, const PLayer& W, cg::cluster_group& cluster, PSmem& s, Consumer& cs,
+                               bool cross, int h, float* part, uint64_t* xbar, int* uses) {
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int grp = tid >> 3, sub = tid & 7;
-  constexpr int G = kPThreads / 8;
-  __shared__ float wred[kPWarps];
-  for (int m = 0; m < a.M; ++m) {
+  const int grp = tid >> 3, sub = tid & 7;  // 32 groups of 8 lanes: one key row per group
+  constexpr int G = kPConsumers / 8;
+  // the head's query of every row (written in the previous phase)
+  for (int idx = tid; idx < a.M * kHeadDim; idx += kPConsumers) {
+    const int m = idx / kHeadDim, d = idx % kHeadDim;
+    s.qh[idx] = __bfloat162float(__ldcg(a.q + (size_t)m * a.D + h * kHeadDim + d));
+  }
+  csync();
+  float stat[MR][2];
+  // ---- scores: streamed keys [j0, js), then the keys written in this launch [js, j1)
+#pragma unroll
+  for (int m = 0; m < MR; ++m) {
+    stat[m][0] = -INFINITY;
+    stat[m][1] = 0.f;
+    if (m >= a.M) continue;
+    const KeyRange k = key_range(a, m, cross, rank);
     float* sc = s.sc + (size_t)m * a.chunk_cap;
-    const bool active = row_active(a.rm, a.st, m);
-    const int slot = row_slot(a.rm, m);
-    const int L = !active ? 0 : src.cross ? a.st.frames[slot] : row_pos(a.rm, a.st, m) + 1;
-    const int chunk = (L + kPClus - 1) / kPClus;
-    const int j0 = min(L, rank * chunk), j1 = min(L, j0 + chunk);
-    const int jown = src.own_last ? L - 1 : -1;
     float q[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) q[t] = s.qh[m * kHeadDim + sub * 8 + t];
     float lmax = -INFINITY;
-    for (int base = j0; base < j1; base += G * 4) {
-      uint4 kv[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = base + grp + u * G;
-        kv[u] = (j < j1 && j != jown) ? ld_cg(src.krow(slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
-        if (j == jown) kv[u] = pack8(s.kn + m * kHeadDim + sub * 8);
+    auto score = [&](uint4 kv, int j) {
+      float d = bf_lo(kv.x) * q[0];
+      d = fmaf(bf_hi(kv.x), q[1], d);
+      d = fmaf(bf_lo(kv.y), q[2], d);
+      d = fmaf(bf_hi(kv.y), q[3], d);
+      d = fmaf(bf_lo(kv.z), q[4], d);
+      d = fmaf(bf_hi(kv.z), q[5], d);
+      d = fmaf(bf_lo(kv.w), q[6], d);
+      d = fmaf(bf_hi(kv.w), q[7], d);
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      if (j >= 0) {
+        d = round_bf16(d) * 0.125f;  // head_dim ** -0.5
+        if (sub == 0) sc[j - k.j0] = d;
+        lmax = fmaxf(lmax, d);
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = base + grp + u * G;
-        float d = bf_lo(kv[u].x) * q[0];
-        d = fmaf(bf_hi(kv[u].x), q[1], d);
-        d = fmaf(bf_lo(kv[u].y), q[2], d);
-        d = fmaf(bf_hi(kv[u].y), q[3], d);
-        d = fmaf(bf_lo(kv[u].z), q[4], d);
-        d = fmaf(bf_hi(kv[u].z), q[5], d);
-        d = fmaf(bf_lo(kv[u].w), q[6], d);
-        d = fmaf(bf_hi(kv[u].w), q[7], d);
-        d += __shfl_xor_sync(0xffffffffu, d, 1);
-        d += __shfl_xor_sync(0xffffffffu, d, 2);
-        d += __shfl_xor_sync(0xffffffffu, d, 4);
-        if (j < j1) {
-          d = round_bf16(d) * 0.125f;  // head_dim ** -0.5
-          if (sub == 0) sc[j - j0] = d;
-          lmax = fmaxf(lmax, d);
-        }
+    };
+    const int nb = key_blocks(k);
+    for (int b = 0; b < nb; ++b) {
+      int lo, hi;
+      block_keys(k, b, lo, hi);
+      const unsigned char* st = cs.wait();
+      for (int i = grp; i < kPKeys; i += G) {  // uniform trip count: shuffles need every lane
+        const bool in = i < hi - lo;
+        const uint4 kv = in ? *reinterpret_cast<const uint4*>(st + (size_t)i * 128 + sub * 16) : make_uint4(0, 0, 0, 0);
+        score(kv, in ? lo + i : -1);
       }
+      cs.release();
+    }
+    for (int base = k.js; base < k.j1; base += G) {
+      const int j = base + grp;
+      const bool in = j < k.j1;
+      const uint4 kv = in ? __ldcg(reinterpret_cast<const uint4*>(key_row(a, W, cross, false, k.slot, h, j) + sub * 8))
+                          : make_uint4(0, 0, 0, 0);
+      score(kv, in ? j : -1);
     }
     lmax = warp_max(lmax);
-    if (lane == 0) wred[warp] = lmax;
-    __syncthreads();
-    float bm = wred[0];
+    if (lane == 0) s.red[warp] = lmax;
+    csync();
+    float bm = s.red[0];
 #pragma unroll
-    for (int w = 1; w < kPWarps; ++w) bm = fmaxf(bm, wred[w]);
-    __syncthreads();
+    for (int w = 1; w < kPWarps; ++w) bm = fmaxf(bm, s.red[w]);
+    csync();
     float lsum = 0.f;
-    for (int j = j0 + tid; j < j1; j += kPThreads) lsum += expf(sc[j - j0] - bm);
+    for (int j = k.j0 + tid; j < k.j1; j += kPConsumers) lsum += expf(sc[j - k.j0] - bm);
     lsum = warp_sum(lsum);
-    if (lane == 0) wred[warp] = lsum;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.f;
+    if (lane == 0) s.red[warp] = lsum;
+    csync();
+    float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < kPWarps; ++w) t += wred[w];
-      s.stat[m * 2 + 0] = bm;
-      s.stat[m * 2 + 1] = t;
-    }
-    __syncthreads();
+    for (int w = 0; w < kPWarps; ++w) t += s.red[w];
+    stat[m][0] = bm;
+    stat[m][1] = t;
+    csync();
   }
-  cluster.sync();  // (1) every CTA's local max and sum are visible
-  for (int m = 0; m < a.M; ++m) {
-    float* sc = s.sc + (size_t)m * a.chunk_cap;
-    const bool active = row_active(a.rm, a.st, m);
-    const int slot = row_slot(a.rm, m);
-    const int L = !active ? 0 : src.cross ? a.st.frames[slot] : row_pos(a.rm, a.st, m) + 1;
-    const int chunk = (L + kPClus - 1) / kPClus;
-    const int j0 = min(L, rank * chunk), j1 = min(L, j0 + chunk);
-    const int jown = src.own_last ? L - 1 : -1;
-    // global max and sum of exp(s - max) over the cluster (softmax, engine.py:291)
-    float mx[kPClus], sm[kPClus];
+  // ---- softmax statistics of the whole head, through the cluster
+  if (tid < a.M * 2) s.red[64 + tid] = stat[tid / 2][tid % 2];
+  csync();
+  const float* st0 = cluster_exchange(a, cluster, s.xch0, s.red + 64, a.M * 2, MR * 2, &xbar[0], uses[0], cs.failed);
+  csync();
+  // ---- p = bf16(exp(s - max) / sum), partial p.V
+  float ov[MR][8];
 #pragma unroll
-    for (int r = 0; r < kPClus; ++r) {
-      const float* st = cluster.map_shared_rank(s.stat, r) + m * 2;
-      mx[r] = st[0];
-      sm[r] = st[1];
-    }
-    float gmax = mx[0];
+  for (int m = 0; m < MR; ++m) {
 #pragma unroll
-    for (int r = 1; r < kPClus; ++r) gmax = fmaxf(gmax, mx[r]);
+    for (int t = 0; t < 8; ++t) ov[m][t] = 0.f;
+    if (m >= a.M) continue;
+    const KeyRange k = key_range(a, m, cross, rank);
+    const float* sc = s.sc + (size_t)m * a.chunk_cap;
+    float gmax = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kPClus; ++r) gmax = fmaxf(gmax, st0[r * MR * 2 + m * 2]);
     float gsum = 0.f;
 #pragma unroll
-    for (int r = 0; r < kPClus; ++r)
-      if (sm[r] > 0.f) gsum += sm[r] * expf(mx[r] - gmax);
-    float acc[8];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-    for (int base = j0; base < j1; base += G * 4) {
-      uint4 vv[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = base + grp + u * G;
-        vv[u] = (j < j1 && j != jown) ? ld_cg(src.vrow(slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
-        if (j == jown) vv[u] = pack8(s.vn + m * kHeadDim + sub * 8);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = base + grp + u * G;
-        const float p = j < j1 ? round_bf16(expf(sc[j - j0] - gmax) / gsum) : 0.f;
-        acc[0] = fmaf(p, bf_lo(vv[u].x), acc[0]);
-        acc[1] = fmaf(p, bf_hi(vv[u].x), acc[1]);
-        acc[2] = fmaf(p, bf_lo(vv[u].y), acc[2]);
-        acc[3] = fmaf(p, bf_hi(vv[u].y), acc[3]);
-        acc[4] = fmaf(p, bf_lo(vv[u].z), acc[4]);
-        acc[5] = fmaf(p, bf_hi(vv[u].z), acc[5]);
-        acc[6] = fmaf(p, bf_lo(vv[u].w), acc[6]);
-        acc[7] = fmaf(p, bf_hi(vv[u].w), acc[7]);
-      }
+    for (int r = 0; r < kPClus; ++r) {
+      const float sm = st0[r * MR * 2 + m * 2 + 1];
+      if (sm > 0.f) gsum += sm * expf(st0[r * MR * 2 + m * 2] - gmax);
     }
+    auto accum = [&](uint4 vv, int j) {
+      const float p = j >= 0 ? round_bf16(expf(sc[j - k.j0] - gmax) / gsum) : 0.f;
+      ov[m][0] = fmaf(p, bf_lo(vv.x), ov[m][0]);
+      ov[m][1] = fmaf(p, bf_hi(vv.x), ov[m][1]);
+      ov[m][2] = fmaf(p, bf_lo(vv.y), ov[m][2]);
+      ov[m][3] = fmaf(p, bf_hi(vv.y), ov[m][3]);
+      ov[m][4] = fmaf(p, bf_lo(vv.z), ov[m][4]);
+      ov[m][5] = fmaf(p, bf_hi(vv.z), ov[m][5]);
+      ov[m][6] = fmaf(p, bf_lo(vv.w), ov[m][6]);
+      ov[m][7] = fmaf(p, bf_hi(vv.w), ov[m][7]);
+    };
+    const int nb = key_blocks(k);
+    for (int b = 0; b < nb; ++b) {
+      int lo, hi;
+      block_keys(k, b, lo, hi);
+      const unsigned char* st = cs.wait();
+      for (int i = grp; i < hi - lo; i += G)
+        accum(*reinterpret_cast<const uint4*>(st + (size_t)i * 128 + sub * 16), lo + i);
+      cs.release();
+    }
+    for (int j = k.js + grp; j < k.j1; j += G)
+      accum(__ldcg(reinterpret_cast<const uint4*>(key_row(a, W, cross, true, k.slot, h, j) + sub * 8)), j);
+  }
+  // this CTA's partial output per row: groups reduced in fixed order
+#pragma unroll
+  for (int m = 0; m < MR; ++m) {
+    if (m >= a.M) continue;
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], 8);
-      acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], 16);
+      ov[m][t] += __shfl_xor_sync(0xffffffffu, ov[m][t], 8);
+      ov[m][t] += __shfl_xor_sync(0xffffffffu, ov[m][t], 16);
     }
     if (lane < 8) {
 #pragma unroll
-      for (int t = 0; t < 8; ++t) s.red[warp * kHeadDim + lane * 8 + t] = acc[t];
+      for (int t = 0; t < 8; ++t) s.red[warp * kHeadDim + lane * 8 + t] = ov[m][t];
     }
-    __syncthreads();
+    csync();
     if (tid < kHeadDim) {
       float o = 0.f;
 #pragma unroll
       for (int w = 0; w < kPWarps; ++w) o += s.red[w * kHeadDim + tid];
-      s.ov[m * kHeadDim + tid] = o;
+      s.oh[m * kHeadDim + tid] = o;
     }
-    __syncthreads();
+    csync();
   }
-  cluster.sync();  // (2) partial outputs visible
-  for (int idx = threadIdx.x; idx < a.M * kDimsLocal; idx += kPThreads) {
-    const int m = idx / kDimsLocal, d = rank * kDimsLocal + idx % kDimsLocal;
-    float v[kPClus];
+  const float* st1 =
+      cluster_exchange(a, cluster, s.xch1, s.oh, a.M * kHeadDim, MR * kHeadDim, &xbar[1], uses[1], cs.failed);
+  csync();
+  // o = bf16(sum over ranks in order)
+  for (int idx = tid; idx < a.M * kHeadDim; idx += kPConsumers) {
+    float o = 0.f;
 #pragma unroll
-    for (int r = 0; r < kPClus; ++r) v[r] = cluster.map_shared_rank(s.ov, r)[m * kHeadDim + d];
-    float o = v[0];
+    for (int r = 0; r < kPClus; ++r) o += st1[r * MR * kHeadDim + idx];
+    s.oh[idx] = round_bf16(o);
+  }
+  csync();
+  // ---- out-projection partial of the CTA's quarter of the features
+  const int per = a.D / kPClus, n0 = rank * per;
+  for (int p = 0; p < per; p += kPKeys) {  // 128 features (x 64 inputs) per piece
+    const unsigned char* st = cs.wait();
+    const int n = min(kPKeys, per - p);
+    for (int i = grp; i < kPKeys; i += G) {
+      const bool in = i < n;
+      const uint4 w = in ? *reinterpret_cast<const uint4*>(st + (size_t)i * 128 + sub * 16) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int r = 1; r < kPClus; ++r) o += v[r];
-    s.av[m * kDimsLocal + idx % kDimsLocal] = round_bf16(o);
-  }
-  __syncthreads();
-}
-
-// L2 prefetches for what this CTA reads in its next phase (weights and the
-// K/V of positions already cached), so that HBM streams them while the grid
-// barrier resolves.  phase: 0 = A of `layer`, 1 = B, 2 = C, 3 = logits.
-static __device__ void prefetch_phase(const PArgs& a, int phase, int layer, int rank, int ci, unsigned nclusters) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane != 0 || !a.prefetch) return;
-  const int D = a.D, H = a.H;
-  const size_t row_bytes = (size_t)D * sizeof(bf16);
-  if (phase == 3) {
-    for (int v = blockIdx.x * kPWarps + warp; v < a.V; v += gridDim.x * kPWarps)
-      prefetch_bulk_l2(a.emb + (size_t)v * D, (unsigned)row_bytes);
-    return;
-  }
-  const PLayer& W = a.layers[layer];
-  if (phase == 2) {
-    const int u0 = blockIdx.x * a.units, u1 = min(a.FFN, u0 + a.units);
-    if (u1 <= u0) return;
-    if (warp == 0) prefetch_bulk_l2(W.w1 + (size_t)u0 * D, (unsigned)((u1 - u0) * row_bytes));
-    if (warp == 1) prefetch_bulk_l2(W.w2T + (size_t)u0 * D, (unsigned)((u1 - u0) * row_bytes));
-    return;
-  }
-  for (int h = ci; h < H; h += nclusters) {
-    if (phase == 0) {
-      if (warp == 0) {  // this CTA's q/k/v rows, in up to two runs
-        int li = rank * kQkvLocal;
-        const int end = li + kQkvLocal;
-        while (li < end) {
-          const int part = li / kHeadDim, d0 = li % kHeadDim;
-          const int n = min(end - li, kHeadDim - d0);
-          prefetch_bulk_l2(W.wqkv + ((size_t)part * D + h * kHeadDim + d0) * D, (unsigned)(n * row_bytes));
-          li += n;
-        }
-      }
-      if (warp == 1)
-        prefetch_bulk_l2(W.woT + (size_t)(h * kHeadDim + rank * kDimsLocal) * D, (unsigned)(kDimsLocal * row_bytes));
-    } else {
-      if (warp == 0)
-        prefetch_bulk_l2(W.wcq + (size_t)(h * kHeadDim + rank * kDimsLocal) * D, (unsigned)(kDimsLocal * row_bytes));
-      if (warp == 1)
-        prefetch_bulk_l2(W.wcoT + (size_t)(h * kHeadDim + rank * kDimsLocal) * D, (unsigned)(kDimsLocal * row_bytes));
-    }
-    for (int m = warp; m < a.M; m += kPWarps) {
-      if (!row_active(a.rm, a.st, m)) continue;
-      const int slot = row_slot(a.rm, m);
-      if (phase == 1) {
-        const int L = a.st.frames[slot];
-        const int chunk = (L + kPClus - 1) / kPClus;
-        const int j0 = min(L, rank * chunk), j1 = min(L, j0 + chunk);
-        if (j1 <= j0) continue;
-        const size_t off = (((size_t)slot * H + h) * a.F + j0) * kHeadDim;
-        prefetch_bulk_l2(W.ck + off, (unsigned)((j1 - j0) * kHeadDim * sizeof(bf16)));
-        prefetch_bulk_l2(W.cv + off, (unsigned)((j1 - j0) * kHeadDim * sizeof(bf16)));
-      } else {
-        const int L = row_pos(a.rm, a.st, m);  // positions before the new token
-        const int chunk = (L + 1 + kPClus - 1) / kPClus;
-        const int j0 = min(L, rank * chunk), j1 = min(L, j0 + chunk);
-        for (int t = j0; t < j1;) {
-          const int n = min(j1 - t, kPageTokens - t % kPageTokens);
-          const size_t off = paged_offset(a.st.page_table, a.pps, H, slot, h, t);
-          prefetch_bulk_l2(W.kpool + off, (unsigned)(n * kHeadDim * sizeof(bf16)));
-          prefetch_bulk_l2(W.vpool + off, (unsigned)(n * kHeadDim * sizeof(bf16)));
-          t += n;
-        }
+      for (int m = 0; m < MR; ++m) {
+        if (m >= a.M) continue;
+        const float* o = s.oh + m * kHeadDim + sub * 8;
+        float d = bf_lo(w.x) * o[0];
+        d = fmaf(bf_hi(w.x), o[1], d);
+        d = fmaf(bf_lo(w.y), o[2], d);
+        d = fmaf(bf_hi(w.y), o[3], d);
+        d = fmaf(bf_lo(w.z), o[4], d);
+        d = fmaf(bf_hi(w.z), o[5], d);
+        d = fmaf(bf_lo(w.w), o[6], d);
+        d = fmaf(bf_hi(w.w), o[7], d);
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        d += __shfl_xor_sync(0xffffffffu, d, 4);
+        if (in && sub == 0) part[((size_t)h * a.M + m) * a.D + n0 + p + i] = d;
       }
     }
+    cs.release();
   }
 }
 
+// ---------------------------------------------------------------- the kernel
 template <int KCH, int MR>
 __global__ void __launch_bounds__(kPThreads, 1) step_persistent_kernel(const PArgs a) {
   cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char pst_smem[];
   constexpr int KP = KCH * 256;
   const int D = a.D, H = a.H;
   const int rank = (int)cluster.block_rank();
-  const unsigned nclusters = gridDim.x / kPClus;
+  const int nclusters = gridDim.x / kPClus;
   const int ci = blockIdx.x / kPClus;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int FP = (a.FFN + 255) / 256 * 256;
 
+  __shared__ __align__(8) uint64_t full[kPMaxStages], empty[kPMaxStages], xbar[2];
+  __shared__ int failed, ok_s, is_last;
+  __shared__ uint32_t rule[kPMaxRows];
+  __shared__ unsigned long long wbest[kPWarps][kPMaxRows];
+
+  Ring ring;
   PSmem s;
   {
-    unsigned char* p = smem_raw;
+    unsigned char* p = pst_smem;
     auto take = [&](size_t bytes) {
       unsigned char* q = p;
-      p += (bytes + 15) & ~size_t(15);
+      p += (bytes + 127) & ~size_t(127);
       return q;
     };
-    s.xk = reinterpret_cast<float*>(take(sizeof(float) * MR * D));
+    ring.buf = take((size_t)a.stages * kPStage);
+    s.x = reinterpret_cast<float*>(take(sizeof(float) * MR * D));
     s.xs = reinterpret_cast<bf16*>(take(sizeof(bf16) * MR * KP));
-    s.y = reinterpret_cast<float*>(take(sizeof(float) * MR * D));
-    s.sc = reinterpret_cast<float*>(take(sizeof(float) * MR * a.chunk_cap));
+    unsigned char* shared_sc = take(max(sizeof(float) * MR * a.chunk_cap, sizeof(bf16) * MR * FP));
+    s.sc = reinterpret_cast<float*>(shared_sc);
+    s.hs = reinterpret_cast<bf16*>(shared_sc);
     s.qh = reinterpret_cast<float*>(take(sizeof(float) * MR * kHeadDim));
-    s.kn = reinterpret_cast<float*>(take(sizeof(float) * MR * kHeadDim));
-    s.vn = reinterpret_cast<float*>(take(sizeof(float) * MR * kHeadDim));
-    s.loc = reinterpret_cast<float*>(take(sizeof(float) * MR * kQkvLocal));
-    s.ov = reinterpret_cast<float*>(take(sizeof(float) * MR * kHeadDim));
-    s.stat = reinterpret_cast<float*>(take(sizeof(float) * MR * 2));
-    s.av = reinterpret_cast<float*>(take(sizeof(float) * MR * kDimsLocal));
-    s.hid = reinterpret_cast<float*>(take(sizeof(float) * MR * a.units));
+    s.oh = reinterpret_cast<float*>(take(sizeof(float) * MR * kHeadDim));
+    s.xch0 = reinterpret_cast<float*>(take(sizeof(float) * 2 * kPClus * MR * 2));
+    s.xch1 = reinterpret_cast<float*>(take(sizeof(float) * 2 * kPClus * MR * kHeadDim));
     s.red = reinterpret_cast<float*>(take(sizeof(float) * kPWarps * kHeadDim));
   }
-  trace_mark(a, kTraceSlots - 1);
-  prefetch_phase(a, 0, 0, rank, ci, nclusters);
-  // Distributed shared memory is only touched after a cluster barrier.
-  cluster.sync();
-  unsigned target = 0;
-  // A prefill chunk reads K/V that other CTAs of the cluster wrote in this
-  // launch through global memory; a decode row only its own new key/value,
-  // which travel through shared memory.
-  const bool prefill = a.rm.prefill != 0;
-
-  for (int l = 0; l < a.L; ++l) {
-    const PLayer& W = a.layers[l];
-    const bool kv_only = !a.logits && l == a.L - 1;
-    const int tb = l * 40;
-    trace_mark(a, tb + 0);
-    // ---------------- phase A
-    if (l == 0)
-      combine_ln<KCH, MR>(a, s, nullptr, 0, nullptr, a.emb_g, a.emb_b, true);
-    else
-      combine_ln<KCH, MR>(a, s, a.part_f, nclusters, a.layers[l - 1].b2, a.layers[l - 1].ln_final_g,
-                          a.layers[l - 1].ln_final_b, false);
-    trace_mark(a, tb + 1);
-    for (int h = ci; h < H; h += nclusters) {
-      const int r0 = rank * kQkvLocal;
-      // this CTA's 48 of the head's 192 rows (q 0-63, k 64-127, v 128-191):
-      // warp w owns local rows w + 8k, all six loaded before any is used
-      constexpr int RW = kQkvLocal / kPWarps;
-      {
-        const int pass = 0;
-        uint4 w[RW][KCH];
-        int rows[RW];
-#pragma unroll
-        for (int k = 0; k < RW; ++k) {
-          const int li = r0 + warp + (pass * RW + k) * kPWarps;
-          rows[k] = (li / kHeadDim) * D + h * kHeadDim + li % kHeadDim;
-#pragma unroll
-          for (int c = 0; c < KCH; ++c) {
-            const int col = c * 256 + lane * 8;
-            w[k][c] = col < D ? ld_w(W.wqkv + (size_t)rows[k] * D + col) : make_uint4(0, 0, 0, 0);
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < RW; ++k) {
-          const int i = warp + (pass * RW + k) * kPWarps;
-          const int li = r0 + i;
-          const int part = li / kHeadDim, d = li % kHeadDim;
-          const float bias = __bfloat162float(W.bqkv[rows[k]]);
-#pragma unroll
-          for (int m = 0; m < MR; ++m) {
-            float acc = 0.f;
-#pragma unroll
-            for (int c = 0; c < KCH; ++c)
-              acc += dot8(w[k][c], *reinterpret_cast<const uint4*>(s.xs + (size_t)m * KP + c * 256 + lane * 8));
-            acc = warp_sum(acc);
-            if (lane == m && m < a.M) {
-              const float val = round_bf16(acc + bias);
-              s.loc[m * kQkvLocal + i] = val;
-              if (part > 0 && row_active(a.rm, a.st, m)) {
-                bf16* dst = part == 1 ? W.kpool : W.vpool;
-                dst[paged_offset(a.st.page_table, a.pps, H, row_slot(a.rm, m), h, row_pos(a.rm, a.st, m)) + d] =
-                    __float2bfloat16_rn(val);
-              }
-            }
-          }
-        }
-      }
-      if (prefill) __threadfence();
-      cluster.sync();  // q, k, v rows of the cluster visible
-      trace_mark(a, tb + 2);
-      for (int idx = tid; idx < a.M * 3 * kHeadDim; idx += kPThreads) {
-        const int m = idx / (3 * kHeadDim), li = idx % (3 * kHeadDim);
-        const float v = cluster.map_shared_rank(s.loc, li / kQkvLocal)[m * kQkvLocal + li % kQkvLocal];
-        float* dst = li < kHeadDim ? s.qh : li < 2 * kHeadDim ? s.kn : s.vn;
-        dst[m * kHeadDim + li % kHeadDim] = v;
-      }
-      __syncthreads();
-      if (kv_only) continue;
-      KeySrc src{false, !prefill, W.kpool, W.vpool, a.st.page_table, a.pps, H, a.F};
-      cluster_attention<MR>(a, cluster, s, src, h);
-      trace_mark(a, tb + 3);
-      axpy_rows<MR>(W.woT, D, h * kHeadDim + rank * kDimsLocal, kDimsLocal, s.av, kDimsLocal, a.M, s.y);
-      cluster.sync();
-      cluster_reduce_y<MR>(cluster, s, D, a.M, a.part_o + (size_t)h * a.M * D);
-      cluster.sync();  // peers finished reading y and loc before they are reused
-      trace_mark(a, tb + 4);
-    }
-    if (kv_only) break;
-    prefetch_phase(a, 1, l, rank, ci, nclusters);
-    grid_barrier(a, target);
-    trace_mark(a, tb + 5);
-    // ---------------- phase B
-    combine_ln<KCH, MR>(a, s, a.part_o, H, W.bo, W.ln_self_g, W.ln_self_b, false);
-    trace_mark(a, tb + 6);
-    for (int h = ci; h < H; h += nclusters) {
-      const int r0 = h * kHeadDim + rank * kDimsLocal;
-      gemv_rows<KCH, MR>(W.wcq, D, r0, r0 + kDimsLocal, s.xs, a.M, [&](int m, int row, float acc) {
-        s.loc[m * kQkvLocal + (row - r0)] = round_bf16(acc + __bfloat162float(W.bcq[row]));
-      });
-      cluster.sync();
-      trace_mark(a, tb + 7);
-      for (int idx = tid; idx < a.M * kHeadDim; idx += kPThreads) {
-        const int m = idx / kHeadDim, d = idx % kHeadDim;
-        s.qh[idx] = cluster.map_shared_rank(s.loc, d / kDimsLocal)[m * kQkvLocal + d % kDimsLocal];
-      }
-      __syncthreads();
-      KeySrc src{true, false, W.ck, W.cv, a.st.page_table, a.pps, H, a.F};
-      cluster_attention<MR>(a, cluster, s, src, h);
-      trace_mark(a, tb + 8);
-      axpy_rows<MR>(W.wcoT, D, h * kHeadDim + rank * kDimsLocal, kDimsLocal, s.av, kDimsLocal, a.M, s.y);
-      cluster.sync();
-      cluster_reduce_y<MR>(cluster, s, D, a.M, a.part_c + (size_t)h * a.M * D);
-      cluster.sync();
-      trace_mark(a, tb + 9);
-    }
-    prefetch_phase(a, 2, l, rank, ci, nclusters);
-    grid_barrier(a, target);
-    trace_mark(a, tb + 10);
-    // ---------------- phase C
-    combine_ln<KCH, MR>(a, s, a.part_c, H, W.bco, W.ln_cross_g, W.ln_cross_b, false);
-    trace_mark(a, tb + 11);
-    {
-      const int u0 = blockIdx.x * a.units;
-      const int u1 = min(a.FFN, u0 + a.units);
-      for (int idx = tid; idx < MR * a.units; idx += kPThreads) s.hid[idx] = 0.f;
-      __syncthreads();
-      gemv_rows<KCH, MR>(W.w1, D, u0, u1, s.xs, a.M, [&](int m, int row, float acc) {
-        const float v = round_bf16(acc + __bfloat162float(W.b1[row]));
-        s.hid[m * a.units + (row - u0)] = round_bf16(gelu_erf(v));
-      });
-      __syncthreads();
-      trace_mark(a, tb + 12);
-      axpy_rows<MR>(W.w2T, D, u0, max(0, u1 - u0), s.hid, a.units, a.M, s.y);
-      cluster.sync();
-      cluster_reduce_y<MR>(cluster, s, D, a.M, a.part_f + (size_t)ci * a.M * D);
-      cluster.sync();
-    }
-    trace_mark(a, tb + 13);
-    if (l + 1 < a.L)
-      prefetch_phase(a, 0, l + 1, rank, ci, nclusters);
-    else if (a.logits)
-      prefetch_phase(a, 3, l, rank, ci, nclusters);
-    grid_barrier(a, target);
-    trace_mark(a, tb + 14);
-  }
-
-  if (a.logits) {
-    // ---------------- logits: residual + final_norm, vocabulary slice, grammar mask, argmax
-    const PLayer& last = a.layers[a.L - 1];
-    combine_ln<KCH, MR>(a, s, a.part_f, nclusters, last.b2, last.ln_final_g, last.ln_final_b, false);
-    trace_mark(a, 40 * a.L);
-    __shared__ uint32_t rule[kPMaxRows];
-    __shared__ unsigned long long wbest[kPWarps][kPMaxRows];
-    __shared__ int is_last;
-    if (tid < MR) rule[tid] = tid < a.M ? (a.gr.kind == 1 ? (uint32_t)a.st.g[tid] : class_mask(a.st, tid)) : 0u;
-    __syncthreads();
-    unsigned long long best[MR];
-#pragma unroll
-    for (int m = 0; m < MR; ++m) best[m] = 0ull;
-    for (int v0 = blockIdx.x * kPWarps + warp; v0 < a.V; v0 += 2 * gridDim.x * kPWarps) {
-      const int v1 = v0 + gridDim.x * kPWarps;
-      uint4 w[2][KCH];
-#pragma unroll
-      for (int c = 0; c < KCH; ++c) {
-        const int col = c * 256 + lane * 8;
-        w[0][c] = col < D ? ld_w(a.emb + (size_t)v0 * D + col) : make_uint4(0, 0, 0, 0);
-        w[1][c] = (col < D && v1 < a.V) ? ld_w(a.emb + (size_t)v1 * D + col) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int v = k == 0 ? v0 : v1;
-        if (v >= a.V) continue;
-        const float bias = a.bias ? a.bias[v] : 0.f;
-        const int cls = a.gr.kind == 1 ? 0 : a.gr.token_class[v];
-#pragma unroll
-        for (int m = 0; m < MR; ++m) {
-          float acc = 0.f;
-#pragma unroll
-          for (int c = 0; c < KCH; ++c)
-            acc += dot8(w[k][c], *reinterpret_cast<const uint4*>(s.xs + (size_t)m * KP + c * 256 + lane * 8));
-          acc = warp_sum(acc);
-          if (m < a.M) {
-            const float logit = round_bf16(acc);
-            if (a.logits_out && lane == 0) a.logits_out[(size_t)m * a.V + v] = logit;
-            const bool allowed =
-                a.gr.kind == 1 ? a.gr.table[(size_t)rule[m] * a.V + v] != 0 : ((rule[m] >> cls) & 1u) != 0;
-            if (allowed) {
-              const unsigned long long key = argmax_key(logit + bias, v);
-              best[m] = key > best[m] ? key : best[m];
-            }
-          }
-        }
-      }
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int m = 0; m < MR; ++m) wbest[warp][m] = best[m];
-    }
-    __syncthreads();
-    if (tid < a.M) {
-      unsigned long long k = 0ull;
-      for (int w = 0; w < kPWarps; ++w) k = wbest[w][tid] > k ? wbest[w][tid] : k;
-      if (k) atomicMax(a.keys + tid, k);
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (is_last) {
-      __threadfence();
-      const bool failed = *(volatile int*)a.err != 0;  // a barrier gave up: leave the slots as they were
-      for (int sl = tid; sl < a.M; sl += kPThreads) {
-        const unsigned long long k = atomicExch(a.keys + sl, 0ull);
-        if (failed) continue;
-        const int64_t greedy = k ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
-        if (a.greedy_out) a.greedy_out[sl] = greedy;
-        const bool active = a.st.finished[sl] == 0;
-        const int64_t tok = a.st.token[sl], pos = a.st.position[sl];
-        int64_t choice = greedy;
-        if (a.forced && a.forced[sl] >= 0) choice = a.forced[sl];
-        if (!active) choice = tok;
-        const int64_t new_pos = active ? pos + 1 : pos;
-        if (active && new_pos < a.T) a.st.out[(size_t)sl * a.T + new_pos] = choice;
-        grammar_update(a.gr, a.st, sl, choice, active, new_pos >= a.T - 1);
-        a.st.token[sl] = choice;
-        a.st.position[sl] = new_pos;
-      }
-      if (tid == 0) *a.counter = 0u;
-    }
-  }
-  trace_mark(a, 40 * a.L + 2);
-  // Leave: the last CTA out resets the barrier counters for the next launch.
-  __syncthreads();
+  ring.full = full;
+  ring.empty = empty;
+  ring.stages = a.stages;
   if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
-      atomicExch(a.bar, 0u);
-      atomicExch(a.bar + 1, 0u);
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kPWarps);
+    }
+    mbar_init(&xbar[0], kPClus);
+    mbar_init(&xbar[1], kPClus);
+    failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  trace_mark(a, kTraceSlots - 1);
+  cluster.sync();  // barriers initialised everywhere before any copy or remote arrival
+
+  if (warp == kPWarps) {
+    // ======================================================== producer warp
+    if ((tid & 31) == 0) {
+      Producer pr;
+      pr.a = &a;
+      pr.ring = ring;
+      int r0, r1;
+      for (int l = 0; l < a.L; ++l) {
+        const PLayer& W = a.layers[l];
+        const bool kv_only = !a.logits && l == a.L - 1;
+        row_slice(3 * D, r0, r1);
+        pr.rows(W.wqkv, D, r0, r1);
+        if (kv_only) break;
+        for (int phase = 0; phase < 2; ++phase) {
+          const bool cross = phase == 1;
+          for (int h = ci; h < H; h += nclusters) {
+            for (int m = 0; m < a.M; ++m) pr.keys(W, cross, false, h, key_range(a, m, cross, rank));
+            for (int m = 0; m < a.M; ++m) pr.keys(W, cross, true, h, key_range(a, m, cross, rank));
+            const int per = D / kPClus;
+            pr.rows((cross ? W.wco_hb : W.wo_hb) + (size_t)h * D * kHeadDim, kHeadDim, rank * per, rank * per + per);
+          }
+          if (!cross) {
+            row_slice(D, r0, r1);
+            pr.rows(W.wcq, D, r0, r1);
+          }
+        }
+        row_slice(a.FFN, r0, r1);
+        pr.rows(W.w1, D, r0, r1);
+        row_slice(D, r0, r1);
+        pr.rows(W.w2, a.FFN, r0, r1);
+      }
+      if (a.logits) {
+        row_slice(a.V, r0, r1);
+        pr.rows(a.emb, D, r0, r1);
+      }
+      pr.drain();
+    }
+    __syncwarp();
+  } else {
+    // ======================================================== consumer warps
+    Consumer cs;
+    cs.a = &a;
+    cs.ring = ring;
+    cs.failed = &failed;
+    unsigned target = 0;
+    int uses[2] = {0, 0};
+    int r0, r1;
+    for (int l = 0; l < a.L; ++l) {
+      const PLayer& W = a.layers[l];
+      const bool kv_only = !a.logits && l == a.L - 1;
+      const int tb = l * 8;
+      trace_mark(a, tb + 0);
+      // ---------------- P1: (embedding) + LayerNorm, QKV rows, K/V append
+      if (l == 0)
+        combine_ln<MR>(a, s, KP, 0, nullptr, nullptr, a.emb_g, a.emb_b);
+      else
+        combine_ln<MR>(a, s, KP, 1, nullptr, nullptr, a.layers[l - 1].ln_final_g, a.layers[l - 1].ln_final_b);
+      row_slice(3 * D, r0, r1);
+      gemv_stream<MR>(cs, D, r0, r1, s.xs, KP, a.M, [&](int m, int row, float acc) {
+        const float v = acc + __bfloat162float(W.bqkv[row]);
+        if (row < D) {
+          a.q[(size_t)m * D + row] = __float2bfloat16_rn(v);
+        } else if (row_active(a.rm, a.st, m)) {
+          const int c = row - D, which = c >= D, cc = which ? c - D : c;
+          bf16* dst = which ? W.vpool : W.kpool;
+          dst[paged_offset(a.st.page_table, a.pps, H, row_slot(a.rm, m), cc / kHeadDim, row_pos(a.rm, a.st, m)) +
+              cc % kHeadDim] = __float2bfloat16_rn(v);
+        }
+      });
+      grid_barrier(a, target, &ok_s);
+      if (kv_only) break;
+      trace_mark(a, tb + 1);
+      // ---------------- P2: self-attention + out-projection partials
+      for (int h = ci; h < H; h += nclusters)
+        head_attention<MR>(a, W, cluster, s, cs, false, h, a.part_o, xbar, uses);
+      grid_barrier(a, target, &ok_s);
+      trace_mark(a, tb + 2);
+      // ---------------- P3: residual + self_attn_norm, cross q rows
+      combine_ln<MR>(a, s, KP, 2, a.part_o, W.bo, W.ln_self_g, W.ln_self_b);
+      row_slice(D, r0, r1);
+      gemv_stream<MR>(cs, D, r0, r1, s.xs, KP, a.M, [&](int m, int row, float acc) {
+        a.q[(size_t)m * D + row] = __float2bfloat16_rn(acc + __bfloat162float(W.bcq[row]));
+      });
+      grid_barrier(a, target, &ok_s);
+      trace_mark(a, tb + 3);
+      // ---------------- P4: cross-attention + cross out-projection partials
+      for (int h = ci; h < H; h += nclusters)
+        head_attention<MR>(a, W, cluster, s, cs, true, h, a.part_c, xbar, uses);
+      grid_barrier(a, target, &ok_s);
+      trace_mark(a, tb + 4);
+      // ---------------- P5: residual + cross_attn_norm, fc1 rows + GELU
+      combine_ln<MR>(a, s, KP, 2, a.part_c, W.bco, W.ln_cross_g, W.ln_cross_b);
+      row_slice(a.FFN, r0, r1);
+      gemv_stream<MR>(cs, D, r0, r1, s.xs, KP, a.M, [&](int m, int row, float acc) {
+        const float v = round_bf16(acc + __bfloat162float(W.b1[row]));
+        a.hid[(size_t)m * a.FFN + row] = __float2bfloat16_rn(gelu_erf(v));
+      });
+      grid_barrier(a, target, &ok_s);
+      trace_mark(a, tb + 5);
+      // ---------------- P6: fc2 rows, r = x + bf16(fc2 + bias)
+      for (int idx = tid; idx < MR * (FP / 8); idx += kPConsumers) {
+        const int m = idx / (FP / 8), col = (idx % (FP / 8)) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (m < a.M && col < a.FFN) v = __ldcg(reinterpret_cast<const uint4*>(a.hid + (size_t)m * a.FFN + col));
+        *reinterpret_cast<uint4*>(s.hs + (size_t)m * FP + col) = v;
+      }
+      csync();
+      row_slice(D, r0, r1);
+      gemv_stream<MR>(cs, a.FFN, r0, r1, s.hs, FP, a.M, [&](int m, int row, float acc) {
+        a.r[(size_t)m * D + row] = s.x[(size_t)m * D + row] + round_bf16(acc + __bfloat162float(W.b2[row]));
+      });
+      grid_barrier(a, target, &ok_s);
+      trace_mark(a, tb + 6);
+    }
+
+    if (a.logits) {
+      // ---------------- logits: final_norm, vocabulary slice, grammar mask, argmax
+      const PLayer& last = a.layers[a.L - 1];
+      combine_ln<MR>(a, s, KP, 1, nullptr, nullptr, last.ln_final_g, last.ln_final_b);
+      if (tid < MR) rule[tid] = tid < a.M ? row_rule(a.gr, a.st, tid) : 0u;
+      csync();
+      unsigned long long best[MR];
+#pragma unroll
+      for (int m = 0; m < MR; ++m) best[m] = 0ull;
+      row_slice(a.V, r0, r1);
+      gemv_stream<MR>(cs, D, r0, r1, s.xs, KP, a.M, [&](int m, int v, float acc) {
+        const float logit = round_bf16(acc);
+        if (a.logits_out) a.logits_out[(size_t)m * a.V + v] = logit;
+        if (token_allowed(a.gr, rule[m], a.V, v)) {
+          const unsigned long long key = argmax_key(rescore_logit(a.rs, a.st, m, v, logit + (a.bias ? a.bias[v] : 0.f)), v);
+          best[m] = key > best[m] ? key : best[m];
+        }
+      });
+      // lane m of each warp holds row m's best key
+      const int lane = tid & 31;
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
+        if (lane == m) wbest[warp][m] = best[m];
+      csync();
+      if (tid < a.M) {
+        unsigned long long k = 0ull;
+        for (int w = 0; w < kPWarps; ++w) k = wbest[w][tid] > k ? wbest[w][tid] : k;
+        if (k) atomicMax(a.keys + tid, k);
+      }
+      __threadfence();
+      csync();
+      if (tid == 0) is_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+      csync();
+      if (is_last) {
+        __threadfence();
+        const bool bad = *(volatile int*)a.err != 0;  // a wait gave up: leave the slots as they were
+        for (int sl = tid; sl < a.M; sl += kPConsumers) {
+          const unsigned long long k = atomicExch(a.keys + sl, 0ull);
+          if (bad) continue;
+          const int64_t greedy = key_token(k);
+          if (a.greedy_out) a.greedy_out[sl] = greedy;
+          const bool active = a.st.finished[sl] == 0;
+          const int64_t tok = a.st.token[sl], pos = a.st.position[sl];
+          int64_t choice = greedy;
+          if (a.forced && a.forced[sl] >= 0) choice = a.forced[sl];
+          if (!active) choice = tok;
+          const int64_t new_pos = active ? pos + 1 : pos;
+          if (active && new_pos < a.T) a.st.out[(size_t)sl * a.T + new_pos] = choice;
+          grammar_update(a.gr, a.st, sl, choice, active, new_pos >= a.T - 1);
+          rescore_commit(a.rs, a.gr, sl, choice, active);
+          a.st.token[sl] = choice;
+          a.st.position[sl] = new_pos;
+        }
+        if (tid == 0) *a.counter = 0u;
+      }
+    }
+    trace_mark(a, 8 * a.L + 1);
+    // the last CTA out resets the barrier counters for the next launch
+    csync();
+    if (tid == 0) {
+      __threadfence();
+      if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
+        atomicExch(a.bar, 0u);
+        atomicExch(a.bar + 1, 0u);
+      }
     }
   }
-  cluster.sync();  // no CTA leaves while a peer may still read its shared memory
+  cluster.sync();  // no CTA leaves while a peer may still write into its shared memory
 }
 
 }  // namespace s2r

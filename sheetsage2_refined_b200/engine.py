@@ -12,8 +12,9 @@ construction raises ``RuntimeError``.
 
 Differences from the reference, all outside the numerics of a step:
 
-* ``frame_weight`` rescoring (engine.py:81-116,318-347,358-369) is not
-  implemented; a non-zero weight raises ``NotImplementedError``.
+* ``frame_weight`` rescoring (engine.py:81-116,318-347,358-369) needs the
+  class grammar (the real vocabulary); ``load``'s ``frame_logp`` tables are
+  copied into the engine per slot.
 * ``grammar=`` accepts a grammar descriptor (``ClassGrammar`` or
   ``TableGrammar``) instead of building ``TokenGrammar(vocab, prompts)``;
   ``load(..., target=n)`` sets the table grammar's target length.
@@ -33,8 +34,12 @@ import torch
 
 from . import _lib
 from .grammar import ENDED, ClassGrammar
-from .vocab_table import FULL_PROMPTS, NO_KEY, OUT
+from .vocab_table import FULL_PROMPTS, NO_CHORD, NO_KEY, OUT, meter_tables
 from .weights import DecoderConfig, param_layout
+
+# Width of each frame table row (engine.py:97).
+FRAME_WIDTHS = {"root": 12, "bass": 12, "detail": NO_CHORD, "quality": NO_CHORD, "key": 24, "key_boundary": 1,
+                "downbeat": 1, "meter": 16}
 
 # Terms a frame head can rescore (engine.py:29-38).
 FRAME_TERMS = {
@@ -112,8 +117,6 @@ class BatchDecoder:
         self.mode_bias = mode_bias if "key_mode" in prompts else None
         self.frame_weight = frame_terms(frame_weight, prompts)
         self.rescore = any(self.frame_weight)
-        if self.rescore:
-            raise NotImplementedError("frame-head rescoring (frame_weight) is not implemented by the B200 engine")
 
         keep: list = []
         state = decoder.state_dict()
@@ -168,6 +171,8 @@ class BatchDecoder:
             bias[start : start + NO_KEY] = np.repeat(np.asarray(self.mode_bias, np.float32), 12)  # engine.py:79-80
             self._bias = bias
             _lib.check(lib.s2r_set_logit_bias(ctx, bias.ctypes.data))
+        if self.rescore:
+            self._set_rescore(vocab)
 
         self.state = {name: self._view(name) for name in (
             "in_shift", "shift_run", "payload", "last_field", "incomplete", "finished", "ended", "token",
@@ -178,6 +183,49 @@ class BatchDecoder:
         self.out = self._view("out").view(batch, self.max_tokens)
         self.bound = [0] * batch
         self.loaded = [False] * batch
+
+    def _set_rescore(self, vocab) -> None:
+        """The rescoring configuration of engine.py:81-116 for the C ABI."""
+
+        if vocab is None or self.grammar.kind != 0:
+            raise ValueError("frame-head rescoring needs the real vocabulary and its class grammar")
+        beats, units = meter_tables()
+        self._meter = (np.ascontiguousarray(beats, np.int32), np.ascontiguousarray(units, np.int32))
+        rs = _lib.Rescore()
+        for i, w in enumerate(self.frame_weight):
+            rs.weight[i] = w
+        spans = {"bass_span": "chord_bass", "key_span": "key", "eighth_span": "eighth_position", "meter_span": "meter"}
+        for field, block in spans.items():
+            getattr(rs, field)[0], getattr(rs, field)[1] = vocab.start[block], vocab.end[block]
+        rs.detail_span[0] = vocab.start["chord_detail"]
+        rs.detail_span[1] = vocab.start["chord_detail"] + NO_CHORD
+        rs.meter_beats, rs.meter_unit = self._meter[0].ctypes.data, self._meter[1].ctypes.data
+        rs.time_hz = int(vocab.time_hz)
+        _lib.check(self._lib.s2r_set_rescore(self._ctx, C.byref(rs)))
+
+    def _load_frame_tables(self, slot: int, frame_logp) -> None:
+        """Copy the window's frame tables (engine.py:218-224) into the engine."""
+
+        frame_logp = frame_logp or {}
+        ptrs = (C.c_void_p * len(FRAME_TERMS))()
+        rows = (C.c_int32 * len(FRAME_TERMS))()
+        keep = []
+        for i, name in enumerate(FRAME_TERMS):
+            if name not in frame_logp:
+                continue
+            t = frame_logp[name]
+            t = t.detach() if isinstance(t, torch.Tensor) else torch.from_numpy(np.asarray(t))
+            t = t.to(dtype=torch.float32)
+            if t.is_cuda and t.device != self.device:
+                t = t.to(self.device)
+            t = t.contiguous()
+            width = FRAME_WIDTHS[name]
+            if tuple(t.shape[1:]) != ((width,) if width > 1 else ()):
+                raise ValueError(f"frame table {name!r} has shape {tuple(t.shape)}; expected [frames{', %d' % width if width > 1 else ''}]")
+            keep.append(t)
+            ptrs[i], rows[i] = t.data_ptr(), t.shape[0]
+        _lib.check(self._lib.s2r_load_frame_tables(self._ctx, slot, ptrs, rows, self._stream()))
+        self._keep_tables = keep  # copies are ordered on the stream; keep the sources alive
 
     # ------------------------------------------------------------ plumbing
     def _view(self, name: str) -> torch.Tensor:
@@ -227,8 +275,6 @@ class BatchDecoder:
              frame_logp=None, target: int | None = None) -> None:
         """Start ``slot`` on a window (engine.py:180-232): ``memory`` ``[1, F, D]`` or ``[F, D]``."""
 
-        if frame_logp and self.rescore:
-            raise NotImplementedError("frame-head rescoring is not implemented by the B200 engine")
         frames = self.frames if frames is None else frames
         if isinstance(memory, np.ndarray):
             memory = torch.from_numpy(memory)
@@ -244,6 +290,8 @@ class BatchDecoder:
         toks = (C.c_int64 * len(prefix))(*[int(t) for t in prefix])
         stop = float("inf") if stop_seconds is None else float(stop_seconds)
         tgt = _lib.S2R_NO_TARGET if target is None else int(target)
+        if self.rescore:
+            self._load_frame_tables(slot, frame_logp)
         _lib.check(self._lib.s2r_load_slot(self._ctx, slot, C.c_void_p(mem.data_ptr()), dtype, mem.shape[0], frames,
                                            toks, len(prefix), stop, tgt, self._stream()))
         self._keep_memory = mem  # the copy into the engine is ordered on the stream; keep the source alive

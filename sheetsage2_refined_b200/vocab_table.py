@@ -50,6 +50,22 @@ NO_KEY = 108
 SWING_CAPACITY = 32
 
 
+def meter_tables() -> tuple[list[int], list[int]]:
+    """Per meter token: bar-length class ``min(numerator, 16) - 1`` and beat unit.
+
+    The meters are every numerator 1..32 with every denominator of (1, 2, 4,
+    8, 16, 32), numerator-major (vocab.py:64); frame-head rescoring reads both
+    (engine.py:103-105).
+    """
+
+    beats, units = [], []
+    for numerator in range(1, 33):
+        for denominator in (1, 2, 4, 8, 16, 32):
+            beats.append(min(numerator, 16) - 1)
+            units.append(denominator)
+    return beats, units
+
+
 class VocabTable:
     """Block layout of the token vocabulary (``vocab.Vocab``, vocab.py:157-187).
 
