@@ -23,6 +23,9 @@ Files:
   two prompt sets, stop seconds and a mode bias.
 * ``grammar_trace.npz`` — ``TokenGrammar`` state after every token of seeded
   random walks through the allowed tokens (EOS included), per prompt set.
+* ``rescore.npz``       — real vocabulary with every frame-head rescoring
+  term switched on: seeded per-frame tables, two slots (one with a prefix
+  that states a time, a meter and a key), greedy tokens and end reasons.
 """
 
 from __future__ import annotations
@@ -172,6 +175,31 @@ def make_real():
 
 
 @torch.no_grad()
+def make_rescore():
+    vocab = Vocab()
+    decoder = ref_decoder(sc.REAL_TINY, sc.REAL_SEED)
+    out = {}
+    for case, weights in sc.RESCORE_CASES.items():
+        engine = BatchDecoder(decoder, vocab, batch=2, frames=sc.REAL_FRAMES, prompts=sc.RESCORE_PROMPTS,
+                              frame_weight=weights)
+        for slot, (prefix, stop, frames, rows, seed) in enumerate(sc.rescore_windows(vocab)):
+            tables = {k: torch.from_numpy(v) for k, v in sc.rescore_tables(rows, seed).items()}
+            memory = torch.from_numpy(memory_array(sc.REAL_FRAMES, sc.REAL_TINY.width, 61 + slot))
+            engine.load(slot, memory, prefix, stop, frames, frame_logp=tables)
+        for _ in range(60):
+            engine.run(4)
+            if len(engine.finished()) == 2:
+                break
+        for slot in (0, 1):
+            length = int(engine.state["position"][slot]) + 1
+            out[f"{case}_s{slot}_tokens"] = engine.out[slot, :length].numpy().copy()
+            out[f"{case}_s{slot}_ended"] = np.array(int(engine.state["ended"][slot]))
+            out[f"{case}_s{slot}_finished"] = np.array(bool(engine.state["finished"][slot]))
+            print("rescore", case, slot, length, bool(engine.state["finished"][slot]), int(engine.state["ended"][slot]))
+    np.savez_compressed(HERE / "rescore.npz", **out)
+
+
+@torch.no_grad()
 def make_trace():
     vocab = Vocab()
     out = {}
@@ -212,8 +240,12 @@ def make_trace():
 
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if sys.argv[1:] == ["rescore"]:  # only the rescoring fixture
+        make_rescore()
+        sys.exit(0)
     make_trace()
     make_single("c1_table.npz", sc.C1, sc.C1_SEED, sc.c1_grammar(), sc.C1_MEMORY_SEED, sc.C1_FRAMES, sc.C1_STEPS)
     make_batch()
     make_real()
     make_single("c2_head.npz", sc.C2, sc.C2_SEED, sc.c2_grammar(), sc.C2_MEMORY_SEED, sc.C2_FRAMES, 24)
+    make_rescore()

@@ -79,3 +79,79 @@ REAL_PROMPT_SETS = (
     FULL_PROMPTS,
     ("timestamp", "downbeat_meter", "chord_detail", "key_mode", "melody_vocal"),
 )
+
+
+# Frame-head rescoring: a prompt set that emits every rescored span (chord
+# detail, key, downbeat/meter) and two weight sets -- chord and key terms,
+# then meter and downbeat terms -- with seeded per-frame tables shaped as
+# transcribe.frame_tables makes them.
+RESCORE_PROMPTS = ("timestamp", "downbeat_meter", "key", "chord_detail")
+RESCORE_CASES = {
+    "chords": {"root": 0.5, "bass": 0.4, "detail": 0.3, "quality": 0.3, "key": 0.5, "key_boundary": 0.6},
+    "meters": {"downbeat": 2.0, "meter": 2.0, "key_boundary": 0.6},
+}
+
+
+def rescore_tables(rows: int, seed: int) -> dict:
+    """Seeded per-frame tables of every term, ``[rows, width]`` (``[rows]`` for the scalar terms).
+
+    Scores ~N(0, 3) rather than normalised log-probabilities, so that the
+    rescored spans outscore the rest of the vocabulary under random weights
+    and every term decides tokens; the meter table prefers long bars (16+
+    beats) so that meter changes happen.
+    """
+
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    widths = {"root": 12, "bass": 12, "detail": 744, "quality": 744, "key": 24, "key_boundary": 0, "downbeat": 0,
+              "meter": 16}
+    tables = {name: (rng.standard_normal((rows, w) if w else rows) * 3.0).astype(np.float32)
+              for name, w in widths.items()}
+    tables["meter"][:, 15] += 6.0
+    return tables
+
+
+def rescore_windows(vocab):
+    """(prefix, stop_seconds, frames, table rows, table seed) per slot.
+
+    Slot 1's prefix states a time (1.5 s), a 4/4 meter, bar position 0 and a
+    key, so the rescoring state starts from the prefix (engine.py:225-232).
+    """
+
+    prefix = vocab.prompt_prefix(RESCORE_PROMPTS)
+    stated = prefix + [vocab.start["time"] + 150, vocab.start["meter"] + 3 * 6 + 2, vocab.start["eighth_position"],
+                       vocab.start["key"] + 5]
+    return [(prefix, None, REAL_FRAMES, REAL_FRAMES, 71), (stated, None, 50, 40, 72)]
+
+
+def rescore_forced(engine, vocab, golden: dict, case: str, load) -> list[tuple[int, int, int]]:
+    """Force the reference's greedy tokens of a rescoring case through ``engine``.
+
+    Loads both windows of the case with their frame tables (``load(slot,
+    memory_seed, prefix, stop, frames, frame_logp)``), then at every step
+    forces each slot's next reference token and records ``(slot, engine's
+    greedy choice, reference's choice)`` while the slot is running.
+    """
+
+    import numpy as np
+
+    windows = rescore_windows(vocab)
+    seqs = [golden[f"{case}_s{slot}_tokens"].tolist() for slot in (0, 1)]
+    for slot, (prefix, stop, frames, rows, seed) in enumerate(windows):
+        load(slot, 61 + slot, prefix, stop, frames, rescore_tables(rows, seed))
+    starts = [len(w[0]) for w in windows]
+    steps = max(len(s) - p for s, p in zip(seqs, starts))
+    record = []
+    for k in range(steps):
+        forced = np.full(getattr(engine, "batch", 2), -1, np.int64)
+        live = []
+        for slot in (0, 1):
+            if starts[slot] + k < len(seqs[slot]):
+                forced[slot] = seqs[slot][starts[slot] + k]
+                live.append(slot)
+        _, greedy = engine.step_debug(forced, want_logits=False) if hasattr(engine, "step_debug") else \
+            engine.step(forced=forced)
+        for slot in live:
+            record.append((slot, int(greedy[slot]), int(forced[slot])))
+    return record

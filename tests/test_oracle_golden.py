@@ -148,3 +148,26 @@ def test_c2_head_fp32():
     logits, greedy = teacher_forced_run(engine, tokens, 2, 24)
     assert np.abs(logits - g["logits"]).max() <= LOGIT_TOL_FP32
     assert greedy.tolist() == tokens[2:26]
+
+
+@pytest.mark.parametrize("case", list(sc.RESCORE_CASES))
+def test_rescore_oracle_vs_reference(case):
+    """Frame-head rescoring: the oracle (fp32) picks the reference's greedy token at every forced step."""
+
+    g = np.load(GOLDEN / "rescore.npz")
+    vocab = VocabTable()
+    from oracle.engine import FRAME_TERM_NAMES
+
+    weights = tuple(float(sc.RESCORE_CASES[case].get(n, 0.0)) for n in FRAME_TERM_NAMES)
+    eng = OracleEngine(sc.REAL_TINY, synthetic_state_dict(sc.REAL_TINY, sc.REAL_SEED),
+                       ClassGrammar(vocab, sc.RESCORE_PROMPTS), batch=2, frames=sc.REAL_FRAMES, mode="fp32",
+                       frame_weight=weights, vocab=vocab)
+
+    def load(slot, memory_seed, prefix, stop, frames, tables):
+        eng.load(slot, memory_array(sc.REAL_FRAMES, sc.REAL_TINY.width, memory_seed), prefix, stop, frames,
+                 frame_logp=tables)
+
+    record = sc.rescore_forced(eng, vocab, g, case, load)
+    same = sum(int(a == b) for _, a, b in record)
+    print(f"rescoring ({case}) oracle fp32 vs reference: {same}/{len(record)}")
+    assert same == len(record)
