@@ -1,6 +1,7 @@
 """Decoder token-loop throughput on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload single|batched]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload single|batched|box|long]
 
 Workloads (synthetic: seeded N(0, 0.02) weights, N(0, 1) encoder memory, a
 seeded 8-state table grammar allowing 25% of the vocabulary per state):
@@ -12,6 +13,10 @@ seeded 8-state table grammar allowing 25% of the vocabulary per state):
 * ``batched``: 64 slots of the same decoder, frames U[600, 3000], target
   lengths U[512, 4096], continuous batching with finished songs replaced; a
   step = 64 steps of the whole batch plus the refills they trigger.
+* ``box`` (C5): 512 such songs sharded by song over the ranks (longest first
+  onto the least-loaded rank); a step = the whole job.  Strong scaling.
+* ``long`` (C4): 16 slots, memory [16, 6000, 1024], 8192 tokens each; a step =
+  load and decode the 16 windows.
 
 Under torchrun every rank decodes its own songs on its own GPU (no
 collective on the data path; weak scaling) and ``value`` is the tokens of all
@@ -47,6 +52,7 @@ CONFIG = DecoderConfig(vocab_size=2048, width=1024, layers=12, heads=16, ffn_wid
 WEIGHT_SEED, MEMORY_SEED, GRAMMAR_SEED = 1, 101, 8
 SINGLE_FRAMES, SINGLE_TOKENS = 1500, 2048
 BATCH, BATCH_FRAMES = 64, 3000
+SONGS, SONGS_SEED = 512, 2024
 OVERRIDES: dict = {}  # profiling-case overrides of the workload, reported in "config"
 CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits", "step")
 
@@ -167,11 +173,16 @@ class CpuDecoder:
     def sample(self, seconds: float, min_tokens: int = 4):
         """Greedy tokens for ``seconds`` of decode; returns (tokens/s, tokens, cores)."""
 
-        n, t0 = 0, time.perf_counter()
-        while n < min_tokens or time.perf_counter() - t0 < seconds:
-            self.eng.step()
-            n += 1
-        return n / (time.perf_counter() - t0), n, os.cpu_count() or 1
+        from threadpoolctl import threadpool_limits
+
+        cores = os.cpu_count() or 1
+        # every host core, also under torchrun (which sets OMP_NUM_THREADS=1 per rank)
+        with threadpool_limits(limits=cores):
+            n, t0 = 0, time.perf_counter()
+            while n < min_tokens or time.perf_counter() - t0 < seconds:
+                self.eng.step()
+                n += 1
+            return n / (time.perf_counter() - t0), n, cores
 
 
 def run_reference(args, world, rank):
@@ -350,6 +361,157 @@ class Batched:
         pass
 
 
+class Box:
+    """C5: 512 songs (frames U[600, 3000], targets U[512, 4096], seeded) sharded by song.
+
+    ``shard.partition_songs`` gives every rank its songs, longest first onto
+    the least-loaded rank; each rank decodes its share with 64 slots and
+    continuous refill.  One bench step = the whole job (every song of the
+    rank decoded to its end); the warm-up is one short batched pass.
+    """
+
+    POLL = 32
+    scaling = "strong"  # the 512 songs are split over the ranks
+
+    def __init__(self, eng, torch, device, rank, world):
+        from sheetsage2_refined_b200.shard import partition_songs
+
+        self.eng, self.torch, self.device = eng, torch, device
+        rng = np.random.default_rng(SONGS_SEED)
+        self.frames = rng.integers(600, BATCH_FRAMES + 1, SONGS).tolist()
+        self.targets = rng.integers(512, 4097, SONGS).tolist()
+        self.share = partition_songs(self.targets, world)[rank]
+        gen = torch.Generator(device=device)
+        gen.manual_seed(MEMORY_SEED + rank)
+        self.pool = [torch.randn(BATCH_FRAMES, CONFIG.width, generator=gen, device=device).to(torch.bfloat16)
+                     for _ in range(4)]
+        self.pool_pinned = [m.cpu().pin_memory() for m in self.pool]
+        self.launches = 0
+        self.h2d_last = 0
+
+    def config(self, world):
+        return {"workload": f"{SONGS} songs sharded by song (LPT) over {world} GPU(s), 64 slots per GPU with "
+                            "refill, 12L d1024 h16 ffn4096 V2048, frames U[600,3000], targets U[512,4096]",
+                "global_batch": BATCH * world, "seq_len": 4096, "parallelism": f"song-sharded x{world}",
+                "l2": "inputs larger than L2 (weights and K/V streamed every step)"}
+
+    def _load(self, slot, song, pinned):
+        mem = (self.pool_pinned if pinned else self.pool)[song % len(self.pool)][: self.frames[song]]
+        self.eng.load(slot, mem, [SOS, OUT], None, self.frames[song], target=self.targets[song])
+        self.launches += load_launches(self.eng)
+        if pinned:
+            self.h2d_last += self.frames[song] * CONFIG.width * 2 + 16
+
+    def _job(self, songs, pinned):
+        queue, live, tokens = list(songs), {}, 0
+        self.h2d_last = 0
+        for slot in range(BATCH):
+            if queue:
+                live[slot] = queue.pop(0)
+                self._load(slot, live[slot], pinned)
+        while live:
+            self.eng.run(self.POLL)
+            self.launches += self.eng.step_launches * self.POLL
+            for slot in self.eng.finished():
+                tokens += len(self.eng.take(slot)[0]) - 3  # SOS, OUT and the closing EOS are not decoded tokens
+                del live[slot]
+                if queue:
+                    live[slot] = queue.pop(0)
+                    self._load(slot, live[slot], pinned)
+        return tokens
+
+    def warm_step(self):
+        return self._job(self.share[:BATCH], False)
+
+    def step_device(self):
+        return self._job(self.share, False)
+
+    def step_e2e(self):
+        return self._job(self.share, True)
+
+    @property
+    def h2d(self):
+        return self.h2d_last
+
+    @property
+    def d2h(self):
+        return 0
+
+    def prepare_profile(self):
+        for slot in range(BATCH):
+            self._load(slot, self.share[slot % len(self.share)], False)
+        self.eng.run(256)
+
+    def finish_profile(self):
+        self.eng.run(4096)
+        for slot in self.eng.finished():
+            self.eng.take(slot)
+
+
+class LongContext:
+    """C4: 16 slots, encoder memory [16, 6000, 1024], 8192 tokens each (split-K attention over long rows).
+
+    One bench step = load the 16 windows and decode 8192 tokens in every slot.
+    """
+
+    SLOTS, FRAMES, TOKENS = 16, 6000, 8192
+
+    def __init__(self, eng, torch, device, rank):
+        self.eng, self.torch, self.device = eng, torch, device
+        gen = torch.Generator(device=device)
+        gen.manual_seed(MEMORY_SEED + rank)
+        self.mem = torch.randn(self.FRAMES, CONFIG.width, generator=gen, device=device).to(torch.bfloat16)
+        self.mem_pinned = self.mem.cpu().pin_memory()
+        self.launches = 0
+        self.h2d = self.SLOTS * (self.FRAMES * CONFIG.width * 2 + 16)
+        self.d2h = self.SLOTS * (self.TOKENS + 3) * 8
+
+    def config(self, world):
+        return {"workload": "16 slots x 8192 tokens, encoder memory [16, 6000, 1024] bf16, 12L d1024 h16 ffn4096 "
+                            "V2048 (max_tokens 8200)", "global_batch": self.SLOTS * world, "seq_len": self.TOKENS,
+                "parallelism": f"song-sharded x{world}", "l2": "inputs larger than L2"}
+
+    def _run(self, mem):
+        for slot in range(self.SLOTS):
+            self.eng.load(slot, mem, [SOS, OUT], None, self.FRAMES, target=self.TOKENS)
+            self.launches += load_launches(self.eng)
+        self.eng.run(self.TOKENS)
+        self.launches += self.eng.step_launches * self.TOKENS
+        return self.SLOTS * self.TOKENS
+
+    def warm_step(self):
+        for slot in range(self.SLOTS):
+            self.eng.load(slot, self.mem, [SOS, OUT], None, self.FRAMES, target=64)
+        self.eng.run(64)
+        for slot in self.eng.finished():
+            self.eng.take(slot)
+        return 0
+
+    def step_device(self):
+        n = self._run(self.mem)
+        for slot in self.eng.finished():
+            self.eng.take(slot)
+        return n
+
+    def step_e2e(self):
+        n = self._run(self.mem_pinned)
+        done = self.eng.finished()
+        for slot in done:
+            self.eng.take(slot)
+        assert len(done) == self.SLOTS
+        return n
+
+    def prepare_profile(self):
+        for slot in range(self.SLOTS):
+            self.eng.load(slot, self.mem, [SOS, OUT], None, self.FRAMES, target=self.TOKENS)
+        self.eng.run(self.TOKENS // 2)
+
+    def finish_profile(self):
+        self.eng.run(self.TOKENS)
+        for slot in self.eng.finished():
+            self.eng.take(slot)
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -370,13 +532,20 @@ def run_b200(args, world, rank, local):
     if args.workload == "single":
         eng = BatchDecoder(dec, None, batch=1, frames=SINGLE_FRAMES, grammar=grammar, device=device, flags=flags)
         work = SingleSong(eng, torch, device, rank)
+    elif args.workload == "box":
+        eng = BatchDecoder(dec, None, batch=BATCH, frames=BATCH_FRAMES, grammar=grammar, device=device, flags=flags)
+        work = Box(eng, torch, device, rank, world)
+    elif args.workload == "long":
+        eng = BatchDecoder(dec, None, batch=LongContext.SLOTS, frames=LongContext.FRAMES, grammar=grammar,
+                           device=device, flags=flags)
+        work = LongContext(eng, torch, device, rank)
     else:
         eng = BatchDecoder(dec, None, batch=BATCH, frames=BATCH_FRAMES, grammar=grammar, device=device, flags=flags)
         work = Batched(eng, torch, device, rank)
 
     stream = torch.cuda.current_stream(device)
     for _ in range(args.warmup):  # warm-up (also captures the step graph)
-        work.step_device()
+        getattr(work, "warm_step", work.step_device)()
     torch.cuda.synchronize(device)
 
     # roofline: per-kernel times of one profiled step at a representative position
@@ -437,7 +606,7 @@ def run_b200(args, world, rank, local):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": getattr(work, "scaling", "weak"), "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**work.config(world), **({"profiling_overrides": OVERRIDES} if OVERRIDES else {})},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": work.h2d, "d2h_bytes_per_step": work.d2h},
             "gpu_launches": launches,
@@ -491,7 +660,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
-    ap.add_argument("--workload", default="single", choices=("single", "batched"))
+    ap.add_argument("--workload", default="single", choices=("single", "batched", "box", "long"))
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     # smaller cases of the same kernels for ncu captures that must fit a few GB (not bench lines)
@@ -507,6 +676,8 @@ def main():
     if args.batch_frames:
         BATCH_FRAMES = args.batch_frames
         OVERRIDES.update(batch_frames=BATCH_FRAMES)
+    if args.workload == "long":  # C4 decodes 8192 tokens: a longer position table
+        CONFIG = dataclasses.replace(CONFIG, max_tokens=max(CONFIG.max_tokens, 8200))
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)

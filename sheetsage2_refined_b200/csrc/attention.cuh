@@ -41,6 +41,7 @@ struct AttnArgs {
   int chunk_cap;  // score buffer length per CTA
   int splits;     // CTAs per (row, head): the cluster size the launch must have
   int* err;       // device error word: set (and the work skipped) on a broken invariant
+  const int32_t* order;  // [M] row of each grid z index (longest first), or null: identity
 };
 
 constexpr int kErrAttnCluster = 1;  // launched without the expected cluster shape
@@ -59,7 +60,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.dim_blocks().x;
   const int rank = (int)cluster.block_rank();
-  const int h = blockIdx.y, m = blockIdx.z;
+  const int h = blockIdx.y, m = a.order ? a.order[blockIdx.z] : (int)blockIdx.z;
   extern __shared__ __align__(16) float smem_f[];
   float* sc = smem_f;                                 // [chunk_cap] scores, then exp values
   float* part = smem_f + ((a.chunk_cap + 3) & ~3);    // [kAttnGroups][64] partial outputs

@@ -155,7 +155,12 @@ struct s2r_ctx {
   // when `tc` (16 or more slots), the cross K/V projection at load when `tc_cross`
   bool tc = false, tc_cross = false;
   int tc_nb = 64;                  // rows per MMA tile of the step and prefill projections
-  int attn_splits = 8;             // CTAs (one cluster) per (row, head) of the attention
+  int attn_splits = 8;             // CTAs (one cluster) per (row, head) of the self-attention
+  int attn_splits_cross = 8;       // ... and of the cross-attention
+  int32_t *order_self = nullptr, *order_cross = nullptr;  // [B] decode rows, longest first (tensor-core engines)
+  int32_t* h_order = nullptr;                             // pinned [2B] staging of both orders
+  cudaEvent_t order_copied = nullptr;                     // the last upload of h_order has run
+  std::vector<int32_t> h_frames;                          // real frames per slot
   bf16* xln = nullptr;             // [maxM][KP] LayerNorm'd rows, the X operand of LN'd projections
   bf16* mem_bf16 = nullptr;        // [F][D] float32 encoder memory rounded to bf16
   // profiling: when set, an event is recorded after every launch of a step
@@ -361,18 +366,42 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
 }
 
 // Every (row, head) of an engine is split over the same number of CTAs
-// (attn_splits) whatever the rows of the launch, so a row's result never
-// depends on how many rows share it (decode with any slots live and prefill
-// chunks give bit-identical K/V and outputs).  Engines of fewer than 16 slots
-// split 8 ways; tensor-core engines split so that the (row, head) pairs of a
-// full batch cover the SMs about four times.
+// (attn_splits, attn_splits_cross) whatever the rows of the launch, so a
+// row's result never depends on how many rows share it (decode with any
+// slots live and prefill chunks give bit-identical K/V and outputs).  Engines
+// of fewer than 16 slots split 8 ways; tensor-core engines split so that the
+// (row, head) pairs of a full batch cover the SMs about four times, and
+// twice that for the cross-attention, whose rows are long (every encoder
+// frame) and uneven.
 constexpr int kAttnSplits = 8;
 
-int attn_splits_for(const s2r_ctx* c) {
+int attn_splits_for(const s2r_ctx* c, int cover) {
   if (!c->tc) return kAttnSplits;
   int sp = 1;
-  while (sp < kAttnSplits && c->B * c->H * sp * 2 <= 4 * c->num_sms) sp *= 2;
+  while (sp < kAttnSplits && c->B * c->H * sp * 2 <= cover * c->num_sms) sp *= 2;
   return sp;
+}
+
+// Decode rows longest first (self: by position, cross: by real frames), so
+// that the attention CTAs of the longest rows start first and the short
+// ones fill in behind them.  Uploaded before each run; the order does not
+// change any row's result.
+int upload_row_order(s2r_ctx* c, cudaStream_t s) {
+  if (!c->order_self) return S2R_OK;
+  CK(cudaEventSynchronize(c->order_copied));  // the previous upload has left the staging buffer
+  int32_t* by_pos = c->h_order;
+  int32_t* by_frames = c->h_order + c->B;
+  for (int i = 0; i < c->B; ++i) by_pos[i] = by_frames[i] = i;
+  std::stable_sort(by_pos, by_pos + c->B, [&](int a, int b) {
+    return (c->loaded[a] ? c->bound[a] : -1) > (c->loaded[b] ? c->bound[b] : -1);
+  });
+  std::stable_sort(by_frames, by_frames + c->B, [&](int a, int b) {
+    return (c->loaded[a] ? c->h_frames[a] : -1) > (c->loaded[b] ? c->h_frames[b] : -1);
+  });
+  CK(cudaMemcpyAsync(c->order_self, by_pos, c->B * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(c->order_cross, by_frames, c->B * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  CK(cudaEventRecord(c->order_copied, s));
+  return S2R_OK;
 }
 
 int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s) {
@@ -390,9 +419,10 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   a.v = cross ? c->layers[layer].cv : c->layers[layer].vpool;
   a.pages_per_slot = c->pps;
   a.frames_cap = c->F;
-  a.splits = c->attn_splits;
+  const int C = cross ? c->attn_splits_cross : c->attn_splits;
+  a.splits = C;
   a.err = c->dev_error;
-  const int C = c->attn_splits;
+  a.order = rm.prefill ? nullptr : (cross ? c->order_cross : c->order_self);
   const int maxlen = cross ? c->F : c->T;
   a.chunk_cap = (maxlen + C - 1) / C;
   const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
@@ -952,7 +982,19 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   c->mem_stage = mem_stage;
   TRYC(dalloc(c, &c->prefill_tokens, kPrefillRows));
   TRYC(setup_tensor_core(c));
-  c->attn_splits = attn_splits_for(c);
+  c->attn_splits = attn_splits_for(c, 4);
+  c->attn_splits_cross = attn_splits_for(c, 8);
+  c->h_frames.assign(c->B, 0);
+  if (c->tc) {
+    TRYC(dalloc(c, &c->order_self, c->B));
+    TRYC(dalloc(c, &c->order_cross, c->B));
+    CK(cudaMallocHost(&c->h_order, 2 * (size_t)c->B * sizeof(int32_t)));
+    CK(cudaEventCreateWithFlags(&c->order_copied, cudaEventDisableTiming));
+    std::vector<int32_t> ident(c->B);
+    for (int i = 0; i < c->B; ++i) ident[i] = i;
+    CK(cudaMemcpy(c->order_self, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->order_cross, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
+  }
   TRYC(dalloc(c, &c->keys, c->B));
   TRYC(dalloc(c, &c->counter, 1));
   TRYC(dalloc(c, &c->dev_error, 1));
@@ -1059,6 +1101,8 @@ int32_t s2r_destroy(s2r_ctx* c) {
   cudaDeviceSynchronize();
   if (c->graph) cudaGraphExecDestroy(c->graph);
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
+  if (c->order_copied) cudaEventDestroy(c->order_copied);
+  if (c->h_order) cudaFreeHost(c->h_order);
   for (void* p : c->allocs) cudaFree(p);
   delete c;
   return S2R_OK;
@@ -1194,6 +1238,7 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
 
   SlotState& st = c->st;
   TRY(put<int32_t>(st.frames, slot, frames, s));
+  c->h_frames[slot] = frames;
   TRY(put<double>(st.stop, slot, stop_seconds, s));
   TRY(put<int64_t>(st.target, slot, target, s));
   TRY(put<int64_t>(st.g, slot, gs.g, s));
@@ -1281,6 +1326,7 @@ int32_t s2r_step(s2r_ctx* c, int32_t n_steps, void* stream) {
     TRY(grow_pages(c, slot, c->bound[slot], &changed));
     if (changed) TRY(upload_page_row(c, slot, s));
   }
+  TRY(upload_row_order(c, s));
   if (c->use_graph) {
     TRY(ensure_graph(c));
     for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(c->graph, s));
