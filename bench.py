@@ -611,7 +611,7 @@ def run_b200(args, world, rank, local):
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": work.h2d, "d2h_bytes_per_step": work.d2h},
             "gpu_launches": launches,
             "clocks": clock_summary,
-            "roofline": roofline(prof, peak, peak_kind),
+            "roofline": roofline(prof, peak, peak_kind, args.workload),
             "step_roofline": prof["step"],
             "kernel_classes": {k: {"us_per_launch": 1000.0 * v["ms"] / max(v["launches"], 1),
                                    "launches": v["launches"],
@@ -645,12 +645,24 @@ def profile(eng):
                                          "gbs": total_bytes / (total_ms * 1e-3) / 1e9}}
 
 
-def roofline(prof, peak, peak_kind):
+# DRAM traffic of the attention launches (dram__bytes_read.sum + dram__bytes_write.sum, one ncu
+# capture each; profiles/): per launch at the single-song workload's position ~1,024, and as a
+# ratio to the algorithmic bytes for the batched workload, whose launches are too large to
+# capture (a one-row launch of the same kernel on the small case; traffic grows with the rows'
+# keys, so the ratio carries over).
+NCU_TRAFFIC = {("single", "self_attn"): 4_244_480, ("single", "cross_attn"): 6_184_960}
+NCU_TRAFFIC_RATIO = {("batched", "cross_attn"): 3_097_088 / 3_096_576, ("batched", "self_attn"): 3_097_088 / 3_096_576}
+
+
+def roofline(prof, peak, peak_kind, workload):
     name, c = max(prof["classes"].items(), key=lambda kv: kv[1]["ms"])
     per_launch_s = c["ms"] / max(c["launches"], 1) / 1000.0
     achieved = c["bytes_per_launch"] / per_launch_s / 1e9
+    traffic = NCU_TRAFFIC.get((workload, name))
+    if traffic is None and (workload, name) in NCU_TRAFFIC_RATIO:
+        traffic = c["bytes_per_launch"] * NCU_TRAFFIC_RATIO[(workload, name)]
     return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-            "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+            "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
             "bytes_per_launch": c["bytes_per_launch"], "us_per_launch": per_launch_s * 1e6}
 
 

@@ -56,6 +56,14 @@ __device__ __forceinline__ const bf16* attn_row(const AttnArgs& a, const bf16* b
   return base + paged_offset(a.st.page_table, a.pages_per_slot, a.H, slot, h, j);
 }
 
+// kPrefetch: the first pass of keys and values (kAttnGroups * kAttnUnroll
+// keys of the CTA's range) is loaded into registers before the kernel waits
+// for the previous kernel, except the keys written during the launch's own
+// step (the rows' own positions).  That is safe because the first kernel of
+// every decode step and prefill chunk starts only after everything before it
+// has completed.  Used by engines below 16 slots, whose CTAs see one or two
+// passes of keys; the batched engines keep the registers for occupancy.
+template <bool kPrefetch>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.dim_blocks().x;
@@ -69,7 +77,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   __shared__ float ovec[kHeadDim];
 
   pdl_launch_dependents();
-  pdl_wait();
   const int tid = threadIdx.x, grp = tid >> 3, sub = tid & 7;
   const int lane = tid & 31, warp = tid >> 5;
   // The whole cluster sees the same row and the same launch shape, so every
@@ -78,6 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     if (threadIdx.x == 0) atomicExch(a.err, kErrAttnCluster);
     return;
   }
+  // the slot state read here was written before the step began
   if (!row_active(a.rm, a.st, m)) return;
   const int slot = row_slot(a.rm, m);
   const int L = a.cross ? a.st.frames[slot] : row_pos(a.rm, a.st, m) + 1;
@@ -87,6 +95,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     return;
   }
   const int j0 = min(L, rank * chunk), j1 = min(L, j0 + chunk);
+  // keys at or after `fresh` are written during this step (the rows' own positions)
+  const int fresh = a.cross ? L : (a.rm.prefill ? a.rm.pos0 : row_pos(a.rm, a.st, m));
+  uint4 kpre[kAttnUnroll], vpre[kAttnUnroll];
+  if constexpr (kPrefetch) {
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      const int j = j0 + grp + u * kAttnGroups;
+      const bool ok = j < j1 && j < fresh;
+      kpre[u] = ok ? ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
+      vpre[u] = ok ? ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  pdl_wait();
 
   const uint4 qraw = *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);
 
@@ -99,7 +120,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
 #pragma unroll
     for (int u = 0; u < kAttnUnroll; ++u) {
       const int j = jb + u * kAttnGroups;
-      kv[u] = j < j1 ? ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
+      if (kPrefetch && base == j0 && j < fresh)
+        kv[u] = kpre[u];
+      else
+        kv[u] = j < j1 ? ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kAttnUnroll; ++u) {
@@ -163,7 +187,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
 #pragma unroll
     for (int u = 0; u < kAttnUnroll; ++u) {
       const int j = jb + u * kAttnGroups;
-      vv[u] = j < j1 ? ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
+      if (kPrefetch && base == j0 && j < fresh)
+        vv[u] = vpre[u];
+      else
+        vv[u] = j < j1 ? ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kAttnUnroll; ++u) {

@@ -426,8 +426,9 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   const int maxlen = cross ? c->F : c->T;
   a.chunk_cap = (maxlen + C - 1) / C;
   const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
-  CK(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  CK(launch_ex(attn_kernel, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
+  void (*fn)(const AttnArgs) = c->tc ? attn_kernel<false> : attn_kernel<true>;
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(launch_ex(fn, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
   return S2R_OK;
 }
 
