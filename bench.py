@@ -651,7 +651,7 @@ def profile(eng):
 # capture (a one-row launch of the same kernel on the small case; traffic grows with the rows'
 # keys, so the ratio carries over).
 NCU_TRAFFIC = {("single", "self_attn"): 4_244_480, ("single", "cross_attn"): 6_184_960}
-NCU_TRAFFIC_RATIO = {("batched", "cross_attn"): 3_097_088 / 3_096_576, ("batched", "self_attn"): 3_097_088 / 3_096_576}
+NCU_TRAFFIC_RATIO = {(w, k): 3_097_088 / 3_096_576 for w in ("batched", "box", "long") for k in ("cross_attn", "self_attn")}
 
 
 def roofline(prof, peak, peak_kind, workload):

@@ -358,7 +358,9 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
   const int kch = kch_for(a.K), mc = mc_for(std::min(a.M, 8));
   ProjFn fn = proj_fn(in, epi, kch, mc);
   if (!fn) return fail(S2R_ENOTSUP, "no projection kernel for in=%d epi=%d", in, epi);
-  const size_t smem = (size_t)(mc == 8 ? 8 : mc) * kch * 256 * sizeof(bf16);
+  // staged rows, then the LayerNorm parameters for LayerNorm'd inputs
+  const size_t smem = (size_t)(mc == 8 ? 8 : mc) * kch * 256 * sizeof(bf16) +
+                      ((in == IN_LN || in == IN_EMBED) ? 2 * (size_t)kch * 256 * sizeof(float) : 0);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int blocks = (a.N + 3) / 4;
   CK(launch_ex(fn, dim3(blocks), dim3(128), smem, s, next_pdl(c), 0, a));

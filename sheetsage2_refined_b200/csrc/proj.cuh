@@ -117,9 +117,13 @@ __device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, f
 // Normalise rows [m0, m0+mc) into xs (bfloat16, KP columns per row, zero
 // padded) and keep the float32 result in x_out.  One warp per row; each lane
 // holds its 8*KCH columns in registers (two-pass mean / variance).
+// sgamma / sbeta: the LayerNorm parameters already in shared memory (or null: read from a.gamma / a.beta).
 template <int KCH, int IN>
 __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m0, int mc, int warp, int lane,
-                                              int nwarps, bool own_rows = false) {
+                                              int nwarps, bool own_rows = false, const float* sgamma = nullptr,
+                                              const float* sbeta = nullptr) {
+  const float* gam = sgamma ? sgamma : a.gamma;
+  const float* bet = sbeta ? sbeta : a.beta;
   constexpr int KP = KCH * 256;
   const int K = a.K;
   for (int i = warp; i < mc; i += nwarps) {
@@ -178,7 +182,7 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
       if (col < K) {
         float y[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = (v[c * 8 + j] - mean) * rstd * a.gamma[col + j] + a.beta[col + j];
+        for (int j = 0; j < 8; ++j) y[j] = (v[c * 8 + j] - mean) * rstd * gam[col + j] + bet[col + j];
         packed = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
         if (keep) {
           float* dst = a.x_out + (size_t)m * K + col;
@@ -194,8 +198,11 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
 template <int KCH, int MC, int IN, int EPI>
 __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MC][KP]
   constexpr int KP = KCH * 256;
+  constexpr bool kLn = IN == IN_LN || IN == IN_EMBED;
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MC][KP]
+  float* sgamma = reinterpret_cast<float*>(smem_raw + (size_t)MC * KP * sizeof(bf16));  // [KP] (LayerNorm inputs)
+  float* sbeta = sgamma + KP;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int K = a.K;
   const int stride = gridDim.x * 4;
@@ -209,14 +216,28 @@ __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
     const int col = c * 256 + lane * 8;
     w[c] = (first < a.N && col < K) ? ld_stream(a.W + (size_t)first * K + col) : make_uint4(0, 0, 0, 0);
   }
+  // ... and so do the LayerNorm parameters and the bias of that row
+  if constexpr (kLn) {
+    for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+      *reinterpret_cast<float4*>(sgamma + i) = *reinterpret_cast<const float4*>(a.gamma + i);
+      *reinterpret_cast<float4*>(sbeta + i) = *reinterpret_cast<const float4*>(a.beta + i);
+    }
+  }
+  const float bias_first = first < a.N ? __bfloat162float(a.bias[first]) : 0.f;
   pdl_launch_dependents();
   pdl_wait();
+  // the residual input of this warp's first row, requested before the staging
+  float xres_first = 0.f;
+  if constexpr (EPI == EPI_RESID) {
+    if (lane < min(MC, a.M) && first < a.N) xres_first = a.x_res[(size_t)lane * a.N + first];
+  }
+  if constexpr (kLn) __syncthreads();  // the LayerNorm parameters are in shared memory
 
   for (int m0 = 0; m0 < a.M; m0 += MC) {
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
     if constexpr (IN == IN_LN || IN == IN_EMBED) {
-      stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4);
+      stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4, false, sgamma, sbeta);
     } else {
       for (int idx = threadIdx.x; idx < MC * (KP / 8); idx += blockDim.x) {
         const int i = idx / (KP / 8), col = (idx % (KP / 8)) * 8;
@@ -264,7 +285,15 @@ __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
 #pragma unroll
       for (int i = 0; i < MC; ++i) {
         acc[i] = warp_sum(acc[i]);
-        if (lane == i && i < mc) proj_epilogue<EPI>(a, m0 + i, n, acc[i]);
+        if (lane == i && i < mc) {
+          const float v = acc[i] + (n == first ? bias_first : __bfloat162float(a.bias[n]));
+          if constexpr (EPI == EPI_RESID) {
+            const size_t o = (size_t)(m0 + i) * a.N + n;
+            a.r_out[o] = (n == first && m0 == 0 ? xres_first : a.x_res[o]) + round_bf16(v);
+          } else {
+            proj_epilogue_biased<EPI>(a, m0 + i, n, v);
+          }
+        }
       }
     }
   }
