@@ -216,9 +216,10 @@ def load_launches(eng) -> int:
     """Kernel launches of one ``load`` with the prefix [SOS, OUT] and bfloat16 memory.
 
     The cross K/V projection (one launch per layer), then the one-row prefill
-    of position 0: a full layer but only the K/V projection in the last one,
-    each LayerNorm'd projection with its own LayerNorm launch on tensor-core
-    engines; the one-kernel step engine prefills with one launch.
+    of position 0: a full layer but only the K/V projection in the last one
+    (6 launches per layer with the attention fused with its out-projection,
+    11 on tensor-core engines with their LayerNorm launches); the one-kernel
+    step engine prefills with one launch.
     """
 
     L, per_step = CONFIG.layers, eng.step_launches
@@ -226,6 +227,8 @@ def load_launches(eng) -> int:
         return L + 1
     if per_step == 11 * L + 2:
         return L + 11 * (L - 1) + 2
+    if per_step == 6 * L + 1:  # attention fused with its out-projection
+        return L + 6 * (L - 1) + 1
     return L + 8 * (L - 1) + 1
 
 

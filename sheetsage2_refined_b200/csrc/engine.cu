@@ -155,6 +155,11 @@ struct s2r_ctx {
   // when `tc` (16 or more slots), the cross K/V projection at load when `tc_cross`
   bool tc = false, tc_cross = false;
   int tc_nb = 64;                  // rows per MMA tile of the step and prefill projections
+  // engines below 16 slots fuse each attention with its out-projection, residual and LayerNorm
+  bool fuse_out = false;
+  float* attn_part = nullptr;      // [H][maxM][D] out-projection partial sums by head
+  unsigned* attn_ticket = nullptr; // [maxM]
+  bf16* xn = nullptr;              // [maxM][D] LayerNorm output in bf16
   int attn_splits = 8;             // CTAs (one cluster) per (row, head) of the self-attention
   int attn_splits_cross = 8;       // ... and of the cross-attention
   int32_t *order_self = nullptr, *order_cross = nullptr;  // [B] decode rows, longest first (tensor-core engines)
@@ -425,10 +430,23 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   a.splits = C;
   a.err = c->dev_error;
   a.order = rm.prefill ? nullptr : (cross ? c->order_cross : c->order_self);
+  if (c->fuse_out) {
+    const LayerBufs& w = c->layers[layer];
+    a.D = c->D;
+    a.wo = cross ? w.wco : w.wo;
+    a.bo = cross ? w.bco : w.bo;
+    a.ln_g = cross ? w.ln_cross_g : w.ln_self_g;
+    a.ln_b = cross ? w.ln_cross_b : w.ln_self_b;
+    a.part = c->attn_part;
+    a.ticket = c->attn_ticket;
+    a.x = c->x;
+    a.xn = c->xn;
+  }
   const int maxlen = cross ? c->F : c->T;
   a.chunk_cap = (maxlen + C - 1) / C;
   const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
-  void (*fn)(const AttnArgs) = c->tc ? attn_kernel<false> : attn_kernel<true>;
+  void (*fn)(const AttnArgs) = c->tc ? attn_kernel<false, false> : c->fuse_out ? attn_kernel<true, true>
+                                                                                : attn_kernel<true, false>;
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CK(launch_ex(fn, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
   return S2R_OK;
@@ -466,6 +484,44 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     TRY(mark(c, K_QKV, s));
   }
   if (last_kv_only) return S2R_OK;
+  if (c->fuse_out) {
+    // attention with its out-projection, residual and LayerNorm fused (attention.cuh); the
+    // projections after them read the bf16 LayerNorm output
+    TRY(launch_attn(c, rm, M, l, false, s));  // 2-3. self-attention ... self_attn_norm
+    TRY(mark(c, K_SELF_ATTN, s));
+    {  // 4. cross q
+      ProjArgs a = proj_base(c);
+      a.rm = rm;
+      a.M = M;
+      a.K = D;
+      a.N = D;
+      a.xin = c->xn;
+      a.ldx = D;
+      a.W = w.wcq;
+      a.bias = w.bcq;
+      a.out = c->q;
+      a.ldo = D;
+      TRY(launch_proj(c, a, IN_BF16, EPI_BF16, s));
+      TRY(mark(c, K_CROSS_Q, s));
+    }
+    TRY(launch_attn(c, rm, M, l, true, s));  // 5-6. cross-attention ... cross_attn_norm
+    TRY(mark(c, K_CROSS_ATTN, s));
+    {  // 7. fc1 + GELU
+      ProjArgs a = proj_base(c);
+      a.rm = rm;
+      a.M = M;
+      a.K = D;
+      a.N = c->FFN;
+      a.xin = c->xn;
+      a.ldx = D;
+      a.W = w.w1;
+      a.bias = w.b1;
+      a.out = c->hid;
+      a.ldo = c->FFN;
+      TRY(launch_proj(c, a, IN_BF16, EPI_GELU, s));
+      TRY(mark(c, K_FC1, s));
+    }
+  } else {
   TRY(launch_attn(c, rm, M, l, false, s));  // 2. self-attention
   TRY(mark(c, K_SELF_ATTN, s));
   {                                         // 3. out-projection + residual
@@ -533,6 +589,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     a.ldo = c->FFN;
     TRY(launch_proj(c, a, IN_LN, EPI_GELU, s));
     TRY(mark(c, K_FC1, s));
+  }
   }
   {  // 8. fc2 + residual
     ProjArgs a = proj_base(c);
@@ -796,6 +853,7 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   if (c->bar) CK(cudaMemsetAsync(c->bar, 0, 2 * sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->counter, 0, sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->keys, 0, c->B * sizeof(unsigned long long), s));
+  if (c->attn_ticket) CK(cudaMemsetAsync(c->attn_ticket, 0, c->maxM * sizeof(unsigned), s));
   return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
               err == kErrAttnCluster ? "attention launched without its cluster shape"
               : err == kErrAttnChunk ? "attention keys exceed the score buffer"
@@ -985,6 +1043,14 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   c->mem_stage = mem_stage;
   TRYC(dalloc(c, &c->prefill_tokens, kPrefillRows));
   TRYC(setup_tensor_core(c));
+  c->fuse_out = !c->tc && !c->persistent;
+  if (c->fuse_out) {
+    TRYC(dalloc(c, &c->attn_part, (size_t)c->H * c->maxM * D));
+    TRYC(dalloc(c, &c->attn_ticket, c->maxM));
+    TRYC(dalloc(c, &c->xn, (size_t)c->maxM * D));
+    CK(cudaMemset(c->attn_ticket, 0, c->maxM * sizeof(unsigned)));
+    CK(cudaMemset(c->xn, 0, (size_t)c->maxM * D * sizeof(bf16)));
+  }
   c->attn_splits = attn_splits_for(c, 4);
   c->attn_splits_cross = attn_splits_for(c, 8);
   c->h_frames.assign(c->B, 0);
@@ -1449,7 +1515,7 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
       self_kv += (double)(pos[b] + 1) * H * kHeadDim * 2 * 2;
       cross_kv += (double)frames[b] * H * kHeadDim * 2 * 2;
     }
-  const double per[K_CLASSES] = {
+  double per[K_CLASSES] = {
       3 * D * D * 2 + 3 * D * 2 + M * D * 8 + M * 3 * D * 2,  // qkv: W, b, r in, x out, q/k/v out
       self_kv + active * D * 4,                               // self attention: K, V, q in, out
       D * D * 2 + D * 2 + M * D * (2 + 4 + 4),                // self out-proj: W, b, a in, x in, r out
@@ -1463,6 +1529,11 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
   };
   double step_bytes = 0.0;
   for (int k = 0; k < K_STEP; ++k) step_bytes += per[k] * (k == K_LOGITS ? 1 : c->L);
+  if (c->fuse_out) {  // the out-projections run inside the attention launches
+    per[K_SELF_ATTN] += per[K_SELF_OUT];
+    per[K_CROSS_ATTN] += per[K_CROSS_OUT];
+    per[K_SELF_OUT] = per[K_CROSS_OUT] = 0.0;
+  }
   for (int b = 0; b < c->B; ++b) {
     if (!c->loaded[b]) continue;
     c->bound[b] = std::min(c->bound[b] + 1, c->T - 1);
@@ -1528,7 +1599,7 @@ int32_t s2r_step_launches(s2r_ctx* c) {
   if (!c) return 0;
   if (c->persistent) return 1;
   // tensor-core engines add a LayerNorm launch before each LayerNorm'd projection and the logits
-  return c->tc ? 11 * c->L + 2 : 8 * c->L + 1;
+  return c->tc ? 11 * c->L + 2 : c->fuse_out ? 6 * c->L + 1 : 8 * c->L + 1;
 }
 
 int32_t s2r_free_pages(s2r_ctx* c) { return c ? (int32_t)c->free_pages.size() : 0; }

@@ -188,4 +188,4 @@ def test_batched_slot_independence_bit_exact():
 
 def test_no_tensor_core_flag_keeps_cuda_core_projections():
     eng = cuda_engine(sc.C1, sc.C1_SEED, sc.c1_grammar(), BATCH, sc.C1_FRAMES, flags=_lib.S2R_FLAG_NO_TENSOR_CORE)
-    assert eng.step_launches == 8 * sc.C1.layers + 1
+    assert eng.step_launches == 6 * sc.C1.layers + 1  # CUDA-core projections, fused attention
