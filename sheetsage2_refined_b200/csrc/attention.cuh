@@ -10,7 +10,10 @@
 // so a split must know the global max and sum before rounding p.  The CTAs
 // exchange their partial max and partial sum through distributed shared
 // memory (two cluster barriers), then each accumulates p v over its keys and
-// rank 0 adds the C partial outputs in rank order.  Keys beyond the visible
+// the C partial outputs are added in rank order.  Every exchange is a push:
+// each CTA sends its value into its peers' shared memory with asynchronous
+// remote stores that count their bytes on the receiver's mbarrier, so a CTA
+// waits only for the values it needs and reads only its own shared memory.  Keys beyond the visible
 // length are never read; the reference masks them with -inf, which gives the
 // same softmax.
 //   self  (engine.py:303-312): keys 0..position of the slot, paged pool
@@ -20,6 +23,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "mbarrier.cuh"
 
 namespace s2r {
 
@@ -39,6 +43,7 @@ struct AttnArgs {
   int pages_per_slot;
   int frames_cap;
   int chunk_cap;  // score buffer length per CTA
+  int stage_cap;  // kAttnPreStage: key and value rows per CTA held in shared memory
   int splits;     // CTAs per (row, head): the cluster size the launch must have
   int* err;       // device error word: set (and the work skipped) on a broken invariant
   const int32_t* order;  // [M] row of each grid z index (longest first), or null: identity
@@ -53,14 +58,28 @@ struct AttnArgs {
   bf16* xn;                  // [M][D] the LayerNorm output in bf16 (the next projection's input)
 };
 
+constexpr int kAttnLnHeads = 16;     // head partials the fused LayerNorm requests at once
 constexpr int kAttnOutPrefetch = 4;  // out-projection passes (32 features each) loaded before the wait
 
 constexpr int kErrAttnCluster = 1;  // launched without the expected cluster shape
 constexpr int kErrAttnChunk = 2;    // a row's keys do not fit the score buffer
+constexpr int kErrAttnStage = 5;    // a bulk copy into shared memory did not complete in time
+constexpr int kErrAttnExchange = 6; // a value from a peer CTA did not arrive in time
+
+// How a CTA gets its keys and values ahead of the PDL wait.
+constexpr int kAttnPreNone = 0;   // read in the loops (batched engines, which keep occupancy)
+constexpr int kAttnPreRegs = 1;   // the first pass of the CTA's earlier keys in registers
+constexpr int kAttnPreStage = 2;  // all of them (up to stage_cap rows) bulk-copied to shared memory
+// static shared memory of the kernel plus the 1 KB the SM reserves per CTA (upper bound)
+constexpr size_t kAttnStaticSmem = 4096;
+// shared memory of an SM left to the projection kernels that run beside the attention
+constexpr size_t kAttnOtherSmem = 32768;
 
 constexpr int kAttnThreads = 256;
+constexpr int kAttnMaxSplits = 8;  // CTAs per (row, head) at most
 constexpr int kAttnGroups = kAttnThreads / 8;  // 8 lanes x 16 bytes per key row
-constexpr int kAttnUnroll = 4;
+constexpr int kAttnUnroll = 4;       // keys per group and pass (kAttnPreNone / kAttnPreRegs)
+constexpr int kAttnUnrollStaged = 8;  // the same from shared memory (kAttnPreStage): more keys in flight
 
 __device__ __forceinline__ uint32_t pack_bf16_pair(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -72,13 +91,36 @@ __device__ __forceinline__ const bf16* attn_row(const AttnArgs& a, const bf16* b
   return base + paged_offset(a.st.page_table, a.pages_per_slot, a.H, slot, h, j);
 }
 
-// kPrefetch: the first pass of keys and values (kAttnGroups * kAttnUnroll
-// keys of the CTA's range) is loaded into registers before the kernel waits
-// for the previous kernel, except the keys written during the launch's own
-// step (the rows' own positions).  That is safe because the first kernel of
-// every decode step and prefill chunk starts only after everything before it
-// has completed.  Used by engines below 16 slots, whose CTAs see one or two
-// passes of keys; the batched engines keep the registers for occupancy.
+// Dynamic shared memory of one attention CTA: the score buffer, the partial
+// outputs of the key groups and, for kAttnPreStage, the staged key and value
+// rows and (with kFuseOut) the residual row, LayerNorm weights and
+// out-projection bias of the fused tail.  Every part starts 16-byte aligned.
+struct AttnSmem {
+  size_t part, sk, sv, sx, sg, sb, sbo, total;
+  __host__ __device__ AttnSmem(int chunk_cap, int stage_cap, int D, bool ln_stage) {
+    part = (size_t)((chunk_cap + 3) & ~3) * 4;
+    sk = part + (size_t)kAttnGroups * kHeadDim * 4;
+    sv = sk + (size_t)stage_cap * kHeadDim * 2;
+    sx = sv + (size_t)stage_cap * kHeadDim * 2;
+    sg = sx + (ln_stage ? (size_t)D * 4 : 0);
+    sb = sg + (ln_stage ? (size_t)D * 4 : 0);
+    sbo = sb + (ln_stage ? (size_t)D * 4 : 0);
+    total = sbo + (ln_stage ? (size_t)D * 2 : 0);
+  }
+};
+
+// kPre says how the CTA's keys and values written before the step (every key
+// of a cross-attention row; the keys before the row's own position of a self-
+// attention row) reach it:
+//   kAttnPreRegs  the first pass (kAttnGroups * kAttnUnroll keys) is loaded
+//                 into registers before the PDL wait;
+//   kAttnPreStage up to stage_cap rows are bulk-copied into shared memory
+//                 before the wait, the keys of the step itself after it (plain
+//                 loads into the same buffer), so both loops read shared memory.
+// Reading before the wait is safe because the first kernel of every decode
+// step and prefill chunk starts only after everything before it has completed.
+// Engines below 16 slots use these; the batched engines keep shared memory and
+// registers for occupancy.
 //
 // kFuseOut (engines below 16 slots): the kernel also runs what follows the
 // attention in the reference (engine.py:312-313):
@@ -90,28 +132,42 @@ __device__ __forceinline__ const bf16* attn_row(const AttnArgs& a, const bf16* b
 // last CTA of the row (a ticket counter) adds the partials of all heads in
 // head order, the bias and the residual, rounds as the reference does, and
 // writes the LayerNorm output as float32 (the next residual input) and bf16
-// (the next projection's input).
-template <bool kPrefetch, bool kFuseOut>
+// (the next projection's input).  With kAttnPreStage the LayerNorm weights and
+// the bias are staged before the wait and the residual row right after it.
+template <int kPre, bool kFuseOut>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
+  constexpr bool kStage = kPre == kAttnPreStage;
+  constexpr bool kLnStage = kStage && kFuseOut;
+  constexpr int kU = kStage ? kAttnUnrollStaged : kAttnUnroll;
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.dim_blocks().x;
   const int rank = (int)cluster.block_rank();
   const int h = blockIdx.y, m = a.order ? a.order[blockIdx.z] : (int)blockIdx.z;
-  extern __shared__ __align__(16) float smem_f[];
-  float* sc = smem_f;                                 // [chunk_cap] scores, then exp values
-  float* part = smem_f + ((a.chunk_cap + 3) & ~3);    // [kAttnGroups][64] partial outputs
-  __shared__ float red[2];                            // this CTA's max and sum
+  extern __shared__ __align__(16) unsigned char attn_smem[];
+  const AttnSmem lay(a.chunk_cap, kStage ? a.stage_cap : 0, a.D, kLnStage);
+  float* sc = reinterpret_cast<float*>(attn_smem);                // [chunk_cap] scores, then exp values
+  float* part = reinterpret_cast<float*>(attn_smem + lay.part);   // [kAttnGroups][64] partial outputs
+  bf16* sk = reinterpret_cast<bf16*>(attn_smem + lay.sk);         // kStage: [stage_cap][64] keys
+  bf16* sv = reinterpret_cast<bf16*>(attn_smem + lay.sv);         //         [stage_cap][64] values
+  float* sx = reinterpret_cast<float*>(attn_smem + lay.sx);       // kLnStage: residual row [D]
+  float* sg = reinterpret_cast<float*>(attn_smem + lay.sg);       //           LayerNorm weight [D]
+  float* sb = reinterpret_cast<float*>(attn_smem + lay.sb);       //           LayerNorm bias [D]
+  bf16* sbo = reinterpret_cast<bf16*>(attn_smem + lay.sbo);       //           out-projection bias [D]
+  __shared__ float xred[2][kAttnMaxSplits];          // every rank's partial max and sum
+  __shared__ float xo[kAttnMaxSplits][kHeadDim];      // every rank's partial output
   __shared__ float wred[kAttnThreads / 32];
-  __shared__ float ovec[kHeadDim];
+  __shared__ float wmax[kAttnThreads / 32], wsum[kAttnThreads / 32];
+  __shared__ __align__(8) uint64_t xbar[3];           // exchanges received: max, sum, output
   __shared__ float ohead[kHeadDim];                   // kFuseOut: the head's output, bf16-rounded
   __shared__ int is_last;
+  __shared__ __align__(8) uint64_t bars[2];           // kStage: [0] rows + weights, [1] residual row
 
   pdl_launch_dependents();
   const int tid = threadIdx.x, grp = tid >> 3, sub = tid & 7;
   const int lane = tid & 31, warp = tid >> 5;
   // The whole cluster sees the same row and the same launch shape, so every
   // early return below is taken by all of its CTAs together.
-  if (C != a.splits) {
+  if (C != a.splits || C > kAttnMaxSplits) {
     if (threadIdx.x == 0) atomicExch(a.err, kErrAttnCluster);
     return;
   }
@@ -127,10 +183,46 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   const int j0 = min(L, rank * chunk), j1 = min(L, j0 + chunk);
   // keys at or after `fresh` are written during this step (the rows' own positions)
   const int fresh = a.cross ? L : (a.rm.prefill ? a.rm.pos0 : row_pos(a.rm, a.st, m));
-  uint4 kpre[kAttnUnroll], vpre[kAttnUnroll];
+  // kStage: rows [j0, js) are read from shared memory, [j0, jbulk) arrive by bulk copy
+  const int js = kStage ? min(j1, j0 + a.stage_cap) : j0;
+  const int jbulk = kStage ? max(j0, min(js, fresh)) : j0;
+  uint4 kpre[kU], vpre[kU];  // kAttnPreRegs (kU == kAttnUnroll there)
   // kFuseOut: this CTA's out-projection features and their weights for head h
   const int per = kFuseOut ? (a.D + C - 1) / C : 0, n0 = rank * per;
   uint4 wpre[kAttnOutPrefetch];
+  // every rank receives the C maxima and sums; the partial outputs go to every
+  // rank with kFuseOut, else to rank 0 alone
+  const bool gets_o = kFuseOut || rank == 0;
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&xbar[i], 1);
+    if constexpr (kStage) {
+      mbar_init(&bars[0], 1);
+      mbar_init(&bars[1], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(&xbar[0], (unsigned)C * 4);
+    mbar_expect_tx(&xbar[1], (unsigned)C * 4);
+    mbar_expect_tx(&xbar[2], gets_o ? (unsigned)(C * kHeadDim * 4) : 0u);
+  }
+  if constexpr (kStage) {
+    if (tid == 0) {
+      mbar_expect_tx(&bars[0], (unsigned)(jbulk - j0) * (2 * kHeadDim * 2) + (kLnStage ? (unsigned)a.D * 10 : 0u));
+      // one copy per run of rows that is contiguous in memory (a page of the
+      // self-attention pool; the whole range for cross-attention)
+      for (int s = j0; s < jbulk;) {
+        const int e = a.cross ? jbulk : min(jbulk, (s / kPageTokens + 1) * kPageTokens);
+        const unsigned bytes = (unsigned)(e - s) * kHeadDim * 2;
+        bulk_load(sk + (size_t)(s - j0) * kHeadDim, attn_row(a, a.k, slot, h, s), bytes, &bars[0]);
+        bulk_load(sv + (size_t)(s - j0) * kHeadDim, attn_row(a, a.v, slot, h, s), bytes, &bars[0]);
+        s = e;
+      }
+      if constexpr (kLnStage) {
+        bulk_load(sg, a.ln_g, (unsigned)a.D * 4, &bars[0]);
+        bulk_load(sb, a.ln_b, (unsigned)a.D * 4, &bars[0]);
+        bulk_load(sbo, a.bo, (unsigned)a.D * 2, &bars[0]);
+      }
+    }
+  }
   if constexpr (kFuseOut) {
 #pragma unroll
     for (int p = 0; p < kAttnOutPrefetch; ++p) {
@@ -138,35 +230,67 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       wpre[p] = (i < per && n < a.D) ? ld_stream(a.wo + (size_t)n * a.D + h * kHeadDim + sub * 8) : make_uint4(0, 0, 0, 0);
     }
   }
-  if constexpr (kPrefetch) {
+  if constexpr (kPre == kAttnPreRegs) {
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int j = j0 + grp + u * kAttnGroups;
       const bool ok = j < j1 && j < fresh;
       kpre[u] = ok ? ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
       vpre[u] = ok ? ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
     }
   }
+  // kStage: whether this thread saw the copies land (if not, it waits for them
+  // again, bounded, before the CTA exits; the error word is set either way)
+  bool staged = true, row_staged = true;
+  auto drain = [&]() {
+    if (kStage && !staged) mbar_wait(&bars[0], 0);
+    if (kLnStage && !row_staged) mbar_wait(&bars[1], 0);
+  };
+  __syncthreads();  // the barriers are initialised before anyone waits on them
+  // First half of a barrier that proves every peer has started and initialised
+  // its barriers before the first store into its shared memory (the wait comes
+  // just before that store).
+  cluster_arrive_relaxed();
   pdl_wait();
 
+  if constexpr (kLnStage) {
+    if (tid == 0) {  // the residual row was written by the previous kernel
+      mbar_expect_tx(&bars[1], (unsigned)a.D * 4);
+      bulk_load(sx, a.x + (size_t)m * a.D, (unsigned)a.D * 4, &bars[1]);
+    }
+  }
   const uint4 qraw = *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);
+  if constexpr (kStage) {
+    // the rows of this step's own positions: plain loads into the stage
+    for (int j = jbulk + grp; j < js; j += kAttnGroups) {
+      const uint4 kk = ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8);
+      const uint4 vv = ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8);
+      *reinterpret_cast<uint4*>(sk + (size_t)(j - j0) * kHeadDim + sub * 8) = kk;
+      *reinterpret_cast<uint4*>(sv + (size_t)(j - j0) * kHeadDim + sub * 8) = vv;
+    }
+    staged = mbar_wait(&bars[0], 0);
+    if (!staged) atomicExch(a.err, kErrAttnStage);
+    __syncthreads();
+  }
 
   // ---- scores and local max
   float lmax = -INFINITY;
   // The loop bound is uniform across the block (the shuffles below need all lanes).
-  for (int base = j0; base < j1; base += kAttnGroups * kAttnUnroll) {
+  for (int base = j0; base < j1; base += kAttnGroups * kU) {
     const int jb = base + grp;
-    uint4 kv[kAttnUnroll];
+    uint4 kv[kU];
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int j = jb + u * kAttnGroups;
-      if (kPrefetch && base == j0 && j < fresh)
+      if (kPre == kAttnPreRegs && base == j0 && j < fresh)
         kv[u] = kpre[u];
+      else if (kStage && j < js)
+        kv[u] = *reinterpret_cast<const uint4*>(sk + (size_t)(j - j0) * kHeadDim + sub * 8);
       else
         kv[u] = j < j1 ? ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int j = jb + u * kAttnGroups;
       float s = bf_lo(kv[u].x) * bf_lo(qraw.x);
       s = fmaf(bf_hi(kv[u].x), bf_hi(qraw.x), s);
@@ -187,16 +311,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     }
   }
   lmax = warp_max(lmax);
-  if (lane == 0) wred[warp] = lmax;
+  if (lane == 0) wmax[warp] = lmax;
   __syncthreads();
-  if (tid == 0) {
-    float v = wred[0];
-    for (int w = 1; w < kAttnThreads / 32; ++w) v = fmaxf(v, wred[w]);
-    red[0] = v;
+  cluster_wait();
+  if (tid < C) {  // thread r sends this CTA's max to rank r
+    float v = wmax[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) v = fmaxf(v, wmax[w]);
+    st_async_f32(&xred[0][rank], tid, v, &xbar[0]);
   }
-  cluster.sync();
+  bool exchanged = mbar_wait(&xbar[0], 0);
   float gmax = -INFINITY;
-  for (int r = 0; r < C; ++r) gmax = fmaxf(gmax, *cluster.map_shared_rank(&red[0], r));
+  for (int r = 0; r < C; ++r) gmax = fmaxf(gmax, xred[0][r]);
 
   // ---- exp and local sum
   float lsum = 0.f;
@@ -206,36 +331,41 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     lsum += e;
   }
   lsum = warp_sum(lsum);
-  if (lane == 0) wred[warp] = lsum;
+  if (lane == 0) wsum[warp] = lsum;
   __syncthreads();
-  if (tid == 0) {
+  if (tid < C) {
     float v = 0.f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) v += wred[w];
-    red[1] = v;
+    for (int w = 0; w < kAttnThreads / 32; ++w) v += wsum[w];
+    st_async_f32(&xred[1][rank], tid, v, &xbar[1]);
   }
-  cluster.sync();
+  exchanged &= mbar_wait(&xbar[1], 0);
   float gsum = 0.f;
-  for (int r = 0; r < C; ++r) gsum += *cluster.map_shared_rank(&red[1], r);
+  for (int r = 0; r < C; ++r) gsum += xred[1][r];
+  // p = bf16(e / sum), once per key (each thread divides the values it wrote)
+  for (int j = j0 + tid; j < j1; j += kAttnThreads) sc[j - j0] = round_bf16(sc[j - j0] / gsum);
+  __syncthreads();
 
-  // ---- p = bf16(e / sum), partial p.V
+  // ---- partial p.V
   float acc[8];
 #pragma unroll
   for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-  for (int base = j0; base < j1; base += kAttnGroups * kAttnUnroll) {
+  for (int base = j0; base < j1; base += kAttnGroups * kU) {
     const int jb = base + grp;
-    uint4 vv[kAttnUnroll];
+    uint4 vv[kU];
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int j = jb + u * kAttnGroups;
-      if (kPrefetch && base == j0 && j < fresh)
+      if (kPre == kAttnPreRegs && base == j0 && j < fresh)
         vv[u] = vpre[u];
+      else if (kStage && j < js)
+        vv[u] = *reinterpret_cast<const uint4*>(sv + (size_t)(j - j0) * kHeadDim + sub * 8);
       else
         vv[u] = j < j1 ? ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int j = jb + u * kAttnGroups;
-      const float p = j < j1 ? round_bf16(sc[j - j0] / gsum) : 0.f;
+      const float p = j < j1 ? sc[j - j0] : 0.f;
       acc[0] = fmaf(p, bf_lo(vv[u].x), acc[0]);
       acc[1] = fmaf(p, bf_hi(vv[u].x), acc[1]);
       acc[2] = fmaf(p, bf_lo(vv[u].y), acc[2]);
@@ -252,23 +382,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   if (tid < kHeadDim) {
     float o = 0.f;
     for (int g = 0; g < kAttnGroups; ++g) o += part[g * kHeadDim + tid];
-    ovec[tid] = o;
+    if (kFuseOut) {  // every rank needs the head's output
+      for (int r = 0; r < C; ++r) st_async_f32(&xo[rank][tid], r, o, &xbar[2]);
+    } else {
+      st_async_f32(&xo[rank][tid], 0, o, &xbar[2]);
+    }
   }
-  cluster.sync();
+  if (gets_o) exchanged &= mbar_wait(&xbar[2], 0);
+  if (!exchanged) atomicExch(a.err, kErrAttnExchange);
+  // Everything sent to this CTA has landed.  Every CTA waits at its exit for
+  // the whole cluster to get here, so no CTA leaves while a store into it
+  // could still be on its way.
+  cluster_arrive_relaxed();
   if constexpr (!kFuseOut) {
     if (rank == 0 && tid < kHeadDim) {
       float o = 0.f;
-      for (int r = 0; r < C; ++r) o += cluster.map_shared_rank(ovec, r)[tid];
+      for (int r = 0; r < C; ++r) o += xo[r][tid];
       a.out[(size_t)m * a.ldo + h * kHeadDim + tid] = __float2bfloat16_rn(o);
     }
-    cluster.sync();  // peers keep their shared memory until rank 0 has read it
+    drain();
+    cluster_wait();
   } else {
     if (tid < kHeadDim) {
       float o = 0.f;
-      for (int r = 0; r < C; ++r) o += cluster.map_shared_rank(ovec, r)[tid];
+      for (int r = 0; r < C; ++r) o += xo[r][tid];
       ohead[tid] = round_bf16(o);  // the attention output is bf16 (engine.py:292)
     }
-    cluster.sync();  // every CTA has its o; peers may leave
+    __syncthreads();
     float oh[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) oh[t] = ohead[sub * 8 + t];
@@ -296,13 +436,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       emit(p, (i < per && n < a.D) ? ld_stream(a.wo + (size_t)n * a.D + h * kHeadDim + sub * 8) : make_uint4(0, 0, 0, 0));
     }
     // ---- the last CTA of the row: residual sum and LayerNorm
-    __threadfence();
+    __syncthreads();  // the block's partials are written
+    if (tid == 0) {
+      // The residual row copy has landed before the ticket, so the last CTA's
+      // rewrite of the row cannot overtake it.
+      if (kLnStage) row_staged = mbar_wait(&bars[1], 0);
+      if (!row_staged) atomicExch(a.err, kErrAttnStage);
+      unsigned prev;
+      // release: the block's partials (ordered before by the barrier); acquire: everyone else's
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.ticket + m) : "memory");
+      is_last = prev == (unsigned)(a.H * C) - 1;
+      if (is_last) a.ticket[m] = 0u;
+    }
     __syncthreads();
-    if (tid == 0) is_last = atomicAdd(a.ticket + m, 1u) == (unsigned)(a.H * C) - 1;
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    if (tid == 0) a.ticket[m] = 0u;
+    if (!is_last) {
+      drain();
+      cluster_wait();
+      return;
+    }
+    // completed already: the wait makes the row visible to every thread
+    if constexpr (kLnStage) row_staged = mbar_wait(&bars[1], 0);
     constexpr int kCols = 16;  // columns per thread (width <= 4096)
     float r[kCols];
     float sum = 0.f;
@@ -311,19 +464,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       const int col = c * 4 * kAttnThreads + tid * 4;
       float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
       if (col < a.D) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int hh = 0; hh < a.H; ++hh) {
-          const float4 p4 = __ldcg(reinterpret_cast<const float4*>(a.part + ((size_t)hh * a.M + m) * a.D + col));
-          acc.x += p4.x;
-          acc.y += p4.y;
-          acc.z += p4.z;
-          acc.w += p4.w;
+        // the head partials, all requested before the first is added (head order)
+        const float* pcol = a.part + (size_t)m * a.D + col;
+        const size_t hstride = (size_t)a.M * a.D;
+        float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 p4[kAttnLnHeads];
+        for (int h0 = 0; h0 < a.H; h0 += kAttnLnHeads) {
+#pragma unroll
+          for (int i = 0; i < kAttnLnHeads; ++i)
+            p4[i] = h0 + i < a.H ? __ldcg(reinterpret_cast<const float4*>(pcol + (h0 + i) * hstride))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int i = 0; i < kAttnLnHeads; ++i) {
+            if (h0 + i >= a.H) break;
+            acc4.x += p4[i].x;
+            acc4.y += p4[i].y;
+            acc4.z += p4[i].z;
+            acc4.w += p4[i].w;
+          }
         }
-        const float4 x4 = *reinterpret_cast<const float4*>(a.x + (size_t)m * a.D + col);
-        v4.x = x4.x + round_bf16(acc.x + __bfloat162float(a.bo[col + 0]));
-        v4.y = x4.y + round_bf16(acc.y + __bfloat162float(a.bo[col + 1]));
-        v4.z = x4.z + round_bf16(acc.z + __bfloat162float(a.bo[col + 2]));
-        v4.w = x4.w + round_bf16(acc.w + __bfloat162float(a.bo[col + 3]));
+        const float4 x4 = kLnStage ? *reinterpret_cast<const float4*>(sx + col)
+                                   : *reinterpret_cast<const float4*>(a.x + (size_t)m * a.D + col);
+        const bf16* bo = kLnStage ? sbo : a.bo;
+        v4.x = x4.x + round_bf16(acc4.x + __bfloat162float(bo[col + 0]));
+        v4.y = x4.y + round_bf16(acc4.y + __bfloat162float(bo[col + 1]));
+        v4.z = x4.z + round_bf16(acc4.z + __bfloat162float(bo[col + 2]));
+        v4.w = x4.w + round_bf16(acc4.w + __bfloat162float(bo[col + 3]));
       }
       r[c * 4 + 0] = v4.x;
       r[c * 4 + 1] = v4.y;
@@ -356,18 +522,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     float var = 0.f;
     for (int w = 0; w < kAttnThreads / 32; ++w) var += wred[w];
     const float rstd = rsqrtf(var / (float)a.D + kLnEps);
+    const float* g = kLnStage ? sg : a.ln_g;
+    const float* b = kLnStage ? sb : a.ln_b;
 #pragma unroll
     for (int c = 0; c < kCols / 4; ++c) {
       const int col = c * 4 * kAttnThreads + tid * 4;
       if (col < a.D) {
         float y[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) y[j] = (r[c * 4 + j] - mean) * rstd * a.ln_g[col + j] + a.ln_b[col + j];
+        for (int j = 0; j < 4; ++j) y[j] = (r[c * 4 + j] - mean) * rstd * g[col + j] + b[col + j];
         *reinterpret_cast<float4*>(a.x + (size_t)m * a.D + col) = make_float4(y[0], y[1], y[2], y[3]);
         *reinterpret_cast<uint2*>(a.xn + (size_t)m * a.D + col) =
             make_uint2(pack_bf16_pair(y[0], y[1]), pack_bf16_pair(y[2], y[3]));
       }
     }
+    drain();
+    cluster_wait();
   }
 }
 

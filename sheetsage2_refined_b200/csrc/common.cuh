@@ -42,6 +42,15 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
+// Cluster barrier in two halves (release on arrive, acquire on wait), every
+// thread of every CTA of the cluster taking part.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// Arrive without ordering memory (execution only).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -107,6 +107,7 @@ struct s2r_ctx {
   int device = 0;
   int D = 0, H = 0, F = 0, FFN = 0, V = 0, L = 0, B = 0, T = 0, maxM = 0, pps = 0, n_pages = 0;
   int num_sms = 148;
+  int smem_per_sm = 228 * 1024;  // shared memory of one SM (bytes)
   bool pdl = true, use_graph = true;
   bool fence_next = false;  // the next launch starts a decode step or prefill chunk: no programmatic overlap
   std::vector<void*> allocs;
@@ -380,7 +381,7 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
 // (row, head) pairs of a full batch cover the SMs about four times, and
 // twice that for the cross-attention, whose rows are long (every encoder
 // frame) and uneven.
-constexpr int kAttnSplits = 8;
+constexpr int kAttnSplits = kAttnMaxSplits;
 
 int attn_splits_for(const s2r_ctx* c, int cover) {
   if (!c->tc) return kAttnSplits;
@@ -444,9 +445,29 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   }
   const int maxlen = cross ? c->F : c->T;
   a.chunk_cap = (maxlen + C - 1) / C;
-  const size_t smem = (size_t)(((a.chunk_cap + 3) & ~3) + kAttnGroups * kHeadDim) * sizeof(float);
-  void (*fn)(const AttnArgs) = c->tc ? attn_kernel<false, false> : c->fuse_out ? attn_kernel<true, true>
-                                                                                : attn_kernel<true, false>;
+  int pre = c->tc ? kAttnPreNone : kAttnPreRegs;
+  if (!c->tc) {
+    // Stage the CTAs' earlier keys and values in shared memory when the
+    // launch fits on the SMs in one wave with room left for a CTA of the
+    // other attention kernel beside each and for the projection kernels in
+    // flight (kernels start ahead of their inputs under PDL).
+    const int ctas = M * c->H * C;
+    const int per_sm = std::max(1, (ctas + c->num_sms - 1) / c->num_sms);
+    const size_t budget = ((size_t)c->smem_per_sm - kAttnOtherSmem) / (2 * per_sm);
+    const size_t fixed = AttnSmem(a.chunk_cap, 0, c->D, c->fuse_out).total + kAttnStaticSmem;
+    if (budget > fixed) {
+      const int cap = (int)std::min<size_t>(a.chunk_cap, (budget - fixed) / (2 * kHeadDim * 2));
+      if (cap == a.chunk_cap || cap >= kAttnGroups * kAttnUnroll) {
+        pre = kAttnPreStage;
+        a.stage_cap = cap;
+      }
+    }
+  }
+  const size_t smem = AttnSmem(a.chunk_cap, a.stage_cap, c->D, pre == kAttnPreStage && c->fuse_out).total;
+  void (*fn)(const AttnArgs) =
+      pre == kAttnPreNone    ? attn_kernel<kAttnPreNone, false>
+      : pre == kAttnPreRegs  ? (c->fuse_out ? attn_kernel<kAttnPreRegs, true> : attn_kernel<kAttnPreRegs, false>)
+                             : (c->fuse_out ? attn_kernel<kAttnPreStage, true> : attn_kernel<kAttnPreStage, false>);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CK(launch_ex(fn, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
   return S2R_OK;
@@ -857,6 +878,8 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
               err == kErrAttnCluster ? "attention launched without its cluster shape"
               : err == kErrAttnChunk ? "attention keys exceed the score buffer"
+              : err == kErrAttnStage ? "a bulk copy of the attention kernel did not complete in time"
+              : err == kErrAttnExchange ? "a value sent between attention CTAs did not arrive in time"
               : err == kErrGemmWait  ? "a wait of the tensor-core projection timed out"
                                      : "a grid barrier of the persistent step timed out");
 }
@@ -919,6 +942,7 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   c->pdl = !(k.flags & S2R_FLAG_NO_PDL);
   c->use_graph = !(k.flags & S2R_FLAG_NO_GRAPH);
   cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&c->smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
   auto cleanup = [&](int rc) {
     s2r_destroy(c);
     return rc;

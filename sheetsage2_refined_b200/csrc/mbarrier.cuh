@@ -53,4 +53,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
                : "memory");
 }
 
+// Store one float into the shared memory of CTA `rank` of the cluster (at the
+// address of `local` there) and count its 4 bytes on that CTA's mbarrier
+// `bar` (also given by its local address).  The receiver waits on `bar`.
+__device__ __forceinline__ void st_async_f32(const void* local, int rank, float v, uint64_t* bar) {
+  uint32_t dst, rbar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst),
+               "r"(__float_as_uint(v)), "r"(rbar)
+               : "memory");
+}
+
 }  // namespace s2r

@@ -131,6 +131,25 @@ def test_one_kernel_and_multi_kernel_steps_agree():
     assert err <= 1.0 and same >= 23
 
 
+def test_plain_launches_bit_exact():
+    """Without the CUDA graph and programmatic dependent launch (the mode the
+    profiles are captured in) the step computes the same logits bit for bit:
+    launching a kernel early changes when it reads, never what it reads."""
+
+    from sheetsage2_refined_b200 import _lib
+
+    g = np.load(GOLDEN / "c2_head.npz")
+    tokens = g["tokens"].tolist()
+    plain = _lib.S2R_FLAG_NO_PDL | _lib.S2R_FLAG_NO_GRAPH
+    engines = [cuda_engine(sc.C2, sc.C2_SEED, sc.c2_grammar(), 1, sc.C2_FRAMES, flags=f) for f in (0, plain)]
+    for e in engines:
+        loader(e, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, 200)
+        e.run(150)  # past two pages of keys, so several CTAs of every cluster stage keys
+    for k in range(8):
+        (la, ga), (lb, gb) = (e.step_debug(np.array([tokens[2 + k]])) for e in engines)
+        assert np.array_equal(la, lb) and ga[0] == gb[0], k
+
+
 def test_c2_long_context_vs_oracle():
     """Full-size decoder, 192 teacher-forced steps past a 320-token prefill.
 
