@@ -111,6 +111,8 @@ struct s2r_ctx {
   bool pdl = true, use_graph = true;
   bool fence_next = false;  // the next launch starts a decode step or prefill chunk: no programmatic overlap
   std::vector<void*> allocs;
+  char* arena = nullptr;  // the current arena of small buffers and its fill
+  size_t arena_used = 0;
   // weights
   float *tok_emb = nullptr, *pos_emb = nullptr, *emb_ln_g = nullptr, *emb_ln_b = nullptr;
   bf16* emb_bf16 = nullptr;
@@ -175,11 +177,33 @@ struct s2r_ctx {
 
 namespace {
 
+// Buffers up to kArenaPiece bytes (activations, slot state, biases and
+// LayerNorm weights) are packed into 32 MB arenas, so that everything a step
+// touches besides the weight matrices and the K/V pools sits in a few large
+// pages; larger buffers get their own allocation.
+constexpr size_t kArenaPiece = 4u << 20;
+constexpr size_t kArenaChunk = 32u << 20;
+
 template <typename T>
 int dalloc(s2r_ctx* c, T** p, size_t count) {
+  const size_t bytes = std::max<size_t>(count, 1) * sizeof(T);
+  if (bytes <= kArenaPiece) {
+    size_t off = (c->arena_used + 255) & ~(size_t)255;
+    if (!c->arena || off + bytes > kArenaChunk) {
+      void* chunk = nullptr;
+      cudaError_t e = cudaMalloc(&chunk, kArenaChunk);
+      if (e != cudaSuccess) return fail(S2R_ENOMEM, "cudaMalloc(%zu bytes): %s", kArenaChunk, cudaGetErrorString(e));
+      c->allocs.push_back(chunk);
+      c->arena = static_cast<char*>(chunk);
+      off = 0;
+    }
+    *p = reinterpret_cast<T*>(c->arena + off);
+    c->arena_used = off + bytes;
+    return S2R_OK;
+  }
   void* ptr = nullptr;
-  cudaError_t e = cudaMalloc(&ptr, std::max<size_t>(count, 1) * sizeof(T));
-  if (e != cudaSuccess) return fail(S2R_ENOMEM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  if (e != cudaSuccess) return fail(S2R_ENOMEM, "cudaMalloc(%zu bytes): %s", bytes, cudaGetErrorString(e));
   c->allocs.push_back(ptr);
   *p = static_cast<T*>(ptr);
   return S2R_OK;
