@@ -195,6 +195,83 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
   }
 }
 
+// One LayerNorm'd row (IN_LN or IN_EMBED) staged by all 128 threads of the CTA
+// (8 columns per thread and pass, block sums in warp order), for launches of
+// a single row: the whole block shares the row's loads instead of one warp.
+template <int KCH, int IN>
+__device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, int m, const float* gam,
+                                                   const float* bet) {
+  constexpr int kG = (KCH * 32 + 127) / 128;  // 8-column groups per thread
+  __shared__ float ln_red[2][4];
+  const int K = a.K, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float* src0 = IN == IN_EMBED ? a.tok_emb + (size_t)row_token(a.rm, a.st, m) * K : a.r + (size_t)m * K;
+  const float* src1 = IN == IN_EMBED ? a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * K : nullptr;  // POSITION_OFFSET
+  float v[kG * 8];
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < kG; ++c) {
+    const int col = (t + 128 * c) * 8;
+    if (col < K) {
+      float4 p0 = *reinterpret_cast<const float4*>(src0 + col);
+      float4 p1 = *reinterpret_cast<const float4*>(src0 + col + 4);
+      if constexpr (IN == IN_EMBED) {
+        const float4 q0 = *reinterpret_cast<const float4*>(src1 + col);
+        const float4 q1 = *reinterpret_cast<const float4*>(src1 + col + 4);
+        p0.x += q0.x; p0.y += q0.y; p0.z += q0.z; p0.w += q0.w;
+        p1.x += q1.x; p1.y += q1.y; p1.z += q1.z; p1.w += q1.w;
+      }
+      v[c * 8 + 0] = p0.x; v[c * 8 + 1] = p0.y; v[c * 8 + 2] = p0.z; v[c * 8 + 3] = p0.w;
+      v[c * 8 + 4] = p1.x; v[c * 8 + 5] = p1.y; v[c * 8 + 6] = p1.z; v[c * 8 + 7] = p1.w;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[c * 8 + j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[c * 8 + j] = 0.f;
+    }
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) ln_red[0][warp] = sum;
+  __syncthreads();
+  const float mean = (((ln_red[0][0] + ln_red[0][1]) + ln_red[0][2]) + ln_red[0][3]) / (float)K;
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < kG; ++c) {
+    if ((t + 128 * c) * 8 < K) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[c * 8 + j] - mean;
+        sq = fmaf(d, d, sq);
+      }
+    }
+  }
+  sq = warp_sum(sq);
+  if (lane == 0) ln_red[1][warp] = sq;
+  __syncthreads();
+  const float var = ((ln_red[1][0] + ln_red[1][1]) + ln_red[1][2]) + ln_red[1][3];
+  const float rstd = rsqrtf(var / (float)K + kLnEps);
+  // x_out is written once per row, by CTA m % gridDim.x
+  const bool keep = a.x_out != nullptr && (m % gridDim.x) == blockIdx.x;
+#pragma unroll
+  for (int c = 0; c < kG; ++c) {
+    const int col = (t + 128 * c) * 8;
+    if (col < KCH * 256) {
+      uint4 packed = make_uint4(0, 0, 0, 0);
+      if (col < K) {
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = (v[c * 8 + j] - mean) * rstd * gam[col + j] + bet[col + j];
+        packed = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+        if (keep) {
+          float* dst = a.x_out + (size_t)m * K + col;
+          *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+        }
+      }
+      *reinterpret_cast<uint4*>(xs + col) = packed;
+    }
+  }
+}
+
 template <int KCH, int MC, int IN, int EPI>
 __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -236,7 +313,9 @@ __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
   for (int m0 = 0; m0 < a.M; m0 += MC) {
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
-    if constexpr (IN == IN_LN || IN == IN_EMBED) {
+    if constexpr ((IN == IN_LN || IN == IN_EMBED) && MC == 1) {
+      stage_ln_row_block<KCH, IN>(a, xs, m0, sgamma, sbeta);
+    } else if constexpr (IN == IN_LN || IN == IN_EMBED) {
       stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4, false, sgamma, sbeta);
     } else {
       for (int idx = threadIdx.x; idx < MC * (KP / 8); idx += blockDim.x) {
