@@ -351,7 +351,7 @@ int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, cons
   if (in == IN_LN || in == IN_EMBED) {
     const int kch = kch_for(a.K);
     LnFn fn = ln_fn(in, kch);
-    CK(launch_ex(fn, dim3((a.M + 3) / 4), dim3(128), 0, s, next_pdl(c), 0, a, c->xln));
+    CK(launch_ex(fn, dim3(a.M), dim3(128), 0, s, next_pdl(c), 0, a, c->xln));
     x = c->xln;
     ldx = kch * 256;
   } else if (in == IN_F32) {

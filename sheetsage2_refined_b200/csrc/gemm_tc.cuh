@@ -389,14 +389,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // LayerNorm (IN_LN) or embedding + LayerNorm (IN_EMBED) of rows [0, M) into
 // bfloat16 rows of stride KCH*256 (the tensor-core GEMM's X operand), and the
-// float32 rows into x_out.  One warp per row, 4 rows per CTA.
+// float32 rows into x_out.  One row per CTA, staged by all of its threads.
 template <int KCH, int IN>
 __global__ void __launch_bounds__(128) ln_rows_kernel(const ProjArgs a, bf16* __restrict__ xb) {
   pdl_launch_dependents();
   pdl_wait();
-  const int m0 = blockIdx.x * 4;
-  stage_ln_rows<KCH, IN>(a, xb + (size_t)m0 * (KCH * 256), m0, min(4, a.M - m0), threadIdx.x >> 5, threadIdx.x & 31,
-                         4, true);
+  // one row per CTA, staged by the whole block
+  const int m = blockIdx.x;
+  stage_ln_row_block<KCH, IN>(a, xb + (size_t)m * (KCH * 256), m, a.gamma, a.beta);
 }
 
 }  // namespace s2r

@@ -283,7 +283,10 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
   for (int m0 = 0; m0 < a.M; m0 += MC) {
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
-    stage_ln_rows<KCH, IN_LN>(pa, xs, m0, mc, warp, lane, NW);
+    if constexpr (MC == 1)
+      stage_ln_row_block<KCH, IN_LN, NW * 32>(pa, xs, m0, a.gamma, a.beta);
+    else
+      stage_ln_rows<KCH, IN_LN>(pa, xs, m0, mc, warp, lane, NW);
     for (int idx = threadIdx.x; idx < (MC - mc) * (KP / 8); idx += blockDim.x) {
       const int i = mc + idx / (KP / 8), col = (idx % (KP / 8)) * 8;
       *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = make_uint4(0, 0, 0, 0);

@@ -195,14 +195,15 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
   }
 }
 
-// One LayerNorm'd row (IN_LN or IN_EMBED) staged by all 128 threads of the CTA
+// One LayerNorm'd row (IN_LN or IN_EMBED) staged by all NT threads of the CTA
 // (8 columns per thread and pass, block sums in warp order), for launches of
 // a single row: the whole block shares the row's loads instead of one warp.
-template <int KCH, int IN>
+template <int KCH, int IN, int NT = 128>
 __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, int m, const float* gam,
                                                    const float* bet) {
-  constexpr int kG = (KCH * 32 + 127) / 128;  // 8-column groups per thread
-  __shared__ float ln_red[2][4];
+  constexpr int kG = (KCH * 32 + NT - 1) / NT;  // 8-column groups per thread
+  constexpr int kW = NT / 32;
+  __shared__ float ln_red[2][kW];
   const int K = a.K, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const float* src0 = IN == IN_EMBED ? a.tok_emb + (size_t)row_token(a.rm, a.st, m) * K : a.r + (size_t)m * K;
   const float* src1 = IN == IN_EMBED ? a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * K : nullptr;  // POSITION_OFFSET
@@ -210,7 +211,7 @@ __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, 
   float sum = 0.f;
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
-    const int col = (t + 128 * c) * 8;
+    const int col = (t + NT * c) * 8;
     if (col < K) {
       float4 p0 = *reinterpret_cast<const float4*>(src0 + col);
       float4 p1 = *reinterpret_cast<const float4*>(src0 + col + 4);
@@ -232,11 +233,14 @@ __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, 
   sum = warp_sum(sum);
   if (lane == 0) ln_red[0][warp] = sum;
   __syncthreads();
-  const float mean = (((ln_red[0][0] + ln_red[0][1]) + ln_red[0][2]) + ln_red[0][3]) / (float)K;
+  float mean = 0.f;
+#pragma unroll
+  for (int w = 0; w < kW; ++w) mean += ln_red[0][w];
+  mean /= (float)K;
   float sq = 0.f;
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
-    if ((t + 128 * c) * 8 < K) {
+    if ((t + NT * c) * 8 < K) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float d = v[c * 8 + j] - mean;
@@ -247,13 +251,15 @@ __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, 
   sq = warp_sum(sq);
   if (lane == 0) ln_red[1][warp] = sq;
   __syncthreads();
-  const float var = ((ln_red[1][0] + ln_red[1][1]) + ln_red[1][2]) + ln_red[1][3];
+  float var = 0.f;
+#pragma unroll
+  for (int w = 0; w < kW; ++w) var += ln_red[1][w];
   const float rstd = rsqrtf(var / (float)K + kLnEps);
   // x_out is written once per row, by CTA m % gridDim.x
   const bool keep = a.x_out != nullptr && (m % gridDim.x) == blockIdx.x;
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
-    const int col = (t + 128 * c) * 8;
+    const int col = (t + NT * c) * 8;
     if (col < KCH * 256) {
       uint4 packed = make_uint4(0, 0, 0, 0);
       if (col < K) {
