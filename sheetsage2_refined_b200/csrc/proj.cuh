@@ -324,7 +324,23 @@ __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
     } else if constexpr (IN == IN_LN || IN == IN_EMBED) {
       stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4, false, sgamma, sbeta);
     } else {
-      for (int idx = threadIdx.x; idx < MC * (KP / 8); idx += blockDim.x) {
+      if constexpr (IN == IN_BF16 && MC == 1) {
+        // one bf16 row: every piece of this thread requested before the first is stored
+        constexpr int kIt = (KP / 8 + 127) / 128;
+        uint4 got[kIt];
+#pragma unroll
+        for (int t = 0; t < kIt; ++t) {
+          const int col = (threadIdx.x + 128 * t) * 8;
+          got[t] = col < K ? *reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.xin) + (size_t)m0 * a.ldx + col)
+                           : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int t = 0; t < kIt; ++t) {
+          const int col = (threadIdx.x + 128 * t) * 8;
+          if (col < KP) *reinterpret_cast<uint4*>(xs + col) = got[t];
+        }
+      }
+      for (int idx = threadIdx.x; !(IN == IN_BF16 && MC == 1) && idx < MC * (KP / 8); idx += blockDim.x) {
         const int i = idx / (KP / 8), col = (idx % (KP / 8)) * 8;
         uint4 packed = make_uint4(0, 0, 0, 0);
         if (i < mc && col < K) {
