@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   __shared__ float xo[kAttnMaxSplits][kHeadDim];      // every rank's partial output
   __shared__ float wred[kAttnThreads / 32];
   __shared__ float wmax[kAttnThreads / 32], wsum[kAttnThreads / 32];
+  __shared__ __align__(16) bf16 sq[kHeadDim];  // kStage: the row's query for this head
   __shared__ __align__(8) uint64_t xbar[3];           // exchanges received: max, sum, output
   __shared__ float ohead[kHeadDim];                   // kFuseOut: the head's output, bf16-rounded
   __shared__ int is_last;
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   }
   const uint4 qraw = *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);
   if constexpr (kStage) {
+    if (grp == 0) *reinterpret_cast<uint4*>(sq + sub * 8) = qraw;
     // the rows of this step's own positions: plain loads into the stage
     for (int j = jbulk + grp; j < js; j += kAttnGroups) {
       const uint4 kk = ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8);
@@ -275,8 +277,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
 
   // ---- scores and local max
   float lmax = -INFINITY;
+  if constexpr (kStage) {
+    // One key per thread.  The eight 8-dimension partial dot products are the
+    // ones the 8-lane groups of the other paths form, added in the same
+    // butterfly order, so the scores are bit-identical to theirs.  Each lane
+    // starts at a different 16-byte piece, so the 8 lanes of a shared-memory
+    // phase read 8 different banks.
+    for (int j = j0 + tid; j < j1; j += kAttnThreads) {
+      const bf16* krow = j < js ? sk + (size_t)(j - j0) * kHeadDim : attn_row(a, a.k, slot, h, j);
+      float part8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c0 = 0; c0 < 8; ++c0) {
+        const int c = (c0 + lane) & 7;
+        const uint4 kk = j < js ? *reinterpret_cast<const uint4*>(krow + c * 8) : ld_stream(krow + c * 8);
+        const uint4 qq = *reinterpret_cast<const uint4*>(sq + c * 8);
+        float d = bf_lo(kk.x) * bf_lo(qq.x);
+        d = fmaf(bf_hi(kk.x), bf_hi(qq.x), d);
+        d = fmaf(bf_lo(kk.y), bf_lo(qq.y), d);
+        d = fmaf(bf_hi(kk.y), bf_hi(qq.y), d);
+        d = fmaf(bf_lo(kk.z), bf_lo(qq.z), d);
+        d = fmaf(bf_hi(kk.z), bf_hi(qq.z), d);
+        d = fmaf(bf_lo(kk.w), bf_lo(qq.w), d);
+        d = fmaf(bf_hi(kk.w), bf_hi(qq.w), d);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) part8[t] = t == c ? d : part8[t];  // static indices: registers
+      }
+      float s = ((part8[0] + part8[1]) + (part8[2] + part8[3])) + ((part8[4] + part8[5]) + (part8[6] + part8[7]));
+      s = round_bf16(s) * 0.125f;  // head_dim ** -0.5 for head_dim 64
+      sc[j - j0] = s;
+      lmax = fmaxf(lmax, s);
+    }
+  }
   // The loop bound is uniform across the block (the shuffles below need all lanes).
-  for (int base = j0; base < j1; base += kAttnGroups * kU) {
+  for (int base = j0; !kStage && base < j1; base += kAttnGroups * kU) {
     const int jb = base + grp;
     uint4 kv[kU];
 #pragma unroll
