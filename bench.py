@@ -218,7 +218,8 @@ def load_launches(eng) -> int:
     The cross K/V projection (one launch per layer), then the one-row prefill
     of position 0: a full layer but only the K/V projection in the last one
     (6 launches per layer with the attention fused with its out-projection,
-    11 on tensor-core engines with their LayerNorm launches); the one-kernel
+    5 when the cross attention also computes its query rows, 11 on
+    tensor-core engines with their LayerNorm launches); the one-kernel
     step engine prefills with one launch.
     """
 
@@ -229,6 +230,8 @@ def load_launches(eng) -> int:
         return L + 11 * (L - 1) + 2
     if per_step == 6 * L + 1:  # attention fused with its out-projection
         return L + 6 * (L - 1) + 1
+    if per_step == 5 * L + 1:  # ... and the cross attention computing its own query rows
+        return L + 5 * (L - 1) + 1
     return L + 8 * (L - 1) + 1
 
 

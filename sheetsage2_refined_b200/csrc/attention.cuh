@@ -56,6 +56,12 @@ struct AttnArgs {
   unsigned* ticket;          // [M] arrivals per row, zero between launches
   float* x;                  // [M][D] float32: residual input, then the LayerNorm output
   bf16* xn;                  // [M][D] the LayerNorm output in bf16 (the next projection's input)
+  // fuse_q (cross attention, kAttnPreStage with kFuseOut, 8 splits, D <= 1024): the kernel
+  // computes its head's query rows itself, q = bf16(xq Wq^T + bq), 8 rows per CTA
+  const bf16* wq;  // [D, D]
+  const bf16* bq;  // [D]
+  const bf16* xq;  // [M, D]: the LayerNorm output the projection reads
+  int fuse_q;
 };
 
 constexpr int kAttnLnHeads = 16;     // head partials the fused LayerNorm requests at once
@@ -78,7 +84,8 @@ constexpr size_t kAttnOtherSmem = 32768;
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxSplits = 8;  // CTAs per (row, head) at most
 constexpr int kAttnGroups = kAttnThreads / 8;  // 8 lanes x 16 bytes per key row
-constexpr int kAttnUnroll = 4;       // keys per group and pass (kAttnPreNone / kAttnPreRegs)
+constexpr int kAttnUnroll = 4;
+constexpr int kAttnQRows = 8;  // fuse_q: query rows computed per CTA (one per warp)       // keys per group and pass (kAttnPreNone / kAttnPreRegs)
 constexpr int kAttnUnrollStaged = 8;  // the same from shared memory (kAttnPreStage): more keys in flight
 
 __device__ __forceinline__ uint32_t pack_bf16_pair(float a, float b) {
@@ -96,8 +103,8 @@ __device__ __forceinline__ const bf16* attn_row(const AttnArgs& a, const bf16* b
 // rows and (with kFuseOut) the residual row, LayerNorm weights and
 // out-projection bias of the fused tail.  Every part starts 16-byte aligned.
 struct AttnSmem {
-  size_t part, sk, sv, sx, sg, sb, sbo, total;
-  __host__ __device__ AttnSmem(int chunk_cap, int stage_cap, int D, bool ln_stage) {
+  size_t part, sk, sv, sx, sg, sb, sbo, sw, total;
+  __host__ __device__ AttnSmem(int chunk_cap, int stage_cap, int D, bool ln_stage, bool fuse_q = false) {
     part = (size_t)((chunk_cap + 3) & ~3) * 4;
     sk = part + (size_t)kAttnGroups * kHeadDim * 4;
     sv = sk + (size_t)stage_cap * kHeadDim * 2;
@@ -105,7 +112,8 @@ struct AttnSmem {
     sg = sx + (ln_stage ? (size_t)D * 4 : 0);
     sb = sg + (ln_stage ? (size_t)D * 4 : 0);
     sbo = sb + (ln_stage ? (size_t)D * 4 : 0);
-    total = sbo + (ln_stage ? (size_t)D * 2 : 0);
+    sw = sbo + (ln_stage ? (((size_t)D * 2 + 15) & ~(size_t)15) : 0);
+    total = sw + (fuse_q ? (size_t)kAttnQRows * D * 2 : 0);
   }
 };
 
@@ -144,7 +152,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   const int rank = (int)cluster.block_rank();
   const int h = blockIdx.y, m = a.order ? a.order[blockIdx.z] : (int)blockIdx.z;
   extern __shared__ __align__(16) unsigned char attn_smem[];
-  const AttnSmem lay(a.chunk_cap, kStage ? a.stage_cap : 0, a.D, kLnStage);
+  const bool fuse_q = kLnStage && a.fuse_q;
+  const AttnSmem lay(a.chunk_cap, kStage ? a.stage_cap : 0, a.D, kLnStage, fuse_q);
   float* sc = reinterpret_cast<float*>(attn_smem);                // [chunk_cap] scores, then exp values
   float* part = reinterpret_cast<float*>(attn_smem + lay.part);   // [kAttnGroups][64] partial outputs
   bf16* sk = reinterpret_cast<bf16*>(attn_smem + lay.sk);         // kStage: [stage_cap][64] keys
@@ -153,12 +162,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   float* sg = reinterpret_cast<float*>(attn_smem + lay.sg);       //           LayerNorm weight [D]
   float* sb = reinterpret_cast<float*>(attn_smem + lay.sb);       //           LayerNorm bias [D]
   bf16* sbo = reinterpret_cast<bf16*>(attn_smem + lay.sbo);       //           out-projection bias [D]
+  bf16* sw = reinterpret_cast<bf16*>(attn_smem + lay.sw);         // fuse_q: this CTA's query weight rows [8][D]
   __shared__ float xred[2][kAttnMaxSplits];          // every rank's partial max and sum
   __shared__ float xo[kAttnMaxSplits][kHeadDim];      // every rank's partial output
   __shared__ float wred[kAttnThreads / 32];
   __shared__ float wmax[kAttnThreads / 32], wsum[kAttnThreads / 32];
   __shared__ __align__(16) bf16 sq[kHeadDim];  // kStage: the row's query for this head
-  __shared__ __align__(8) uint64_t xbar[3];           // exchanges received: max, sum, output
+  __shared__ __align__(8) uint64_t xbar[4];           // exchanges received: max, sum, output, query
+  __shared__ float sqx[kHeadDim];                     // fuse_q: the head's query, from every rank
   __shared__ float ohead[kHeadDim];                   // kFuseOut: the head's output, bf16-rounded
   __shared__ int is_last;
   __shared__ __align__(8) uint64_t bars[2];           // kStage: [0] rows + weights, [1] residual row
@@ -195,7 +206,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   // rank with kFuseOut, else to rank 0 alone
   const bool gets_o = kFuseOut || rank == 0;
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(&xbar[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 1);
     if constexpr (kStage) {
       mbar_init(&bars[0], 1);
       mbar_init(&bars[1], 1);
@@ -204,10 +215,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     mbar_expect_tx(&xbar[0], (unsigned)C * 4);
     mbar_expect_tx(&xbar[1], (unsigned)C * 4);
     mbar_expect_tx(&xbar[2], gets_o ? (unsigned)(C * kHeadDim * 4) : 0u);
+    mbar_expect_tx(&xbar[3], fuse_q ? (unsigned)(kHeadDim * 4) : 0u);
   }
   if constexpr (kStage) {
     if (tid == 0) {
-      mbar_expect_tx(&bars[0], (unsigned)(jbulk - j0) * (2 * kHeadDim * 2) + (kLnStage ? (unsigned)a.D * 10 : 0u));
+      mbar_expect_tx(&bars[0], (unsigned)(jbulk - j0) * (2 * kHeadDim * 2) + (kLnStage ? (unsigned)a.D * 10 : 0u) +
+                                   (fuse_q ? (unsigned)(kAttnQRows * a.D * 2) : 0u));
       // one copy per run of rows that is contiguous in memory (a page of the
       // self-attention pool; the whole range for cross-attention)
       for (int s = j0; s < jbulk;) {
@@ -221,6 +234,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         bulk_load(sg, a.ln_g, (unsigned)a.D * 4, &bars[0]);
         bulk_load(sb, a.ln_b, (unsigned)a.D * 4, &bars[0]);
         bulk_load(sbo, a.bo, (unsigned)a.D * 2, &bars[0]);
+        if (fuse_q)  // the CTA's 8 query rows of head h: contiguous in Wq
+          bulk_load(sw, a.wq + (size_t)(h * kHeadDim + rank * kAttnQRows) * a.D, (unsigned)(kAttnQRows * a.D * 2),
+                    &bars[0]);
       }
     }
   }
@@ -231,6 +247,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       wpre[p] = (i < per && n < a.D) ? ld_stream(a.wo + (size_t)n * a.D + h * kHeadDim + sub * 8) : make_uint4(0, 0, 0, 0);
     }
   }
+  // fuse_q: the bias of this warp's query row
+  const float qbias = fuse_q && lane == 0 ? __bfloat162float(a.bq[h * kHeadDim + rank * kAttnQRows + warp]) : 0.f;
   if constexpr (kPre == kAttnPreRegs) {
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -260,9 +278,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       bulk_load(sx, a.x + (size_t)m * a.D, (unsigned)a.D * 4, &bars[1]);
     }
   }
-  const uint4 qraw = *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);
+  const uint4 qraw = fuse_q ? make_uint4(0, 0, 0, 0)
+                            : *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);
+  if constexpr (kLnStage) {
+    if (fuse_q) {
+      // This CTA's 8 query rows of head h, one per warp, with the projection
+      // kernel's arithmetic (16-byte pieces of 8 products, pieces added in
+      // order, then the warp butterfly; + bias, rounded to bf16), sent to
+      // every rank of the cluster.
+      const int kch = a.D / 256;
+      const bf16* xrow = a.xq + (size_t)m * a.D;
+      uint4 xv[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        xv[c] = c < kch ? *reinterpret_cast<const uint4*>(xrow + c * 256 + lane * 8) : make_uint4(0, 0, 0, 0);
+      staged = mbar_wait(&bars[0], 0);  // the weight rows came with the stage
+      const bf16* wrow = sw + (size_t)warp * a.D;
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= kch) break;
+        const uint4 w = *reinterpret_cast<const uint4*>(wrow + c * 256 + lane * 8);
+        float d = bf_lo(w.x) * bf_lo(xv[c].x);
+        d = fmaf(bf_hi(w.x), bf_hi(xv[c].x), d);
+        d = fmaf(bf_lo(w.y), bf_lo(xv[c].y), d);
+        d = fmaf(bf_hi(w.y), bf_hi(xv[c].y), d);
+        d = fmaf(bf_lo(w.z), bf_lo(xv[c].z), d);
+        d = fmaf(bf_hi(w.z), bf_hi(xv[c].z), d);
+        d = fmaf(bf_lo(w.w), bf_lo(xv[c].w), d);
+        d = fmaf(bf_hi(w.w), bf_hi(xv[c].w), d);
+        acc += d;
+      }
+      acc = warp_sum(acc);
+      cluster_wait();  // every peer has started: the first store into its shared memory follows
+      if (lane == 0) {
+        const float qb = round_bf16(acc + qbias);
+        for (int r = 0; r < C; ++r) st_async_f32(&sqx[rank * kAttnQRows + warp], r, qb, &xbar[3]);
+      }
+    }
+  }
   if constexpr (kStage) {
-    if (grp == 0) *reinterpret_cast<uint4*>(sq + sub * 8) = qraw;
+    if (grp == 0 && !fuse_q) *reinterpret_cast<uint4*>(sq + sub * 8) = qraw;
     // the rows of this step's own positions: plain loads into the stage
     for (int j = jbulk + grp; j < js; j += kAttnGroups) {
       const uint4 kk = ld_stream(attn_row(a, a.k, slot, h, j) + sub * 8);
@@ -272,6 +328,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     }
     staged = mbar_wait(&bars[0], 0);
     if (!staged) atomicExch(a.err, kErrAttnStage);
+    if (fuse_q) {
+      if (!mbar_wait(&xbar[3], 0)) atomicExch(a.err, kErrAttnExchange);
+      if (tid < kHeadDim) sq[tid] = __float2bfloat16_rn(sqx[tid]);  // bf16 values already
+    }
     __syncthreads();
   }
 
@@ -346,7 +406,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   lmax = warp_max(lmax);
   if (lane == 0) wmax[warp] = lmax;
   __syncthreads();
-  cluster_wait();
+  if (!fuse_q) cluster_wait();  // (with fuse_q the query exchange waited already)
   if (tid < C) {  // thread r sends this CTA's max to rank r
     float v = wmax[0];
     for (int w = 1; w < kAttnThreads / 32; ++w) v = fmaxf(v, wmax[w]);

@@ -436,7 +436,47 @@ int upload_row_order(s2r_ctx* c, cudaStream_t s) {
   return S2R_OK;
 }
 
+// How an attention launch of M rows gets its keys (kAttnPre*), how many rows
+// it stages, whether it computes its own query rows, and its dynamic shared
+// memory.  The same for every launch of an engine with the same M.
+struct AttnPlan {
+  int C = 1, chunk_cap = 0, pre = kAttnPreNone, stage_cap = 0;
+  bool fuse_q = false;
+  size_t smem = 0;
+};
+
+AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
+  AttnPlan p;
+  p.C = cross ? c->attn_splits_cross : c->attn_splits;
+  p.chunk_cap = ((cross ? c->F : c->T) + p.C - 1) / p.C;
+  p.pre = c->tc ? kAttnPreNone : kAttnPreRegs;
+  // the cross attention of a fused engine can compute its own query rows
+  // (8 per CTA, one per warp) when it stages and splits 8 ways
+  const bool can_fuse_q = cross && c->fuse_out && p.C * kAttnQRows == kHeadDim && c->D % 256 == 0 && c->D <= 1024;
+  if (!c->tc) {
+    // Stage the CTAs' earlier keys and values in shared memory when the
+    // launch fits on the SMs in one wave with room left for a CTA of the
+    // other attention kernel beside each and for the projection kernels in
+    // flight (kernels start ahead of their inputs under PDL).
+    const int ctas = M * c->H * p.C;
+    const int per_sm = std::max(1, (ctas + c->num_sms - 1) / c->num_sms);
+    const size_t budget = ((size_t)c->smem_per_sm - kAttnOtherSmem) / (2 * per_sm);
+    const size_t fixed = AttnSmem(p.chunk_cap, 0, c->D, c->fuse_out, can_fuse_q).total + kAttnStaticSmem;
+    if (budget > fixed) {
+      const int cap = (int)std::min<size_t>(p.chunk_cap, (budget - fixed) / (2 * kHeadDim * 2));
+      if (cap == p.chunk_cap || cap >= kAttnGroups * kAttnUnroll) {
+        p.pre = kAttnPreStage;
+        p.stage_cap = cap;
+        p.fuse_q = can_fuse_q;
+      }
+    }
+  }
+  p.smem = AttnSmem(p.chunk_cap, p.stage_cap, c->D, p.pre == kAttnPreStage && c->fuse_out, p.fuse_q).total;
+  return p;
+}
+
 int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s) {
+  const AttnPlan plan = plan_attn(c, M, cross);
   AttnArgs a{};
   a.M = M;
   a.H = c->H;
@@ -451,7 +491,7 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   a.v = cross ? c->layers[layer].cv : c->layers[layer].vpool;
   a.pages_per_slot = c->pps;
   a.frames_cap = c->F;
-  const int C = cross ? c->attn_splits_cross : c->attn_splits;
+  const int C = plan.C;
   a.splits = C;
   a.err = c->dev_error;
   a.order = rm.prefill ? nullptr : (cross ? c->order_cross : c->order_self);
@@ -466,28 +506,17 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
     a.ticket = c->attn_ticket;
     a.x = c->x;
     a.xn = c->xn;
-  }
-  const int maxlen = cross ? c->F : c->T;
-  a.chunk_cap = (maxlen + C - 1) / C;
-  int pre = c->tc ? kAttnPreNone : kAttnPreRegs;
-  if (!c->tc) {
-    // Stage the CTAs' earlier keys and values in shared memory when the
-    // launch fits on the SMs in one wave with room left for a CTA of the
-    // other attention kernel beside each and for the projection kernels in
-    // flight (kernels start ahead of their inputs under PDL).
-    const int ctas = M * c->H * C;
-    const int per_sm = std::max(1, (ctas + c->num_sms - 1) / c->num_sms);
-    const size_t budget = ((size_t)c->smem_per_sm - kAttnOtherSmem) / (2 * per_sm);
-    const size_t fixed = AttnSmem(a.chunk_cap, 0, c->D, c->fuse_out).total + kAttnStaticSmem;
-    if (budget > fixed) {
-      const int cap = (int)std::min<size_t>(a.chunk_cap, (budget - fixed) / (2 * kHeadDim * 2));
-      if (cap == a.chunk_cap || cap >= kAttnGroups * kAttnUnroll) {
-        pre = kAttnPreStage;
-        a.stage_cap = cap;
-      }
+    if (plan.fuse_q) {
+      a.wq = w.wcq;
+      a.bq = w.bcq;
+      a.xq = c->xn;
+      a.fuse_q = 1;
     }
   }
-  const size_t smem = AttnSmem(a.chunk_cap, a.stage_cap, c->D, pre == kAttnPreStage && c->fuse_out).total;
+  a.chunk_cap = plan.chunk_cap;
+  a.stage_cap = plan.stage_cap;
+  const int pre = plan.pre;
+  const size_t smem = plan.smem;
   void (*fn)(const AttnArgs) =
       pre == kAttnPreNone    ? attn_kernel<kAttnPreNone, false>
       : pre == kAttnPreRegs  ? (c->fuse_out ? attn_kernel<kAttnPreRegs, true> : attn_kernel<kAttnPreRegs, false>)
@@ -534,7 +563,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     // projections after them read the bf16 LayerNorm output
     TRY(launch_attn(c, rm, M, l, false, s));  // 2-3. self-attention ... self_attn_norm
     TRY(mark(c, K_SELF_ATTN, s));
-    {  // 4. cross q
+    if (!plan_attn(c, M, true).fuse_q) {  // 4. cross q (else the cross attention computes it)
       ProjArgs a = proj_base(c);
       a.rm = rm;
       a.M = M;
@@ -1581,6 +1610,10 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
     per[K_SELF_ATTN] += per[K_SELF_OUT];
     per[K_CROSS_ATTN] += per[K_CROSS_OUT];
     per[K_SELF_OUT] = per[K_CROSS_OUT] = 0.0;
+    if (plan_attn(c, c->B, true).fuse_q) {  // and so does the cross q projection
+      per[K_CROSS_ATTN] += per[K_CROSS_Q];
+      per[K_CROSS_Q] = 0.0;
+    }
   }
   for (int b = 0; b < c->B; ++b) {
     if (!c->loaded[b]) continue;
@@ -1647,7 +1680,11 @@ int32_t s2r_step_launches(s2r_ctx* c) {
   if (!c) return 0;
   if (c->persistent) return 1;
   // tensor-core engines add a LayerNorm launch before each LayerNorm'd projection and the logits
-  return c->tc ? 11 * c->L + 2 : c->fuse_out ? 6 * c->L + 1 : 8 * c->L + 1;
+  if (c->tc) return 11 * c->L + 2;
+  if (!c->fuse_out) return 8 * c->L + 1;
+  // attention fused with its out-projection; the cross q launch folds into
+  // the cross attention when that computes its own query rows
+  return (plan_attn(c, c->B, true).fuse_q ? 5 : 6) * c->L + 1;
 }
 
 int32_t s2r_free_pages(s2r_ctx* c) { return c ? (int32_t)c->free_pages.size() : 0; }
