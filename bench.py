@@ -652,11 +652,12 @@ def profile(eng):
 
 
 # DRAM traffic of the attention launches (dram__bytes_read.sum + dram__bytes_write.sum, one ncu
-# capture each; profiles/): per launch at the single-song workload's position ~1,024, and as a
-# ratio to the algorithmic bytes for the batched workload, whose launches are too large to
-# capture (a one-row launch of the same kernel on the small case; traffic grows with the rows'
-# keys, so the ratio carries over).
-NCU_TRAFFIC = {("single", "self_attn"): 4_244_480, ("single", "cross_attn"): 6_184_960}
+# capture each; profiles/): per launch at the single-song workload's position ~1,025 (the fused
+# launches: self attention + out-projection; cross attention + its query rows + out-projection),
+# and as a ratio to the algorithmic bytes for the batched workload, whose launches are too large
+# to capture (a one-row launch of the same kernel on the small case; traffic grows with the
+# rows' keys, so the ratio carries over).
+NCU_TRAFFIC = {("single", "self_attn"): 6_403_584, ("single", "cross_attn"): 10_443_520}
 NCU_TRAFFIC_RATIO = {(w, k): 3_097_088 / 3_096_576 for w in ("batched", "box", "long") for k in ("cross_attn", "self_attn")}
 
 
