@@ -392,8 +392,9 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
   const size_t smem = (size_t)(mc == 8 ? 8 : mc) * kch * 256 * sizeof(bf16) +
                       ((in == IN_LN || in == IN_EMBED) ? 2 * (size_t)kch * 256 * sizeof(float) : 0);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const int blocks = (a.N + 3) / 4;
-  CK(launch_ex(fn, dim3(blocks), dim3(128), smem, s, next_pdl(c), 0, a));
+  const int threads = mc == 1 ? proj_threads<1>() : proj_threads<2>(), warps = threads / 32;
+  const int blocks = (a.N + warps - 1) / warps;
+  CK(launch_ex(fn, dim3(blocks), dim3(threads), smem, s, next_pdl(c), 0, a));
   return S2R_OK;
 }
 

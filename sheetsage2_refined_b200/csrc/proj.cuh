@@ -278,8 +278,17 @@ __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, 
   }
 }
 
+// Threads per CTA of proj_kernel: 8 warps for single-row launches (the row's
+// staging is shared by twice as many output rows), else 4.
+template <int MC>
+__host__ __device__ constexpr int proj_threads() {
+  return MC == 1 ? 256 : 128;
+}
+
 template <int KCH, int MC, int IN, int EPI>
-__global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
+__global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs a) {
+  constexpr int NT = proj_threads<MC>();
+  constexpr int kWarps = NT / 32;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int KP = KCH * 256;
   constexpr bool kLn = IN == IN_LN || IN == IN_EMBED;
@@ -288,8 +297,8 @@ __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
   float* sbeta = sgamma + KP;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int K = a.K;
-  const int stride = gridDim.x * 4;
-  const int first = blockIdx.x * 4 + warp;
+  const int stride = gridDim.x * kWarps;
+  const int first = blockIdx.x * kWarps + warp;
 
   // The weights do not depend on earlier kernels: start streaming this warp's
   // first row before waiting for them.
@@ -320,23 +329,23 @@ __global__ void __launch_bounds__(128) proj_kernel(const ProjArgs a) {
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
     if constexpr ((IN == IN_LN || IN == IN_EMBED) && MC == 1) {
-      stage_ln_row_block<KCH, IN>(a, xs, m0, sgamma, sbeta);
+      stage_ln_row_block<KCH, IN, NT>(a, xs, m0, sgamma, sbeta);
     } else if constexpr (IN == IN_LN || IN == IN_EMBED) {
       stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4, false, sgamma, sbeta);
     } else {
       if constexpr (IN == IN_BF16 && MC == 1) {
         // one bf16 row: every piece of this thread requested before the first is stored
-        constexpr int kIt = (KP / 8 + 127) / 128;
+        constexpr int kIt = (KP / 8 + NT - 1) / NT;
         uint4 got[kIt];
 #pragma unroll
         for (int t = 0; t < kIt; ++t) {
-          const int col = (threadIdx.x + 128 * t) * 8;
+          const int col = (threadIdx.x + NT * t) * 8;
           got[t] = col < K ? *reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.xin) + (size_t)m0 * a.ldx + col)
                            : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int t = 0; t < kIt; ++t) {
-          const int col = (threadIdx.x + 128 * t) * 8;
+          const int col = (threadIdx.x + NT * t) * 8;
           if (col < KP) *reinterpret_cast<uint4*>(xs + col) = got[t];
         }
       }
