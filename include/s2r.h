@@ -243,9 +243,10 @@ int32_t s2r_free_pages(s2r_ctx* ctx);
  * logits[r][v] + bias[v] : -inf), lowest index on ties, 0 for a row with
  * nothing allowed.  `logits` [rows, vocab] float32, `bias` [vocab] float32 or
  * NULL, `allowed` [rows, vocab] uint8, `out` [rows] int64, all device memory.
- * For callers that must not allocate while decoding: code that records a
- * CUDA graph (an allocation cannot be captured) or a host that gives all
- * device memory to its own pool allocator up front.  Its cross-CTA scratch is
+ * For callers that cannot call cudaMalloc while decoding: a host whose pool
+ * allocator reserves all device memory up front and forbids allocations
+ * outside it, or a serving loop that must not stall the device (cudaFree
+ * synchronises it, cudaMalloc may too).  Its cross-CTA scratch is
  * a static device array of 1024 rows + 1 counter, one copy per GPU that loads
  * the library; rows > 1024 fail with S2R_EINVAL.  Every call shares that
  * array, so calls that overlap on the GPU race; each call clears it first.

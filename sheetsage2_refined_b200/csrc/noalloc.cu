@@ -9,10 +9,10 @@
 // file-scope device array instead of memory the engine allocates, so a call
 // makes no cudaMalloc / cudaFree and touches no allocator.
 //
-// Who needs it: callers that must not allocate device memory while they
-// decode, such as code recording a CUDA graph (an allocation cannot be
-// captured and would break the capture) or a host that hands all device
-// memory to its own pool allocator up front and forbids stray allocations.
+// Who needs it: callers that cannot call cudaMalloc while they decode, such
+// as a host that hands all device memory to its own pool allocator up front
+// and forbids stray allocations, or a serving loop that must not stall the
+// device (cudaFree synchronises it, and cudaMalloc may).
 //
 // Limits and sharing: at most kNoAllocMaxRows rows per call.  The scratch
 // array is process-wide (every GPU that loads the library holds its own copy

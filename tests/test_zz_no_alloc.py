@@ -1,8 +1,9 @@
 """The allocation-free masked argmax entry point against the engine's own selection.
 
-``s2r_masked_argmax_noalloc`` is for callers that must not allocate device
-memory while decoding (code recording a CUDA graph, or a host whose pool
-allocator owns all device memory).  It must pick exactly the token the
+``s2r_masked_argmax_noalloc`` is for callers that cannot call cudaMalloc
+while decoding (a host whose pool allocator reserves all device memory up
+front, or a serving loop that must not stall the device, which cudaFree
+synchronises).  It must pick exactly the token the
 engine's fused logits kernel picks: this test runs the engine one step at a
 time through ``s2r_step_debug`` (which returns the raw logits and the greedy
 choice), rebuilds the grammar mask from the slots' state before the step, and
