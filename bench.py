@@ -182,27 +182,30 @@ class CpuDecoder:
             while n < min_tokens or time.perf_counter() - t0 < seconds:
                 self.eng.step()
                 n += 1
-            return n / (time.perf_counter() - t0), n, cores
+            dt = time.perf_counter() - t0
+            return n / dt, n, cores, dt
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     cpu = CpuDecoder()
-    values = []
+    values, seconds = [], []
     tokens = 0
     for _ in range(args.warmup):
         cpu.sample(seconds=0.5, min_tokens=2)
     for _ in range(args.steps):
-        v, n, cores = cpu.sample(seconds=args.cpu_seconds / max(args.steps, 1), min_tokens=4)
+        v, n, cores, dt = cpu.sample(seconds=args.cpu_seconds / max(args.steps, 1), min_tokens=4)
         values.append(v)
+        seconds.append(dt)
         tokens += n
     value = statistics.mean(values)
     sample = (f"single-song workload: greedy decode from position 1, {tokens} tokens over {args.steps} steps, "
               "float32 numpy restatement of the reference CPU path")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(seconds),
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": single_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
@@ -602,7 +605,7 @@ def run_b200(args, world, rank, local):
 
     cpu = None
     if world == 1 and not args.no_cpu:
-        v, n, cores = CpuDecoder().sample(seconds=args.cpu_seconds)
+        v, n, cores, _ = CpuDecoder().sample(seconds=args.cpu_seconds)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} greedy tokens of the single-song workload from position 1 (load excluded), "
                          "float32 numpy restatement of the reference CPU path, all host cores"}
