@@ -1,0 +1,42 @@
+"""``bench.py --impl reference`` (the CPU arm) keeps the bench line contract,
+and under a multi-rank launch only rank 0 runs and prints it."""
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+CMD = [sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "1", "--cpu-seconds", "1"]
+
+
+def run(env_extra: dict) -> subprocess.CompletedProcess:
+    env = {**os.environ, **env_extra}
+    return subprocess.run(CMD, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+
+
+def test_reference_arm_prints_one_contract_line():
+    out = run({"RANK": "0", "WORLD_SIZE": "1", "LOCAL_RANK": "0"})
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference"
+    assert line["steps"] == 2 and line["warmup"] == 1 and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    # a step is one bounded sample of about cpu-seconds / steps of decode
+    assert 100.0 < line["ms_per_step"] < 60_000.0
+    assert line["config"]["workload"].startswith("single-song decode")
+
+
+def test_reference_arm_other_ranks_exit_without_work():
+    out = run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert not [l for l in out.stdout.splitlines() if l.startswith("{")]
