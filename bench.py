@@ -272,6 +272,25 @@ class SingleSong:
         assert done == [0] and len(tokens) == SINGLE_TOKENS + 3
         return SINGLE_TOKENS
 
+    def time_load(self, k: int = 5) -> dict:
+        """CUDA-event time of one window's ``load`` (memory resident on the device)."""
+
+        torch = self.torch
+        stream = torch.cuda.current_stream(self.device)
+        ms = []
+        for _ in range(k):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            self.eng.load(0, self.mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+            end.record(stream)
+            torch.cuda.synchronize(self.device)
+            ms.append(start.elapsed_time(end))
+        flop = 2.0 * SINGLE_FRAMES * CONFIG.width * 2 * CONFIG.width * CONFIG.layers
+        return {"ms": statistics.median(ms), "loads": k, "frames": SINGLE_FRAMES, "prefix_tokens": 2,
+                "cross_kv_gflop": flop / 1e9,
+                "what": "one window's load: memory copy, cross K/V projection of every layer on the tcgen05 GEMM, "
+                        "slot state, prefill of position 0"}
+
     def prepare_profile(self):
         self.eng.load(0, self.mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)
         self.eng.run(SINGLE_TOKENS // 2)
@@ -595,6 +614,7 @@ def run_b200(args, world, rank, local):
     launches = work.launches - launches0
     clock_summary = clocks.summary()
     ms_e2e, tokens_e2e = timed(work.step_e2e, max(1, args.steps // 2))
+    load = work.time_load() if hasattr(work, "time_load") else None
 
     ms_max = reduce_max(ms, world, device)
     ms_e2e_max = reduce_max(ms_e2e, world, device)
@@ -628,6 +648,8 @@ def run_b200(args, world, rank, local):
                                for k, v in prof["classes"].items()},
             "cpu_baseline": cpu,
         }
+        if load is not None:
+            line["load"] = load
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:
