@@ -170,13 +170,14 @@ class CpuDecoder:
                       target=SINGLE_TOKENS)
         self.eng.step()  # warm-up
 
-    def sample(self, seconds: float, min_tokens: int = 4):
-        """Greedy tokens for ``seconds`` of decode; returns (tokens/s, tokens, cores)."""
+    def sample(self, seconds: float, min_tokens: int = 4, threads: int | None = None):
+        """Greedy tokens for ``seconds`` of decode on ``threads`` threads (default: every host core);
+        returns (tokens/s, tokens, threads, seconds)."""
 
         from threadpoolctl import threadpool_limits
 
-        cores = os.cpu_count() or 1
-        # every host core, also under torchrun (which sets OMP_NUM_THREADS=1 per rank)
+        cores = threads or os.cpu_count() or 1
+        # every host core by default, also under torchrun (which sets OMP_NUM_THREADS=1 per rank)
         with threadpool_limits(limits=cores):
             n, t0 = 0, time.perf_counter()
             while n < min_tokens or time.perf_counter() - t0 < seconds:
@@ -200,6 +201,7 @@ def run_reference(args, world, rank):
         seconds.append(dt)
         tokens += n
     value = statistics.mean(values)
+    one, one_n, _, _ = cpu.sample(seconds=max(2.0, args.cpu_seconds / 4), min_tokens=2, threads=1)
     sample = (f"single-song workload: greedy decode from position 1, {tokens} tokens over {args.steps} steps, "
               "float32 numpy restatement of the reference CPU path")
     line = {
@@ -208,7 +210,8 @@ def run_reference(args, world, rank):
         "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": single_config(args.gpus),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample,
+                         "one_thread": {"value": one, "tokens": one_n}},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -625,10 +628,13 @@ def run_b200(args, world, rank, local):
 
     cpu = None
     if world == 1 and not args.no_cpu:
-        v, n, cores, _ = CpuDecoder().sample(seconds=args.cpu_seconds)
+        cpu_dec = CpuDecoder()
+        v, n, cores, _ = cpu_dec.sample(seconds=args.cpu_seconds)
+        one, one_n, _, _ = cpu_dec.sample(seconds=max(2.0, args.cpu_seconds / 4), min_tokens=2, threads=1)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} greedy tokens of the single-song workload from position 1 (load excluded), "
-                         "float32 numpy restatement of the reference CPU path, all host cores"}
+                         "float32 numpy restatement of the reference CPU path, all host cores",
+               "one_thread": {"value": one, "tokens": one_n}}
 
     if rank == 0:
         peak, peak_kind = peaks()

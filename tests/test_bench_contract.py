@@ -29,6 +29,7 @@ def test_reference_arm_prints_one_contract_line():
     assert line["steps"] == 2 and line["warmup"] == 1 and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["one_thread"]["value"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     # a step is one bounded sample of about cpu-seconds / steps of decode
