@@ -65,3 +65,40 @@ def test_two_rank_gather_over_gloo():
     shares = partition_songs(costs, 2)
     for i, (rank, song, cost) in merged.items():
         assert song == i and cost == costs[i] and i in shares[rank]
+
+
+def _timing_rank(rank, world, port, queue):
+    import sys
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cpu = torch.device("cpu")
+        slowest = bench.reduce_max(100.0 + rank, world, cpu)  # each rank's device time, ms
+        tokens = bench.reduce_sum(2048.0 * (rank + 1), world, cpu)
+        if rank == 0:
+            queue.put((slowest, tokens))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_takes_the_slowest_rank_and_all_tokens_over_gloo():
+    """The bench's whole-job value: tokens of every rank over the slowest rank's time."""
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_timing_rank, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    slowest, tokens = queue.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert slowest == 101.0 and tokens == 2048.0 * 3
