@@ -183,6 +183,7 @@ class BatchDecoder:
         self.out = self._view("out").view(batch, self.max_tokens)
         self.bound = [0] * batch
         self.loaded = [False] * batch
+        self._inflight: list = []  # (event, sources) of loads whose copies may still be pending
 
     def _set_rescore(self, vocab) -> None:
         """The rescoring configuration of engine.py:81-116 for the C ABI."""
@@ -225,9 +226,23 @@ class BatchDecoder:
             keep.append(t)
             ptrs[i], rows[i] = t.data_ptr(), t.shape[0]
         _lib.check(self._lib.s2r_load_frame_tables(self._ctx, slot, ptrs, rows, self._stream()))
-        self._keep_tables = keep  # copies are ordered on the stream; keep the sources alive
+        return keep
 
     # ------------------------------------------------------------ plumbing
+    def _retain(self, sources) -> None:
+        """Keep a load's source tensors alive until the stream has run the copies that read them.
+
+        The engine copies ``memory`` and the frame tables asynchronously on the
+        current stream, so a pinned host or device tensor that the caller drops
+        right after ``load`` could otherwise be handed out again before the copy
+        reads it.  Sources whose copies have completed are released here.
+        """
+
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.device))
+        self._inflight = [(e, s) for e, s in self._inflight if not e.query()]
+        self._inflight.append((done, sources))
+
     def _view(self, name: str) -> torch.Tensor:
         ptr, numel, dtype = C.c_void_p(), C.c_int64(), C.c_int32()
         _lib.check(self._lib.s2r_get_buffer(self._ctx, name.encode(), C.byref(ptr), C.byref(numel), C.byref(dtype)))
@@ -290,11 +305,10 @@ class BatchDecoder:
         toks = (C.c_int64 * len(prefix))(*[int(t) for t in prefix])
         stop = float("inf") if stop_seconds is None else float(stop_seconds)
         tgt = _lib.S2R_NO_TARGET if target is None else int(target)
-        if self.rescore:
-            self._load_frame_tables(slot, frame_logp)
+        tables = self._load_frame_tables(slot, frame_logp) if self.rescore else None
         _lib.check(self._lib.s2r_load_slot(self._ctx, slot, C.c_void_p(mem.data_ptr()), dtype, mem.shape[0], frames,
                                            toks, len(prefix), stop, tgt, self._stream()))
-        self._keep_memory = mem  # the copy into the engine is ordered on the stream; keep the source alive
+        self._retain((mem, tables))
         self.bound[slot], self.loaded[slot] = len(prefix) - 1, True
 
     def run(self, steps: int) -> None:
