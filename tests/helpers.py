@@ -8,7 +8,7 @@ import scenarios as sc
 from oracle.engine import OracleEngine
 from sheetsage2_refined_b200.weights import DecoderWeights, memory_array, synthetic_state_dict
 
-# teacher-forced logits within 2e-2 (bf16), greedy tokens
+# Parity tolerances against the reference decoder: teacher-forced logits within 2e-2 (bf16), greedy tokens
 # equal on at least 99.5% of steps, every divergence an argmax near-tie.
 LOGIT_TOL = 2e-2
 LOGIT_MAX = 3e-2  # bound on every logit (see logit_error)

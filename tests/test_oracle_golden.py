@@ -5,7 +5,7 @@ the reference ``BatchDecoder`` / ``TokenDecoder`` / ``TokenGrammar`` on CPU
 (float32).  The oracle's ``fp32`` mode must reproduce them: greedy tokens and
 grammar states bit-exactly, logits within 1e-4 (float32 summation order).
 The ``bf16`` mode (the reference's CUDA numerics) must stay within the
-north-star logit tolerance of 2e-2 of the float32 logits.
+parity tolerance of 2e-2 of the float32 logits.
 """
 
 from pathlib import Path
@@ -22,7 +22,7 @@ from sheetsage2_refined_b200.weights import memory_array, synthetic_state_dict
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 LOGIT_TOL_FP32 = 1e-4
-LOGIT_TOL_BF16 = 2e-2  # north-star tolerance for teacher-forced bf16 logits
+LOGIT_TOL_BF16 = 2e-2  # parity tolerance for teacher-forced bf16 logits
 
 
 def oracle_loader(engine, width, frames_engine):
