@@ -104,8 +104,13 @@ class OracleEngine:
     def _attend(self, q: np.ndarray, k: np.ndarray, v: np.ndarray) -> np.ndarray:
         """engine.py:286-292 for one row: q ``[H, hd]``, k/v ``[H, n, hd]`` (only the visible keys)."""
 
+        scale = np.float32(self.head_dim ** -0.5)
+        if self.mode == "fp32":
+            # the reference CPU path's batched matmuls (bmm), here BLAS per head
+            scores = np.matmul(k, q[:, :, None])[..., 0] * scale
+            return np.matmul(softmax(scores)[:, None, :], v)[:, 0, :].reshape(-1)
         rnd = self._round
-        scores = rnd(np.einsum("hd,hnd->hn", q, k)) * np.float32(self.head_dim ** -0.5)
+        scores = rnd(np.einsum("hd,hnd->hn", q, k)) * scale
         p = rnd(softmax(scores))
         return rnd(np.einsum("hn,hnd->hd", p, v)).reshape(-1)
 
