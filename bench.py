@@ -176,15 +176,23 @@ class CpuDecoder:
 
         from threadpoolctl import threadpool_limits
 
+        import torch
+
         cores = threads or os.cpu_count() or 1
-        # every host core by default, also under torchrun (which sets OMP_NUM_THREADS=1 per rank)
-        with threadpool_limits(limits=cores):
-            n, t0 = 0, time.perf_counter()
-            while n < min_tokens or time.perf_counter() - t0 < seconds:
-                self.eng.step()
-                n += 1
-            dt = time.perf_counter() - t0
-            return n / dt, n, cores, dt
+        # every host core by default, also under torchrun (which sets OMP_NUM_THREADS=1 per rank);
+        # the float32 port's matrix products run on torch's CPU thread pool
+        before = torch.get_num_threads()
+        torch.set_num_threads(cores)
+        try:
+            with threadpool_limits(limits=cores):
+                n, t0 = 0, time.perf_counter()
+                while n < min_tokens or time.perf_counter() - t0 < seconds:
+                    self.eng.step()
+                    n += 1
+                dt = time.perf_counter() - t0
+                return n / dt, n, cores, dt
+        finally:
+            torch.set_num_threads(before)
 
 
 def run_reference(args, world, rank):
@@ -203,7 +211,7 @@ def run_reference(args, world, rank):
     value = statistics.mean(values)
     one, one_n, _, _ = cpu.sample(seconds=max(2.0, args.cpu_seconds / 4), min_tokens=2, threads=1)
     sample = (f"single-song workload: greedy decode from position 1, {tokens} tokens over {args.steps} steps, "
-              "float32 numpy restatement of the reference CPU path")
+              "float32 restatement of the reference CPU path (numpy, torch CPU matrix products)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(seconds),
@@ -633,7 +641,7 @@ def run_b200(args, world, rank, local):
         one, one_n, _, _ = cpu_dec.sample(seconds=max(2.0, args.cpu_seconds / 4), min_tokens=2, threads=1)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} greedy tokens of the single-song workload from position 1 (load excluded), "
-                         "float32 numpy restatement of the reference CPU path, all host cores",
+                         "float32 restatement of the reference CPU path (numpy, torch CPU matrix products), all host cores",
                "one_thread": {"value": one, "tokens": one_n}}
 
     if rank == 0:

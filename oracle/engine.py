@@ -1,5 +1,9 @@
 """The batched greedy decode engine restated in numpy (test infrastructure).
 
+The ``fp32`` mode (the reference CPU path) runs its matrix products through
+torch's CPU kernels, as that path does; everything else, and the whole
+``bf16`` mode, is numpy.
+
 ``OracleEngine`` mirrors ``sheetsage2_refined/engine.py:52-369``:
 construction (55-149), ``load`` (180-232), ``run`` (234-246), ``finished``
 (248-252), ``take`` (254-262), the step ``_forward`` (294-357) and the
@@ -16,6 +20,7 @@ causal forward up to float32 summation order.
 from __future__ import annotations
 
 import numpy as np
+import torch
 
 from sheetsage2_refined_b200.grammar import ENDED
 from sheetsage2_refined_b200.vocab_table import EOS, NO_CHORD, OUT, meter_tables
@@ -55,6 +60,13 @@ class OracleEngine:
         self.pos_emb = sd["position_embedding.weight"]
         self.emb_norm = (sd["embedding_norm.weight"], sd["embedding_norm.bias"])
         self.out_emb_t = np.ascontiguousarray(rnd(self.tok_emb).T)  # tied logits (engine.py:123,315)
+        # fp32 mode runs its matrix products through torch's CPU kernels, as the
+        # reference CPU path does (one thread pool for every product)
+        self._t = None
+        if mode == "fp32":
+            self._t = {key: (torch.from_numpy(wt), torch.from_numpy(b)) for key, (wt, b) in self.lin.items()
+                       if not key[1].endswith("_norm")}
+            self._t["logits"] = torch.from_numpy(self.out_emb_t)
         self.grammar = make_grammar_oracle(grammar)
         self.logit_bias = None if logit_bias is None else np.asarray(logit_bias, np.float32)
 
@@ -95,6 +107,9 @@ class OracleEngine:
 
     # ------------------------------------------------------------ numerics
     def _linear(self, layer: int, name: str, x: np.ndarray) -> np.ndarray:
+        if self._t is not None:
+            wt, b = self._t[(layer, name)]
+            return (torch.from_numpy(np.ascontiguousarray(x, np.float32)) @ wt + b).numpy()
         wt, b = self.lin[(layer, name)]
         return self._round(self._round(x) @ wt + b)
 
@@ -106,9 +121,11 @@ class OracleEngine:
 
         scale = np.float32(self.head_dim ** -0.5)
         if self.mode == "fp32":
-            # the reference CPU path's batched matmuls (bmm), here BLAS per head
-            scores = np.matmul(k, q[:, :, None])[..., 0] * scale
-            return np.matmul(softmax(scores)[:, None, :], v)[:, 0, :].reshape(-1)
+            # the reference CPU path's batched matmuls (bmm over the heads)
+            q_t = torch.from_numpy(np.ascontiguousarray(q, np.float32))
+            scores = torch.bmm(torch.from_numpy(k), q_t[:, :, None])[..., 0].numpy() * scale
+            p_t = torch.from_numpy(softmax(scores))
+            return torch.bmm(p_t[:, None, :], torch.from_numpy(v))[:, 0, :].numpy().reshape(-1)
         rnd = self._round
         scores = rnd(np.einsum("hd,hnd->hn", q, k)) * scale
         p = rnd(softmax(scores))
@@ -136,6 +153,8 @@ class OracleEngine:
         return x
 
     def _logits(self, x: np.ndarray) -> np.ndarray:
+        if self._t is not None:
+            return (torch.from_numpy(np.ascontiguousarray(x, np.float32)) @ self._t["logits"]).numpy()
         return self._round(self._round(x) @ self.out_emb_t).astype(np.float32)
 
     # --------------------------------------------------------------- slots
