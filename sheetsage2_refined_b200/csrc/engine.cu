@@ -1006,6 +1006,12 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     int rc_ = (x);                 \
     if (rc_ != S2R_OK) return cleanup(rc_); \
   } while (0)
+#define CKC(call)                                                                                    \
+  do {                                                                                               \
+    cudaError_t err_ = (call);                                                                       \
+    if (err_ != cudaSuccess)                                                                         \
+      return cleanup(fail(S2R_ECUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(err_), __FILE__, __LINE__)); \
+  } while (0)
 
   const size_t D = c->D, V = c->V, FFN = c->FFN, T = c->T;
   // weights
@@ -1077,10 +1083,10 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     TRYC(upload_f32(b.ln_cross_b, lw.cross_norm_b, D));
     TRYC(upload_f32(b.ln_final_g, lw.final_norm_w, D));
     TRYC(upload_f32(b.ln_final_b, lw.final_norm_b, D));
-    CK(cudaMemset(b.kpool, 0, pool * sizeof(bf16)));
-    CK(cudaMemset(b.vpool, 0, pool * sizeof(bf16)));
-    CK(cudaMemset(b.ck, 0, cross * sizeof(bf16)));
-    CK(cudaMemset(b.cv, 0, cross * sizeof(bf16)));
+    CKC(cudaMemset(b.kpool, 0, pool * sizeof(bf16)));
+    CKC(cudaMemset(b.vpool, 0, pool * sizeof(bf16)));
+    CKC(cudaMemset(b.ck, 0, cross * sizeof(bf16)));
+    CKC(cudaMemset(b.cv, 0, cross * sizeof(bf16)));
   }
   TRYC(setup_persistent(c));
   if (c->persistent) {
@@ -1099,14 +1105,14 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
       p.kpool = b.kpool; p.vpool = b.vpool; p.ck = b.ck; p.cv = b.cv;
     }
     TRYC(dalloc(c, &c->d_layers, c->L));
-    CK(cudaMemcpy(c->d_layers, pl.data(), c->L * sizeof(PLayer), cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(c->d_layers, pl.data(), c->L * sizeof(PLayer), cudaMemcpyHostToDevice));
     TRYC(dalloc(c, &c->part_o, (size_t)c->H * kPMaxRows * D));
     TRYC(dalloc(c, &c->part_c, (size_t)c->H * kPMaxRows * D));
     TRYC(dalloc(c, &c->bar, 2));
-    CK(cudaMemset(c->bar, 0, 2 * sizeof(unsigned)));
+    CKC(cudaMemset(c->bar, 0, 2 * sizeof(unsigned)));
     if (c->cfg.flags & S2R_FLAG_TRACE) {
       TRYC(dalloc(c, &c->trace, (size_t)kTraceCtas * kTraceSlots));
-      CK(cudaMemset(c->trace, 0, (size_t)kTraceCtas * kTraceSlots * sizeof(long long)));
+      CKC(cudaMemset(c->trace, 0, (size_t)kTraceCtas * kTraceSlots * sizeof(long long)));
     }
   }
   // activations
@@ -1126,8 +1132,8 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     TRYC(dalloc(c, &c->attn_part, (size_t)c->H * c->maxM * D));
     TRYC(dalloc(c, &c->attn_ticket, c->maxM));
     TRYC(dalloc(c, &c->xn, (size_t)c->maxM * D));
-    CK(cudaMemset(c->attn_ticket, 0, c->maxM * sizeof(unsigned)));
-    CK(cudaMemset(c->xn, 0, (size_t)c->maxM * D * sizeof(bf16)));
+    CKC(cudaMemset(c->attn_ticket, 0, c->maxM * sizeof(unsigned)));
+    CKC(cudaMemset(c->xn, 0, (size_t)c->maxM * D * sizeof(bf16)));
   }
   c->attn_splits = attn_splits_for(c, 4);
   c->attn_splits_cross = attn_splits_for(c, 8);
@@ -1135,26 +1141,26 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   if (c->tc) {
     TRYC(dalloc(c, &c->order_self, c->B));
     TRYC(dalloc(c, &c->order_cross, c->B));
-    CK(cudaMallocHost(&c->h_order, 2 * (size_t)c->B * sizeof(int32_t)));
-    CK(cudaEventCreateWithFlags(&c->order_copied, cudaEventDisableTiming));
+    CKC(cudaMallocHost(&c->h_order, 2 * (size_t)c->B * sizeof(int32_t)));
+    CKC(cudaEventCreateWithFlags(&c->order_copied, cudaEventDisableTiming));
     std::vector<int32_t> ident(c->B);
     for (int i = 0; i < c->B; ++i) ident[i] = i;
-    CK(cudaMemcpy(c->order_self, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(c->order_cross, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(c->order_self, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(c->order_cross, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
   }
   TRYC(dalloc(c, &c->keys, c->B));
   TRYC(dalloc(c, &c->counter, 1));
   TRYC(dalloc(c, &c->dev_error, 1));
-  CK(cudaMemset(c->dev_error, 0, sizeof(int)));
+  CKC(cudaMemset(c->dev_error, 0, sizeof(int)));
   TRYC(dalloc(c, &c->bias, V));
   TRYC(dalloc(c, &c->dbg_forced, c->B));
   TRYC(dalloc(c, &c->dbg_logits, (size_t)c->B * V));
   TRYC(dalloc(c, &c->dbg_greedy, c->B));
-  CK(cudaMemset(c->keys, 0, c->B * sizeof(unsigned long long)));
-  CK(cudaMemset(c->counter, 0, sizeof(unsigned int)));
-  CK(cudaMemset(c->bias, 0, V * sizeof(float)));
-  CK(cudaMemset(c->r, 0, M * D * sizeof(float)));
-  CK(cudaMemset(c->x, 0, M * D * sizeof(float)));
+  CKC(cudaMemset(c->keys, 0, c->B * sizeof(unsigned long long)));
+  CKC(cudaMemset(c->counter, 0, sizeof(unsigned int)));
+  CKC(cudaMemset(c->bias, 0, V * sizeof(float)));
+  CKC(cudaMemset(c->r, 0, M * D * sizeof(float)));
+  CKC(cudaMemset(c->x, 0, M * D * sizeof(float)));
   // slot state (engine.py:138-146, grammar.py:99-112): every slot starts finished
   SlotState& st = c->st;
   const size_t B = c->B;
@@ -1179,24 +1185,24 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     std::vector<uint8_t> ones(B, 1);
     std::vector<double> inf(B, INFINITY);
     std::vector<int32_t> frames(B, c->F);
-    CK(cudaMemcpy(st.token, eos.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.position, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.finished, ones.data(), B, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.ended, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.in_shift, ones.data(), B, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.shift_run, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.payload, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.last_field, minus.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.incomplete, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.g, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.count, zeros.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.target, none.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(st.stop, inf.data(), B * 8, cudaMemcpyHostToDevice));
-    CK(cudaMemset(st.out, 0, B * T * 8));
-    CK(cudaMemcpy(st.frames, frames.data(), B * 4, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.token, eos.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.position, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.finished, ones.data(), B, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.ended, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.in_shift, ones.data(), B, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.shift_run, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.payload, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.last_field, minus.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.incomplete, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.g, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.count, zeros.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.target, none.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(st.stop, inf.data(), B * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemset(st.out, 0, B * T * 8));
+    CKC(cudaMemcpy(st.frames, frames.data(), B * 4, cudaMemcpyHostToDevice));
   }
   c->h_page_table.assign(B * c->pps, 0);
-  CK(cudaMemset(st.page_table, 0, B * c->pps * sizeof(int32_t)));
+  CKC(cudaMemset(st.page_table, 0, B * c->pps * sizeof(int32_t)));
   for (int p = c->n_pages - 1; p >= 0; --p) c->free_pages.push_back(p);
   c->slot_pages.assign(B, {});
   c->loaded.assign(B, 0);
@@ -1208,9 +1214,9 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     c->h_token_class.resize(V);
     c->h_field.resize(13);
     c->h_time.resize(V);
-    CK(cudaMemcpy(c->h_token_class.data(), g->token_class, V, cudaMemcpyDefault));
-    CK(cudaMemcpy(c->h_field.data(), g->field_of_class, 13 * 4, cudaMemcpyDefault));
-    CK(cudaMemcpy(c->h_time.data(), g->time_seconds, V * 8, cudaMemcpyDefault));
+    CKC(cudaMemcpy(c->h_token_class.data(), g->token_class, V, cudaMemcpyDefault));
+    CKC(cudaMemcpy(c->h_field.data(), g->field_of_class, 13 * 4, cudaMemcpyDefault));
+    CKC(cudaMemcpy(c->h_time.data(), g->time_seconds, V * 8, cudaMemcpyDefault));
     for (size_t v = 0; v < V; ++v)
       if (c->h_token_class[v] < 0 || c->h_token_class[v] > 12) {
         return cleanup(fail(S2R_EINVAL, "token_class[%zu] = %d is not a class 0..12", v, c->h_token_class[v]));
@@ -1221,25 +1227,26 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     TRYC(dalloc(c, &tc, V));
     TRYC(dalloc(c, &fc, 13));
     TRYC(dalloc(c, &ts, V));
-    CK(cudaMemcpy(tc, c->h_token_class.data(), V, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(fc, c->h_field.data(), 13 * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(ts, c->h_time.data(), V * 8, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(tc, c->h_token_class.data(), V, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(fc, c->h_field.data(), 13 * 4, cudaMemcpyHostToDevice));
+    CKC(cudaMemcpy(ts, c->h_time.data(), V * 8, cudaMemcpyHostToDevice));
     gr.token_class = tc;
     gr.field_of_class = fc;
     gr.time_seconds = ts;
   } else {
     uint8_t* tb = nullptr;
     TRYC(dalloc(c, &tb, (size_t)g->states * V));
-    CK(cudaMemcpy(tb, g->table, (size_t)g->states * V, cudaMemcpyDefault));
+    CKC(cudaMemcpy(tb, g->table, (size_t)g->states * V, cudaMemcpyDefault));
     gr.table = tb;
     gr.states = g->states;
     gr.multiplier = g->multiplier;
   }
-  CK(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
-  CK(cudaDeviceSynchronize());
+  CKC(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
+  CKC(cudaDeviceSynchronize());
   *out = c;
   return S2R_OK;
 #undef TRYC
+#undef CKC
 }
 
 int32_t s2r_destroy(s2r_ctx* c) {
