@@ -134,6 +134,7 @@ struct s2r_ctx {
   Grammar gr{};
   Rescore rs{};  // frame-head rescoring (device tables and state)
   int rs_time_hz = 100;
+  int rs_meters = 0;  // entries of the device meter tables (sized by the first s2r_set_rescore)
   // host copies for prefix replay
   std::vector<int8_t> h_token_class;
   std::vector<int32_t> h_field;
@@ -1301,6 +1302,8 @@ int32_t s2r_set_rescore(s2r_ctx* c, const s2r_rescore* in) {
   Rescore& r = c->rs;
   const int no_chord = in->detail_span[1] - in->detail_span[0];
   if (r.frame_now && no_chord != r.d1 - r.d0) return fail(S2R_EINVAL, "rescoring: the detail span width cannot change");
+  if (r.frame_now && n_meters > c->rs_meters)
+    return fail(S2R_EINVAL, "rescoring: the meter span grew from %d to %d tokens", c->rs_meters, n_meters);
   if (!r.frame_now) {  // first call: tables and state
     for (int t = 0; t < FT_COUNT; ++t) {
       float* tab = nullptr;
@@ -1314,6 +1317,7 @@ int32_t s2r_set_rescore(s2r_ctx* c, const s2r_rescore* in) {
     TRY(dalloc(c, &unit, n_meters));
     r.meter_beats = beats;
     r.meter_unit = unit;
+    c->rs_meters = n_meters;
     TRY(dalloc(c, &r.frame_now, c->B));
     TRY(dalloc(c, &r.key_seen, c->B));
     TRY(dalloc(c, &r.active_meter, c->B));
