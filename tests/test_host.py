@@ -32,3 +32,35 @@ def test_batch_decoder_refuses_to_run_without_cuda():
 
     with pytest.raises(RuntimeError, match="no CPU path"):
         BatchDecoder(object(), object(), batch=1, frames=16)
+
+
+def test_load_sources_are_held_until_their_copies_complete(monkeypatch):
+    """``BatchDecoder._retain`` keeps each load's sources until the event recorded after its copies has completed."""
+
+    import types
+
+    from sheetsage2_refined_b200 import BatchDecoder
+
+    class FakeEvent:
+        done = set()
+        count = 0
+
+        def __init__(self):
+            FakeEvent.count += 1
+            self.id = FakeEvent.count
+
+        def record(self, stream):
+            self.stream = stream
+
+        def query(self):
+            return self.id in FakeEvent.done
+
+    monkeypatch.setattr(torch.cuda, "Event", FakeEvent)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda device=None: "stream")
+    eng = types.SimpleNamespace(_inflight=[], device=torch.device("cpu"))
+    for i in range(3):
+        BatchDecoder._retain(eng, (f"memory{i}", None))
+    assert [s[0] for _, s in eng._inflight] == ["memory0", "memory1", "memory2"]
+    FakeEvent.done.update({1, 2})  # the first two loads' copies have run
+    BatchDecoder._retain(eng, ("memory3", None))
+    assert [s[0] for _, s in eng._inflight] == ["memory2", "memory3"]
