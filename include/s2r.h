@@ -70,7 +70,7 @@ typedef struct s2r_config {
 #define S2R_FLAG_NO_GRAPH 2u /* issue steps as plain launches, no CUDA graph */
 #define S2R_FLAG_ONE_KERNEL_STEP 4u /* batch <= 8: run a step as one persistent kernel */
 #define S2R_FLAG_TRACE 8u          /* one-kernel step records globaltimer marks (ns) per phase ("trace" buffer) */
-#define S2R_FLAG_NO_PREFETCH 16u   /* accepted for compatibility; no effect */
+/* 16u: unused (was a no-op switch) */
 #define S2R_FLAG_NO_TENSOR_CORE 32u /* every projection on the CUDA-core kernel (by default the cross K/V
                                        projection at load, and with batch >= 16 the step and prefill
                                        projections, run on tcgen05 tensor cores) */
@@ -251,7 +251,10 @@ int32_t s2r_free_pages(s2r_ctx* ctx);
  * the library; rows > 1024 fail with S2R_EINVAL.  Every call shares that
  * array, so calls that overlap on the GPU race; each call clears it first.
  * The first call on a device looks up the array's address and should come
- * before any stream capture on that device.  Asynchronous on `stream`.
+ * before any stream capture on that device; the address is kept for the
+ * process's life, so the entry point must not be called on a device after a
+ * cudaDeviceReset of it.  A best allowed value of -inf also gives index 0,
+ * and -0.0 ties with +0.0, as in torch.argmax.  Asynchronous on `stream`.
  * No counterpart in the reference (it computes this step with torch ops,
  * engine.py:316-317,349-350, inside its engine). */
 int32_t s2r_masked_argmax_noalloc(const float* logits, const float* bias, const uint8_t* allowed, int32_t rows,

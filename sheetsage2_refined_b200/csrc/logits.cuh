@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "proj.cuh"
+#include "select.cuh"
 
 namespace s2r {
 
@@ -142,12 +143,6 @@ __device__ __forceinline__ void grammar_update(const Grammar& gr, const SlotStat
   }
 }
 
-__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
-}
-
 __host__ __device__ constexpr int frame_term_width(int term, int no_chord) {
   return term == FT_ROOT || term == FT_BASS ? 12
          : term == FT_DETAIL || term == FT_QUALITY ? no_chord
@@ -207,12 +202,6 @@ __device__ __forceinline__ void rescore_commit(const Rescore& r, const Grammar& 
     r.meter_changed[s] = r.active_meter[s] >= 0 && m != r.active_meter[s];
     r.active_meter[s] = m;
   }
-}
-
-// torch.argmax over a row whose best value is -inf (every token masked or
-// pushed to -inf) returns index 0; otherwise the key's token.
-__device__ __forceinline__ int64_t key_token(unsigned long long k) {
-  return (k >> 32) > 0x007fffffull ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
 }
 
 // Commit one step for rows [0, M) once every key is final: the greedy token

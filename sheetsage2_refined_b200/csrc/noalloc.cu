@@ -20,13 +20,19 @@
 // streams, two threads) race on it and must be serialised by the caller.
 // Each call clears the scratch before use.  The first call on a device looks
 // up the array's device address (cudaGetSymbolAddress) and should come
-// before any stream capture on that device.
+// before any stream capture on that device.  That address belongs to the
+// device's primary context and is kept for the life of the process: after a
+// cudaDeviceReset of the device the entry point must not be called again.
+//
+// The selection keys (select.cuh) are the fused logits kernel's own, so both
+// paths pick the same token, -inf and signed-zero cases included.
 #include <cuda_runtime.h>
 
 #include <mutex>
 
 #include "../../include/s2r.h"
 #include "common.cuh"
+#include "select.cuh"
 
 namespace {
 
@@ -39,12 +45,6 @@ static __device__ __align__(256) unsigned long long g_argmax_scratch[kNoAllocMax
 
 std::mutex g_setup_mutex;
 unsigned long long* g_scratch_ptr[kNoAllocMaxDevices] = {};
-
-__device__ __forceinline__ unsigned long long noalloc_key(float v, int idx) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
-}
 
 __global__ void __launch_bounds__(kNoAllocThreads)
     masked_argmax_noalloc_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kNoAllocThreads)
     for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < vocab; v += gridDim.x * blockDim.x) {
       const size_t i = (size_t)r * vocab + v;
       if (allowed[i]) {
-        const unsigned long long k = noalloc_key(logits[i] + (bias ? bias[v] : 0.f), v);
+        const unsigned long long k = s2r::argmax_key(logits[i] + (bias ? bias[v] : 0.f), v);
         best = k > best ? k : best;
       }
     }
@@ -83,8 +83,8 @@ __global__ void __launch_bounds__(kNoAllocThreads)
   if (!is_last) return;
   __threadfence();
   for (int r = threadIdx.x; r < rows; r += blockDim.x) {
-    const unsigned long long k = atomicExch(scratch + r, 0ull);
-    out[r] = k ? (int64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;  // all masked: index 0
+    // nothing allowed, or a best value of -inf: index 0, as torch.argmax
+    out[r] = s2r::key_token(atomicExch(scratch + r, 0ull));
   }
   if (threadIdx.x == 0) *ticket = 0u;
 }

@@ -1,9 +1,13 @@
 """Generate the golden fixtures of this directory by running the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference``::
+Run where the reference package is importable from a checkout or an
+install directory (read only), given as the first argument or as
+``S2R_REFERENCE``::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py /path/to/reference [fixture ...]
+
+With fixture names (``trace c1 batch real c2 rescore real_full``) only those
+files are rewritten.
 
 The reference package is imported from that checkout with a stub for
 ``soundfile`` (only ``transcribe.load_waveform`` uses it).  Its CPU path is
@@ -17,7 +21,7 @@ engine through its grammar duck type (``engine.grammar`` and extra state).
 Files:
 
 * ``c1_table.npz``      — 2L/d256/V512 decoder, one slot, 128 greedy steps.
-* ``c2_head.npz``       — 12L/d1024/V2048 decoder, F=1500, first 24 steps.
+* ``c2_head.npz``       — 12L/d1024/V2048 decoder, F=1500, first 128 steps.
 * ``batch_table.npz``   — three slots with prefill, masking, limit, refill.
 * ``real_grammar.npz``  — real 32,576-token vocabulary and ``TokenGrammar``,
   two prompt sets, stop seconds and a mode bias.
@@ -26,10 +30,17 @@ Files:
 * ``rescore.npz``       — real vocabulary with every frame-head rescoring
   term switched on: seeded per-frame tables, two slots (one with a prefix
   that states a time, a meter and a key), greedy tokens and end reasons.
+* ``real_full.npz``     — the product decoder shape (6L/d512/8 heads/FFN 2048,
+  32,576 tokens, 7,500 frames) with the real grammar, the mode bias or the
+  key terms, and frame-head rescoring: per case and slot the greedy tokens of
+  160 steps, the top 8 (value, token) of the masked logits the reference's
+  argmax saw at every step, and teacher-forced logits of the first 64 steps
+  at 1,024 seeded vocabulary columns.
 """
 
 from __future__ import annotations
 
+import os
 import sys
 import types
 from pathlib import Path
@@ -42,7 +53,11 @@ REPO = HERE.parents[1]
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REPO / "tests"))
 sys.modules.setdefault("soundfile", types.ModuleType("soundfile"))
-sys.path.insert(0, "/root/reference")
+_ARGS = [a for a in sys.argv[1:] if "/" in a or Path(a).is_dir()]
+REFERENCE = _ARGS[0] if _ARGS else os.environ.get("S2R_REFERENCE")
+if not REFERENCE:
+    sys.exit("make_golden.py: give the reference package's directory (argument or S2R_REFERENCE)")
+sys.path.insert(0, REFERENCE)
 
 from sheetsage2_refined.decoder import DecoderConfig as RefConfig  # noqa: E402
 from sheetsage2_refined.decoder import TokenDecoder  # noqa: E402
@@ -238,14 +253,76 @@ def make_trace():
     print("grammar_trace written")
 
 
+class ArgmaxTap(torch.overrides.TorchFunctionMode):
+    """Records the input of every ``[rows, vocab]`` argmax: the reference engine's masked logits
+    (engine.py:350), as its CPU path evaluates them eagerly."""
+
+    def __init__(self, vocab_size):
+        super().__init__()
+        self.vocab_size, self.seen = vocab_size, []
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        if func in (torch.Tensor.argmax, torch.argmax) and args and args[0].dim() == 2 \
+                and args[0].shape[-1] == self.vocab_size:
+            self.seen.append(args[0].detach().clone())
+        return func(*args, **kwargs)
+
+
+@torch.no_grad()
+def make_real_full():
+    vocab = Vocab()
+    decoder = ref_decoder(sc.REAL, sc.REAL_FULL_SEED)
+    cols = sc.real_logit_columns(vocab.size)
+    out = {"columns": cols}
+    for case, spec in sc.REAL_CASES.items():
+        engine = BatchDecoder(decoder, vocab, batch=2, frames=sc.REAL_FULL_FRAMES, prompts=spec["prompts"],
+                              mode_bias=spec["mode_bias"], frame_weight=spec["frame_weight"])
+        windows = sc.real_windows(vocab, case)
+        for slot, (seed, prefix, stop, frames, rows, table_seed) in enumerate(windows):
+            tables = {k: torch.from_numpy(v) for k, v in sc.rescore_tables(rows, table_seed).items()}
+            memory = torch.from_numpy(memory_array(sc.REAL_FULL_FRAMES, sc.REAL.width, seed))
+            engine.load(slot, memory, prefix, stop, frames, frame_logp=tables)
+        tap = ArgmaxTap(vocab.size)
+        steps = 0
+        with tap:
+            for _ in range(sc.REAL_STEPS):
+                engine.run(1)
+                steps += 1
+                if len(engine.finished()) == 2:
+                    break
+        masked = torch.stack(tap.seen)  # [steps, 2, vocab]
+        assert masked.shape[0] == steps, (masked.shape, steps)
+        top = torch.topk(masked, 8, dim=-1)
+        for slot, (seed, prefix, stop, frames, rows, table_seed) in enumerate(windows):
+            length = int(engine.state["position"][slot]) + 1
+            tokens = engine.out[slot, :length].numpy().copy()
+            out[f"{case}_s{slot}_tokens"] = tokens
+            out[f"{case}_s{slot}_ended"] = np.array(int(engine.state["ended"][slot]))
+            out[f"{case}_s{slot}_top_values"] = top.values[:, slot].numpy().astype(np.float32)
+            out[f"{case}_s{slot}_top_tokens"] = top.indices[:, slot].numpy().astype(np.int32)
+            n = len(prefix)
+            forced = min(sc.REAL_LOGIT_STEPS, length - n)
+            logits = teacher_forced(decoder, seed, sc.REAL_FULL_FRAMES, frames, tokens[: n + forced].tolist(), n - 1)
+            out[f"{case}_s{slot}_logits"] = logits[:, cols]
+            print("real_full", case, slot, length, int(engine.state["ended"][slot]), logits.shape)
+    np.savez_compressed(HERE / "real_full.npz", **out)
+
+
+FIXTURES = {
+    "trace": make_trace,
+    "c1": lambda: make_single("c1_table.npz", sc.C1, sc.C1_SEED, sc.c1_grammar(), sc.C1_MEMORY_SEED, sc.C1_FRAMES,
+                              sc.C1_STEPS),
+    "batch": make_batch,
+    "real": make_real,
+    "c2": lambda: make_single("c2_head.npz", sc.C2, sc.C2_SEED, sc.c2_grammar(), sc.C2_MEMORY_SEED, sc.C2_FRAMES, 128),
+    "rescore": make_rescore,
+    "real_full": make_real_full,
+}
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
-    if sys.argv[1:] == ["rescore"]:  # only the rescoring fixture
-        make_rescore()
-        sys.exit(0)
-    make_trace()
-    make_single("c1_table.npz", sc.C1, sc.C1_SEED, sc.c1_grammar(), sc.C1_MEMORY_SEED, sc.C1_FRAMES, sc.C1_STEPS)
-    make_batch()
-    make_real()
-    make_single("c2_head.npz", sc.C2, sc.C2_SEED, sc.c2_grammar(), sc.C2_MEMORY_SEED, sc.C2_FRAMES, 24)
-    make_rescore()
+    chosen = [a for a in sys.argv[1:] if a in FIXTURES] or list(FIXTURES)
+    for name in chosen:
+        FIXTURES[name]()

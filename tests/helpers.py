@@ -96,6 +96,53 @@ def masked(logits: np.ndarray, allowed: np.ndarray, bias=None) -> np.ndarray:
     return np.where(allowed, x, -np.inf)
 
 
+def window_agreement(pairs, tie_at):
+    """Greedy agreement of free-running windows with the reference's tokens.
+
+    ``pairs`` holds ``(got, ref, start)`` per window: both token lists and the
+    index of the first generated token.  Tokens are compared from ``start`` up
+    to the window's first divergence; after it the two histories differ, so
+    later tokens of that window are not compared.  ``tie_at(window, k)``
+    returns the reference-side masked logits (bias and rescoring included) of
+    the step that chose token ``k``, to judge the divergence a near-tie.
+
+    Returns ``(same, compared, divergences)``; every divergence is ``(window,
+    k, engine token, reference token, is_near_tie)``.
+    """
+
+    same = compared = 0
+    divergences = []
+    for w, (got, ref, start) in enumerate(pairs):
+        n = min(len(got), len(ref))
+        k = next((i for i in range(start, n) if got[i] != ref[i]), None)
+        if k is None:
+            assert len(got) == len(ref), (w, len(got), len(ref))
+            same += n - start
+            compared += n - start
+            continue
+        same += k - start
+        compared += k - start + 1
+        divergences.append((w, k, int(got[k]), int(ref[k]), near_tie(tie_at(w, k), int(got[k]), int(ref[k]))))
+    return same, compared, divergences
+
+
+def masked_logits_at(oracle, load_args, ref, k):
+    """The oracle's masked logits for the step that chose ``ref[k]`` in slot 0.
+
+    ``load_args`` = ``(load, memory_seed, prefix, stop, frames, target)``: the
+    window is loaded into slot 0, the reference tokens after its prefix are
+    forced one by one up to position ``k``, and the masked logits of the
+    step predicting ``ref[k]`` are returned.
+    """
+
+    load, seed, prefix, stop, frames, target = load_args
+    load(0, seed, prefix, stop, frames, target)
+    for i in range(len(prefix), k):
+        oracle.step(forced=np.array([ref[i]]))
+    oracle.step(forced=np.array([ref[k]]))
+    return oracle.last_masked[0]
+
+
 def teacher_forced_compare(engine, oracle, tokens, prefix_len, steps, slot=0):
     """Force ``tokens[prefix_len:]`` through both engines (slot ``slot``); compare per step.
 

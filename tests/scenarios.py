@@ -20,6 +20,10 @@ C1 = DecoderConfig(vocab_size=512, width=256, layers=2, heads=4, ffn_width=1024,
 C1_SHORT = DecoderConfig(vocab_size=512, width=256, layers=2, heads=4, ffn_width=1024, max_tokens=256)
 C2 = DecoderConfig(vocab_size=2048, width=1024, layers=12, heads=16, ffn_width=4096, max_tokens=5120)
 REAL_TINY = DecoderConfig(vocab_size=32576, width=128, layers=2, heads=2, ffn_width=256, max_tokens=5120)
+# The product decoder's shape (decoder.py:12-21 with the real vocabulary, model.py:22) and its
+# 300 s window of 7,500 encoder frames (model.py:15, encoder.py:37-39).
+REAL = DecoderConfig(vocab_size=32576, width=512, layers=6, heads=8, ffn_width=2048, max_tokens=5120)
+REAL_FULL_SEED, REAL_FULL_FRAMES, REAL_STEPS, REAL_LOGIT_STEPS = 6, 7500, 160, 64
 
 C1_SEED, C1_MEMORY_SEED, C1_GRAMMAR_SEED, C1_FRAMES, C1_STEPS = 0, 100, 7, 256, 128
 C2_SEED, C2_MEMORY_SEED, C2_GRAMMAR_SEED, C2_FRAMES = 1, 101, 8, 1500
@@ -125,13 +129,15 @@ def rescore_windows(vocab):
     return [(prefix, None, REAL_FRAMES, REAL_FRAMES, 71), (stated, None, 50, 40, 72)]
 
 
-def rescore_forced(engine, vocab, golden: dict, case: str, load) -> list[tuple[int, int, int]]:
+def rescore_forced(engine, vocab, golden: dict, case: str, load, masks: list | None = None) -> list[tuple[int, int, int]]:
     """Force the reference's greedy tokens of a rescoring case through ``engine``.
 
     Loads both windows of the case with their frame tables (``load(slot,
     memory_seed, prefix, stop, frames, frame_logp)``), then at every step
     forces each slot's next reference token and records ``(slot, engine's
-    greedy choice, reference's choice)`` while the slot is running.
+    greedy choice, reference's choice)`` while the slot is running.  With
+    ``masks`` (an oracle engine only) the masked logits of every recorded
+    choice are appended to it as well.
     """
 
     import numpy as np
@@ -154,4 +160,87 @@ def rescore_forced(engine, vocab, golden: dict, case: str, load) -> list[tuple[i
             engine.step(forced=forced)
         for slot in live:
             record.append((slot, int(greedy[slot]), int(forced[slot])))
+            if masks is not None:
+                masks.append(engine.last_masked[slot].copy())
+    return record
+
+
+# Product-shape cases: the real vocabulary and TokenGrammar, mode bias or the key terms, and the
+# frame-head rescoring terms each prompt set can use (engine.py:29-38: key and key_mode share a
+# prompt group, so the key terms and the mode bias never meet).
+REAL_CASES = {
+    "mode": {"prompts": ("timestamp", "downbeat_meter", "chord_detail", "key_mode", "melody_full"),
+             "mode_bias": [0.0, 1.5, -0.5, 2.0, 0.25, -1.0, 3.0, 0.5, -2.0],
+             "frame_weight": {"root": 0.5, "bass": 0.4, "detail": 0.3, "quality": 0.3, "downbeat": 2.0,
+                              "meter": 2.0}},
+    "key": {"prompts": ("timestamp", "downbeat_meter", "key", "chord_detail", "melody_full"),
+            "mode_bias": None,
+            "frame_weight": {"root": 0.5, "bass": 0.4, "detail": 0.3, "quality": 0.3, "key": 0.5,
+                             "key_boundary": 0.6, "downbeat": 2.0, "meter": 2.0}},
+}
+
+# Columns of the teacher-forced logits kept in the product-shape fixture (the full rows would be
+# 130 KB each): a seeded sample of the vocabulary.
+REAL_LOGIT_COLUMNS = 1024
+
+
+def real_logit_columns(vocab_size: int):
+    import numpy as np
+
+    return np.sort(np.random.default_rng(77).choice(vocab_size, REAL_LOGIT_COLUMNS, replace=False))
+
+
+def real_windows(vocab, case: str):
+    """(memory seed, prefix, stop seconds, real frames, table rows, table seed) of the case's two slots.
+
+    Slot 0 starts from the prompt prefix and sees every frame; slot 1's prefix
+    states a time, a meter, bar position 0 and a key (or key-and-mode) token,
+    and it sees 6,000 of the 7,500 frames.
+    """
+
+    prompts = REAL_CASES[case]["prompts"]
+    prefix = vocab.prompt_prefix(prompts)
+    key = vocab.start["key"] + 5 if "key" in prompts else vocab.start["key_mode"] + 17
+    stated = prefix + [vocab.start["time"] + 150, vocab.start["meter"] + 3 * 6 + 2, vocab.start["eighth_position"], key]
+    return [(201, prefix, None, REAL_FULL_FRAMES, REAL_FULL_FRAMES, 81),
+            (202, stated, None, 6000, 5000, 82)]
+
+
+def real_forced(engine, vocab, golden: dict, case: str, load, masks: list | None = None,
+                logits: list | None = None) -> list[tuple[int, int, int, int]]:
+    """Force the reference's greedy tokens of a product-shape case through ``engine``.
+
+    Loads both windows of the case with their frame tables (``load(slot,
+    memory_seed, prefix, stop, frames, frame_logp)``), then at every step
+    forces each slot's next reference token and records ``(slot, step,
+    engine's greedy choice, reference's choice)`` while the slot has
+    reference tokens left.  ``masks`` (an oracle engine only) receives the
+    masked logits of every record; ``logits`` receives ``(slot, step, raw
+    logits row)`` of every record.
+    """
+
+    import numpy as np
+
+    windows = real_windows(vocab, case)
+    seqs = [golden[f"{case}_s{slot}_tokens"].tolist() for slot in (0, 1)]
+    for slot, (seed, prefix, stop, frames, rows, table_seed) in enumerate(windows):
+        load(slot, seed, prefix, stop, frames, rescore_tables(rows, table_seed))
+    starts = [len(w[1]) for w in windows]
+    steps = max(len(s) - p for s, p in zip(seqs, starts))
+    record = []
+    for k in range(steps):
+        forced = np.full(getattr(engine, "batch", 2), -1, np.int64)
+        live = [slot for slot in (0, 1) if starts[slot] + k < len(seqs[slot])]
+        for slot in live:
+            forced[slot] = seqs[slot][starts[slot] + k]
+        if hasattr(engine, "step_debug"):
+            raw, greedy = engine.step_debug(forced, want_logits=logits is not None)
+        else:
+            raw, greedy = engine.step(forced=forced)
+        for slot in live:
+            record.append((slot, k, int(greedy[slot]), int(forced[slot])))
+            if masks is not None:
+                masks.append(engine.last_masked[slot].copy())
+            if logits is not None:
+                logits.append((slot, k, raw[slot].copy()))
     return record

@@ -17,7 +17,7 @@ import torch
 
 import scenarios as sc
 from helpers import (LOGIT_WITHIN_FRACTION, TOKEN_AGREEMENT, cuda_engine, logit_error, logit_within, loader,
-                     masked, near_tie, oracle_engine, teacher_forced_compare)
+                     masked, masked_logits_at, near_tie, oracle_engine, teacher_forced_compare, window_agreement)
 from oracle.grammar import TableGrammarOracle
 from sheetsage2_refined_b200.grammar import ClassGrammar
 from sheetsage2_refined_b200.vocab_table import NO_KEY, OUT, SOS, VocabTable
@@ -95,21 +95,40 @@ def test_c1_vs_oracle_bf16(flags):
 
 
 def test_c2_head_vs_reference_golden():
+    """12-layer headline decoder, teacher-forced along the reference's own greedy tokens.
+
+    Logits within 2e-2 of the reference's float32 logits; every step where the
+    engine's greedy choice differs from the reference's is a near-tie of the
+    reference's masked logits (random-init weights put ~8% of steps within one
+    bf16 ulp between the two best tokens).
+    """
+
     g = np.load(GOLDEN / "c2_head.npz")
     tokens = g["tokens"].tolist()
+    steps = len(g["logits"])
     eng = cuda_engine(sc.C2, sc.C2_SEED, sc.c2_grammar(), 1, sc.C2_FRAMES)
-    loader(eng, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, 24)
-    worst, err, same, within, count = 0.0, 0.0, 0, 0, 0
-    for k in range(24):
+    loader(eng, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, steps)
+    grammar = TableGrammarOracle(sc.c2_grammar())
+    state = grammar.new_state(1)
+    worst, err, same, ties, within, count = 0.0, 0.0, 0, 0, 0, 0
+    for k in range(steps):
         lg, greedy = eng.step_debug(np.array([tokens[2 + k]]))
         worst = max(worst, float(np.abs(lg[0] - g["logits"][k]).max()))
         err = max(err, logit_error(lg[0], g["logits"][k]))
         w, n = logit_within(lg[0], g["logits"][k])
         within, count = within + w, count + n
-        same += int(greedy[0] == tokens[2 + k])
+        if greedy[0] == tokens[2 + k]:
+            same += 1
+        else:
+            ml = masked(g["logits"][k], grammar.allowed(state)[0])
+            assert near_tie(ml, int(greedy[0]), tokens[2 + k]), (k, greedy[0], tokens[2 + k])
+            ties += 1
+        grammar.update(state, np.array([tokens[2 + k]]), np.array([True]), np.array([np.inf]), np.array([False]))
+    print(f"c2 vs reference fp32 ({steps} steps): max |dlogit| {worst:.2e}, within 2e-2 {within}/{count}, "
+          f"agreement {same}/{steps}, near-ties {ties}")
+    assert steps >= 128
     assert err <= 1.0 and within / count >= LOGIT_WITHIN_FRACTION, (worst, err, within / count)
-    assert same >= 23, same
-    print(f"c2 vs reference fp32: max |dlogit| {worst:.2e}, within 2e-2 {within}/{count}, agreement {same}/24")
+    assert same / steps >= TOKEN_AGREEMENT or ties == steps - same
 
 
 def test_one_kernel_and_multi_kernel_steps_agree():
@@ -207,15 +226,32 @@ def test_c2_long_context_vs_oracle():
 def test_continuous_batch_vs_reference_golden():
     g = np.load(GOLDEN / "batch_table.npz")
     eng = cuda_engine(sc.C1_SHORT, sc.BATCH_SEED, sc.batch_grammar(), 3, sc.BATCH_FRAMES)
-    taken = sc.continuous_batch(eng, loader(eng, sc.C1_SHORT.width, sc.BATCH_FRAMES))
+    base = loader(eng, sc.C1_SHORT.width, sc.BATCH_FRAMES)
+    loads: dict = {}
+
+    def load(slot, *args):  # remember each slot's windows, in order
+        loads.setdefault(slot, []).append(args)
+        base(slot, *args)
+
+    taken = sc.continuous_batch(eng, load)
     assert [s for s, _, _ in taken] == g["slots"].tolist()
     assert [e for _, _, e in taken] == g["ended"].tolist()
     assert [len(t) for _, t, _ in taken] == g["lengths"].tolist()
-    ref = np.split(g["tokens"], np.cumsum(g["lengths"])[:-1])
-    total = sum(len(t) for _, t, _ in taken)
-    same = sum(int(a == b) for (_, t, _), r in zip(taken, ref) for a, b in zip(t, r.tolist()))
-    print(f"continuous batch vs reference fp32: {same}/{total} tokens equal")
-    assert same / total >= 0.9
+    ref = [r.tolist() for r in np.split(g["tokens"], np.cumsum(g["lengths"])[:-1])]
+    windows, seen = [], {}
+    for slot, _, _ in taken:
+        windows.append(loads[slot][seen.get(slot, 0)])
+        seen[slot] = seen.get(slot, 0) + 1
+
+    def tie_at(w, k):
+        ora = oracle_engine(sc.C1_SHORT, sc.BATCH_SEED, sc.batch_grammar(), 1, sc.BATCH_FRAMES, mode="fp32")
+        return masked_logits_at(ora, (loader(ora, sc.C1_SHORT.width, sc.BATCH_FRAMES), *windows[w]), ref[w], k)
+
+    pairs = [(t, r, len(windows[w][1])) for w, ((_, t, _), r) in enumerate(zip(taken, ref))]
+    same, compared, div = window_agreement(pairs, tie_at)
+    print(f"continuous batch vs reference fp32: {same}/{compared} generated tokens equal, divergences {div}")
+    assert all(t for *_, t in div), div
+    assert same / compared >= TOKEN_AGREEMENT
 
 
 @STEP_PATHS
@@ -297,14 +333,15 @@ def test_real_grammar_vs_reference_golden():
     from helpers import weights
 
     dec = DecoderWeights(sc.REAL_TINY, weights(sc.REAL_TINY, sc.REAL_SEED))
-    total = same = 0
+    pairs, windows = [], []
     for i, prompts in enumerate(sc.REAL_PROMPT_SETS):
         bias = [0.0, 1.5, -0.5, 2.0, 0.25, -1.0, 3.0, 0.5, -2.0] if "key_mode" in prompts else None
         eng = BatchDecoder(dec, vocab, batch=2, frames=sc.REAL_FRAMES, prompts=prompts, mode_bias=bias)
         prefix = vocab.prompt_prefix(prompts)
         load = loader(eng, sc.REAL_TINY.width, sc.REAL_FRAMES)
-        load(0, 31 + i, prefix, 2.5, sc.REAL_FRAMES, None)
-        load(1, 41 + i, prefix + [vocab.start["shift"] + 3], None, 50, None)
+        plan = [(31 + i, prefix, 2.5, sc.REAL_FRAMES, None), (41 + i, prefix + [vocab.start["shift"] + 3], None, 50, None)]
+        for slot, args in enumerate(plan):
+            load(slot, *args)
         for _ in range(40):
             eng.run(5)
             if len(eng.finished()) == 2:
@@ -313,13 +350,21 @@ def test_real_grammar_vs_reference_golden():
             ref = g[f"p{i}_s{slot}_tokens"].tolist()
             length = int(eng.state["position"][slot]) + 1
             got = eng.out[slot, :length].tolist()
-            n = min(len(got), len(ref))
-            total += len(ref)
-            same += sum(int(a == b) for a, b in zip(got[:n], ref[:n]))
+            pairs.append((got, ref, len(plan[slot][1])))
+            windows.append((prompts, getattr(eng, "_bias", None) if bias else None, plan[slot]))
             if got == ref:
                 assert int(eng.state["ended"][slot]) == int(g[f"p{i}_s{slot}_ended"])
-    print(f"real grammar vs reference fp32: {same}/{total} tokens equal")
-    assert same / total >= 0.9
+
+    def tie_at(w, k):
+        prompts, bias, args = windows[w]
+        ora = oracle_engine(sc.REAL_TINY, sc.REAL_SEED, ClassGrammar(vocab, prompts), 1, sc.REAL_FRAMES, mode="fp32",
+                            logit_bias=bias)
+        return masked_logits_at(ora, (loader(ora, sc.REAL_TINY.width, sc.REAL_FRAMES), *args), pairs[w][1], k)
+
+    same, compared, div = window_agreement(pairs, tie_at)
+    print(f"real grammar vs reference fp32: {same}/{compared} generated tokens equal, divergences {div}")
+    assert all(t for *_, t in div), div
+    assert same / compared >= TOKEN_AGREEMENT
 
 
 def test_real_grammar_states_follow_forced_trace():

@@ -144,10 +144,11 @@ def test_c2_head_fp32():
     sd = synthetic_state_dict(sc.C2, sc.C2_SEED)
     engine = OracleEngine(sc.C2, sd, sc.c2_grammar(), batch=1, frames=sc.C2_FRAMES, mode="fp32")
     tokens = g["tokens"].tolist()
-    oracle_loader(engine, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, 24)
-    logits, greedy = teacher_forced_run(engine, tokens, 2, 24)
+    steps = len(g["logits"])
+    oracle_loader(engine, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, steps)
+    logits, greedy = teacher_forced_run(engine, tokens, 2, steps)
     assert np.abs(logits - g["logits"]).max() <= LOGIT_TOL_FP32
-    assert greedy.tolist() == tokens[2:26]
+    assert greedy.tolist() == tokens[2:2 + steps]
 
 
 @pytest.mark.parametrize("case", list(sc.RESCORE_CASES))
@@ -171,3 +172,59 @@ def test_rescore_oracle_vs_reference(case):
     same = sum(int(a == b) for _, a, b in record)
     print(f"rescoring ({case}) oracle fp32 vs reference: {same}/{len(record)}")
     assert same == len(record)
+
+
+@pytest.mark.parametrize("case", list(sc.REAL_CASES))
+def test_real_full_oracle_vs_reference(case):
+    """Product decoder shape: the oracle (fp32) picks the reference's greedy token at every forced
+    step, its masked maximum equals the one the reference's argmax saw, and its teacher-forced
+    logits match the reference's at the fixture's columns."""
+
+    from oracle.engine import FRAME_TERM_NAMES
+    from sheetsage2_refined_b200.engine import frame_terms
+
+    g = np.load(GOLDEN / "real_full.npz")
+    vocab = VocabTable()
+    spec = sc.REAL_CASES[case]
+    bias = None
+    if spec["mode_bias"] is not None:
+        bias = np.zeros(vocab.size, np.float32)
+        bias[vocab.start["key_mode"]: vocab.start["key_mode"] + 108] = np.repeat(np.float32(spec["mode_bias"]), 12)
+    eng = OracleEngine(sc.REAL, synthetic_state_dict(sc.REAL, sc.REAL_FULL_SEED), ClassGrammar(vocab, spec["prompts"]),
+                       batch=2, frames=sc.REAL_FULL_FRAMES, mode="fp32", logit_bias=bias,
+                       frame_weight=frame_terms(spec["frame_weight"], spec["prompts"]), vocab=vocab)
+    assert len(FRAME_TERM_NAMES) == 8
+
+    def load(slot, memory_seed, prefix, stop, frames, tables):
+        eng.load(slot, memory_array(sc.REAL_FULL_FRAMES, sc.REAL.width, memory_seed), prefix, stop, frames,
+                 frame_logp=tables)
+
+    masks, logits = [], []
+    record = sc.real_forced(eng, vocab, g, case, load, masks, logits)
+    cols = g["columns"]
+    for (slot, k, greedy, ref), m in zip(record, masks):
+        assert greedy == ref, (slot, k, greedy, ref)
+        assert abs(float(m[ref]) - float(g[f"{case}_s{slot}_top_values"][k, 0])) <= LOGIT_TOL_FP32, (slot, k)
+    worst = 0.0
+    for slot, k, row in logits:
+        if k < sc.REAL_LOGIT_STEPS:
+            worst = max(worst, float(np.abs(row[cols] - g[f"{case}_s{slot}_logits"][k]).max()))
+    print(f"real_full {case}: {len(record)} forced steps, greedy equal; max |dlogit| {worst:.2e}")
+    assert worst <= LOGIT_TOL_FP32
+
+
+def test_bf16_rounding_matches_the_bit_rule():
+    """The oracle's bfloat16 rounding (torch's conversion) equals round-to-nearest-even on the bits,
+    ties, subnormals, infinities and NaN included."""
+
+    from oracle.numerics import bf16, bf16_rule
+
+    rng = np.random.default_rng(0)
+    bits = rng.integers(0, 2 ** 32, 1 << 20, dtype=np.uint64).astype(np.uint32)
+    ties = (rng.integers(0, 2 ** 16, 4096, dtype=np.uint64).astype(np.uint32) << 16) | np.uint32(0x8000)
+    x = np.concatenate([bits, ties]).view(np.float32)
+    x = np.concatenate([x, np.float32([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-40, 3.4e38])])
+    a, b = bf16(x), bf16_rule(x)
+    nan = np.isnan(x)
+    assert np.array_equal(np.isnan(a), nan) and np.array_equal(np.isnan(b), nan)
+    assert np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
