@@ -57,64 +57,27 @@ _ARGS = [a for a in sys.argv[1:] if "/" in a or Path(a).is_dir()]
 REFERENCE = _ARGS[0] if _ARGS else os.environ.get("S2R_REFERENCE")
 if not REFERENCE:
     sys.exit("make_golden.py: give the reference package's directory (argument or S2R_REFERENCE)")
-sys.path.insert(0, REFERENCE)
-
-from sheetsage2_refined.decoder import DecoderConfig as RefConfig  # noqa: E402
-from sheetsage2_refined.decoder import TokenDecoder  # noqa: E402
-from sheetsage2_refined.engine import BatchDecoder  # noqa: E402
-from sheetsage2_refined.grammar import TokenGrammar  # noqa: E402
-from sheetsage2_refined.vocab import Vocab  # noqa: E402
 
 import scenarios as sc  # noqa: E402
-from sheetsage2_refined_b200.weights import memory_array, synthetic_state_dict  # noqa: E402
+from reference_path import load_reference  # noqa: E402
+from reference_path import ref_decoder as _ref_decoder  # noqa: E402
+from reference_path import table_engine as _table_engine  # noqa: E402
+from sheetsage2_refined_b200.weights import memory_array  # noqa: E402
 
-
-class TorchTableGrammar:
-    """The table grammar in the reference engine's grammar duck type (engine.py:74,211,349,355)."""
-
-    def __init__(self, desc):
-        self.table = torch.tensor(desc.table)
-        self.states, self.multiplier = desc.states, desc.multiplier
-        self.time_seconds = torch.tensor(desc.time_seconds)
-        self.prompts = desc.prompts
-
-    def allowed(self, state):
-        return self.table[state["g"]]
-
-    def update(self, state, tokens, active, stop, at_limit):
-        g = (self.multiplier * state["g"] + tokens) % self.states
-        count = state["count"] + 1
-        done = count >= state["target"]
-        ended = torch.where(done, 1, torch.where(at_limit, 3, 0))
-        finished = done | at_limit
-        state["g"].copy_(torch.where(active, g, state["g"]))
-        state["count"].copy_(torch.where(active, count, state["count"]))
-        state["ended"].copy_(torch.where(active & finished, ended, state["ended"]))
-        state["finished"].copy_(state["finished"] | (active & finished))
-
-    def prefix_state(self, tokens, out_index, device):
-        g = 0
-        for token in tokens[out_index + 1 :]:
-            g = (self.multiplier * g + token) % self.states
-        z = lambda v: torch.tensor([v], dtype=torch.long)  # noqa: E731
-        return {"g": z(g), "count": z(0), "finished": torch.tensor([False]), "ended": z(0)}
+REF = load_reference(REFERENCE)
+if REF is None:
+    sys.exit(f"make_golden.py: no sheetsage2_refined package under {REFERENCE}")
+BatchDecoder = REF.engine.BatchDecoder
+TokenGrammar = REF.grammar.TokenGrammar
+Vocab = REF.vocab.Vocab
 
 
 def ref_decoder(config, seed):
-    decoder = TokenDecoder(RefConfig(vocab_size=config.vocab_size, width=config.width, layers=config.layers,
-                                     heads=config.heads, ffn_width=config.ffn_width, max_tokens=config.max_tokens))
-    state = {k: torch.from_numpy(v) for k, v in synthetic_state_dict(config, seed).items()}
-    decoder.load_state_dict(state, strict=True)
-    return decoder.eval()
+    return _ref_decoder(REF, config, seed)
 
 
 def table_engine(decoder, desc, batch, frames):
-    engine = BatchDecoder(decoder, Vocab(), batch=batch, frames=frames)
-    engine.grammar = TorchTableGrammar(desc)
-    engine.state["g"] = torch.zeros(batch, dtype=torch.long)
-    engine.state["count"] = torch.zeros(batch, dtype=torch.long)
-    engine.state["target"] = torch.full((batch,), np.iinfo(np.int64).max, dtype=torch.long)
-    return engine
+    return _table_engine(REF, decoder, desc, batch, frames)
 
 
 def ref_loader(engine, width, frames_engine):

@@ -102,3 +102,85 @@ def test_bench_takes_the_slowest_rank_and_all_tokens_over_gloo():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert slowest == 101.0 and tokens == 2048.0 * 3
+
+
+class FakeEngine:
+    """The BatchDecoder surface decode_songs drives, without a GPU: a slot loaded with target n
+    finishes after n steps with tokens prefix + [song marker] * n."""
+
+    def __init__(self, batch):
+        self.batch = batch
+        self.loaded = [None] * batch  # (prefix, target, steps done)
+
+    def free_slots(self):
+        return [s for s in range(self.batch) if self.loaded[s] is None]
+
+    def load(self, slot, memory, prefix, stop, frames=None, target=None):
+        assert self.loaded[slot] is None
+        self.loaded[slot] = [list(prefix), int(target), 0, int(memory)]
+
+    def run(self, steps):
+        for entry in self.loaded:
+            if entry is not None:
+                entry[2] = min(entry[1], entry[2] + steps)
+
+    def finished(self):
+        return [s for s, e in enumerate(self.loaded) if e is not None and e[2] >= e[1]]
+
+    def take(self, slot):
+        prefix, target, _, marker = self.loaded[slot]
+        self.loaded[slot] = None
+        return prefix + [marker] * target + [2], "eos"
+
+
+def test_decode_songs_refills_every_slot_and_decodes_each_song_once():
+    from sheetsage2_refined_b200.shard import DecodeStats, Song, decode_songs
+
+    import numpy as np
+
+    rng = np.random.default_rng(5)
+    targets = rng.integers(10, 200, 37).tolist()
+    songs = {i: Song(memory=1000 + i, prefix=[1, 3], target=t) for i, t in enumerate(targets)}
+    stats = DecodeStats()
+    out = decode_songs(FakeEngine(8), songs, poll_every=16, stats=stats)
+    assert sorted(out) == list(range(37)) and stats.loads == 37
+    for i, (tokens, ended) in out.items():
+        assert tokens == [1, 3] + [1000 + i] * targets[i] + [2] and ended == "eos"
+    assert 0.0 < stats.occupancy(8) <= 1.0 and stats.tail_seconds() >= 0.0
+
+
+def _box_rank(rank, world, port, targets, queue):
+    import torch.distributed as dist
+
+    from sheetsage2_refined_b200.shard import Song, decode_box
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        songs = [Song(memory=1000 + i, prefix=[1, 3], target=t) for i, t in enumerate(targets)]
+        merged = decode_box(FakeEngine(4), songs, targets, poll_every=8)
+        if rank == 0:
+            queue.put(merged)
+        else:
+            assert merged is None
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_box_job_over_gloo():
+    """The box job: each rank decodes its LPT share with refill; rank 0 gets every song once."""
+
+    targets = [70, 400, 51, 250, 120, 333, 90, 17, 260, 44, 180]
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_box_rank, args=(r, 2, port, targets, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    merged = queue.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert sorted(merged) == list(range(len(targets)))
+    for i, (tokens, ended) in merged.items():
+        assert tokens == [1, 3] + [1000 + i] * targets[i] + [2]
