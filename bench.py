@@ -450,12 +450,15 @@ class Batched:
     def _positions(self):
         return self.eng.state["position"].cpu().tolist()
 
+    def _done(self):
+        return self.eng.finished()
+
     def _step(self, pinned):
         tokens = 0
         for _ in range(self.POLLS):
             self.eng.run(self.POLL)
             self.launches += self.eng.step_launches * self.POLL
-            done = self.eng.finished()
+            done = self._done()
             if done:
                 pos = self._positions()
                 for slot in done:
@@ -727,7 +730,13 @@ class RealSong:
 
 
 class RealBatched(Batched):
-    """Product shape, 64 slots with refill: 7,500-frame windows, one bench step = 32 decode steps."""
+    """Product shape, 64 slots with refill: 7,500-frame windows, one bench step = 32 decode steps.
+
+    Random-init weights rarely end a window by themselves, so each window gets
+    a length drawn from U[512, 4096] tokens (the batched workload's targets):
+    once a slot has generated that many tokens it is taken and refilled like
+    a finished one.
+    """
 
     name = "real_b64"
     POLLS = 1
@@ -741,20 +750,27 @@ class RealBatched(Batched):
         self.pool, self.pool_pinned = random_pool(torch, device, REAL_FRAMES, REAL.width, MEMORY_SEED + rank)
         self.tables = [real_tables(torch, device, REAL_FRAMES, 93 + i) for i in range(2)]
         self.tables_pinned = [{k: v.cpu().pin_memory() for k, v in t.items()} for t in self.tables]
+        self.ends = [0] * BATCH
         self._init_slots()
 
     def config(self, world):
         return real_config(world, BATCH, "64 slots with refill, real frames U[3000, 7500]")
 
     def _window(self):
-        return int(self.rng.integers(3000, REAL_FRAMES + 1)), None
+        return int(self.rng.integers(3000, REAL_FRAMES + 1)), int(self.rng.integers(512, 4097))
 
     def _load(self, slot, frames, target, mem):
         tables = (self.tables_pinned if mem.device.type == "cpu" else self.tables)[self.k % 2]
         self.eng.load(slot, mem, self.prefix, None, frames, tables)
         if mem.device.type == "cpu":
             self.h2d_total += sum(t.numel() * 4 for t in tables.values())
+        self.ends[slot] = len(self.prefix) - 1 + target
         return self.prefix
+
+    def _done(self):
+        done = set(self.eng.finished())
+        pos = self._positions()
+        return sorted(done | {s for s in range(BATCH) if self.eng.loaded[s] and pos[s] >= self.ends[s]})
 
 
 def profile(eng):
@@ -894,8 +910,10 @@ def reference_gpu(torch, device, seconds: float = 20.0):
         torch.cuda.synchronize(device)
         return start.elapsed_time(end), n
 
+    # the decoder's parameters are ordinary tensors (the engine reads their version counters, engine.py:151-153);
+    # the decode itself runs under inference mode, as transcribe_many runs it (transcribe.py:225)
+    decoder = ref_decoder(ref, CONFIG, WEIGHT_SEED, device)
     with torch.inference_mode():
-        decoder = ref_decoder(ref, CONFIG, WEIGHT_SEED, device)
         eng = table_engine(ref, decoder, c2_grammar(), 1, SINGLE_FRAMES)
         mem = torch.from_numpy(memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED)).to(device)
 

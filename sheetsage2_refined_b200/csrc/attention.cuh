@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "mbarrier.cuh"
+#include "proj.cuh"
 
 namespace s2r {
 
@@ -47,30 +48,34 @@ struct AttnArgs {
   int splits;     // CTAs per (row, head): the cluster size the launch must have
   int* err;       // device error word: set (and the work skipped) on a broken invariant
   const int32_t* order;  // [M] row of each grid z index (longest first), or null: identity
-  // kFuseOut: the out-projection, residual and LayerNorm that follow the attention
+  // kAccOut (engines below 16 slots): the out-projection that follows the attention
+  // (engine.py:292,312): every CTA adds its share of the head's contribution,
+  // sum_d Wo[n][64h + d] o_h[d], to acc_out[m][n] as a fixed-point sum (acc_add);
+  // the next launch adds the bias and the residual and normalises (IN_ACC)
   int D;
-  const bf16* wo;            // out-projection weight [D, D]
-  const bf16* bo;            // its bias [D]
-  const float *ln_g, *ln_b;  // the LayerNorm after the residual sum
-  float* part;               // [H][M][D] out-projection partial sums by head
-  unsigned* ticket;          // [M] arrivals per row, zero between launches
-  float* x;                  // [M][D] float32: residual input, then the LayerNorm output
-  bf16* xn;                  // [M][D] the LayerNorm output in bf16 (the next projection's input)
-  // fuse_q (cross attention, kAttnPreStage with kFuseOut, 8 splits, D <= 1024): the kernel
-  // computes its head's query rows itself, q = bf16(xq Wq^T + bq), 8 rows per CTA
+  const bf16* wo;                 // out-projection weight [D, D]
+  unsigned long long* acc_out;    // [M][D]
+  // fuse_q (cross attention, kAttnPreStage with kAccOut, 8 splits, D <= 1024): the kernel
+  // forms its input row itself, x = LayerNorm(x_in + bf16(acc_in + bias_in)) (the previous
+  // attention's residual sum and norm, engine.py:312), writes it to x_out once, and computes
+  // its head's query rows from it, q = bf16(x Wq^T + bq), 8 rows per CTA
+  const unsigned long long* acc_in;  // [M][D]
+  const bf16* bias_in;               // [D]
+  const float* x_in;                 // [M][D]
+  float* x_out;                      // [M][D]
+  const float *ln_g, *ln_b;          // [D]
   const bf16* wq;  // [D, D]
   const bf16* bq;  // [D]
-  const bf16* xq;  // [M, D]: the LayerNorm output the projection reads
   int fuse_q;
 };
 
-constexpr int kAttnLnHeads = 16;     // head partials the fused LayerNorm requests at once
 constexpr int kAttnOutPrefetch = 4;  // out-projection passes (32 features each) loaded before the wait
 
 constexpr int kErrAttnCluster = 1;  // launched without the expected cluster shape
 constexpr int kErrAttnChunk = 2;    // a row's keys do not fit the score buffer
 constexpr int kErrAttnStage = 5;    // a bulk copy into shared memory did not complete in time
 constexpr int kErrAttnExchange = 6; // a value from a peer CTA did not arrive in time
+constexpr int kErrAccRange = 7;     // an out-projection partial too large (or NaN) for the fixed-point sum
 
 // How a CTA gets its keys and values ahead of the PDL wait.
 constexpr int kAttnPreNone = 0;   // read in the loops (batched engines, which keep occupancy)
@@ -84,8 +89,9 @@ constexpr size_t kAttnOtherSmem = 32768;
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxSplits = 8;  // CTAs per (row, head) at most
 constexpr int kAttnGroups = kAttnThreads / 8;  // 8 lanes x 16 bytes per key row
-constexpr int kAttnUnroll = 4;
-constexpr int kAttnQRows = 8;  // fuse_q: query rows computed per CTA (one per warp)       // keys per group and pass (kAttnPreNone / kAttnPreRegs)
+constexpr int kAttnUnroll = 4;  // keys per group and pass (kAttnPreNone / kAttnPreRegs)
+constexpr int kAttnQRows = 8;  // fuse_q: query rows computed per CTA (one per warp)
+constexpr int kAttnQLnGroups = 128;  // fuse_q: 8-column groups of the input row (D <= 1024)
 constexpr int kAttnUnrollStaged = 8;  // the same from shared memory (kAttnPreStage): more keys in flight
 
 __device__ __forceinline__ uint32_t pack_bf16_pair(float a, float b) {
@@ -100,20 +106,22 @@ __device__ __forceinline__ const bf16* attn_row(const AttnArgs& a, const bf16* b
 
 // Dynamic shared memory of one attention CTA: the score buffer, the partial
 // outputs of the key groups and, for kAttnPreStage, the staged key and value
-// rows and (with kFuseOut) the residual row, LayerNorm weights and
-// out-projection bias of the fused tail.  Every part starts 16-byte aligned.
+// rows and (with fuse_q) the input LayerNorm's parameters, the previous
+// out-projection's bias, the CTA's query weight rows and the normalised input
+// row.  Every part starts 16-byte aligned.
 struct AttnSmem {
-  size_t part, sk, sv, sx, sg, sb, sbo, sw, total;
-  __host__ __device__ AttnSmem(int chunk_cap, int stage_cap, int D, bool ln_stage, bool fuse_q = false) {
+  size_t part, sk, sv, sg, sb, sbi, sw, sxq, total;
+  __host__ __device__ AttnSmem(int chunk_cap, int stage_cap, int D, bool fuse_q) {
+    const size_t dq = fuse_q ? (size_t)D : 0;
     part = (size_t)((chunk_cap + 3) & ~3) * 4;
     sk = part + (size_t)kAttnGroups * kHeadDim * 4;
     sv = sk + (size_t)stage_cap * kHeadDim * 2;
-    sx = sv + (size_t)stage_cap * kHeadDim * 2;
-    sg = sx + (ln_stage ? (size_t)D * 4 : 0);
-    sb = sg + (ln_stage ? (size_t)D * 4 : 0);
-    sbo = sb + (ln_stage ? (size_t)D * 4 : 0);
-    sw = sbo + (ln_stage ? (((size_t)D * 2 + 15) & ~(size_t)15) : 0);
-    total = sw + (fuse_q ? (size_t)kAttnQRows * D * 2 : 0);
+    sg = sv + (size_t)stage_cap * kHeadDim * 2;
+    sb = sg + dq * 4;
+    sbi = sb + dq * 4;
+    sw = sbi + ((dq * 2 + 15) & ~(size_t)15);
+    sxq = sw + dq * kAttnQRows * 2;
+    total = sxq + ((dq * 2 + 15) & ~(size_t)15);
   }
 };
 
@@ -130,49 +138,45 @@ struct AttnSmem {
 // Engines below 16 slots use these; the batched engines keep shared memory and
 // registers for occupancy.
 //
-// kFuseOut (engines below 16 slots): the kernel also runs what follows the
-// attention in the reference (engine.py:312-313):
-//     r = x + bf16(o @ Wo^T + bo),   x = LayerNorm(r)
-// Every CTA of the head's cluster adds the C partial outputs in rank order
-// (the same o in each), then computes its 1/C of the output features of the
-// head's share of the out-projection, sum_d Wo[n][64h + d] o[d], as a float32
-// partial sum over the head (the weights are loaded before the PDL wait).  The
-// last CTA of the row (a ticket counter) adds the partials of all heads in
-// head order, the bias and the residual, rounds as the reference does, and
-// writes the LayerNorm output as float32 (the next residual input) and bf16
-// (the next projection's input).  With kAttnPreStage the LayerNorm weights and
-// the bias are staged before the wait and the residual row right after it.
-template <int kPre, bool kFuseOut>
+// kAccOut (engines below 16 slots): the kernel also runs the out-projection
+// that follows the attention in the reference (engine.py:292,312).  Every CTA
+// of the head's cluster adds the C partial outputs in rank order (the same o
+// in each), rounds the head's output to bf16 as the reference does, computes
+// its 1/C of the output features of the head's share of the projection,
+// sum_d Wo[n][64h + d] o[d] (the weights are loaded before the PDL wait), and
+// adds it to acc_out[m][n] as a fixed-point sum: the totals do not depend on
+// the order in which the H*C CTAs of a row arrive, and nothing waits for the
+// last of them.  The next launch adds the bias and the residual and
+// normalises the row (IN_ACC), as reference's self_attn_norm / cross_attn_norm.
+template <int kPre, bool kAccOut>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   constexpr bool kStage = kPre == kAttnPreStage;
-  constexpr bool kLnStage = kStage && kFuseOut;
   constexpr int kU = kStage ? kAttnUnrollStaged : kAttnUnroll;
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.dim_blocks().x;
   const int rank = (int)cluster.block_rank();
   const int h = blockIdx.y, m = a.order ? a.order[blockIdx.z] : (int)blockIdx.z;
   extern __shared__ __align__(16) unsigned char attn_smem[];
-  const bool fuse_q = kLnStage && a.fuse_q;
-  const AttnSmem lay(a.chunk_cap, kStage ? a.stage_cap : 0, a.D, kLnStage, fuse_q);
+  const bool fuse_q = kStage && kAccOut && a.fuse_q;
+  const AttnSmem lay(a.chunk_cap, kStage ? a.stage_cap : 0, a.D, fuse_q);
   float* sc = reinterpret_cast<float*>(attn_smem);                // [chunk_cap] scores, then exp values
   float* part = reinterpret_cast<float*>(attn_smem + lay.part);   // [kAttnGroups][64] partial outputs
   bf16* sk = reinterpret_cast<bf16*>(attn_smem + lay.sk);         // kStage: [stage_cap][64] keys
   bf16* sv = reinterpret_cast<bf16*>(attn_smem + lay.sv);         //         [stage_cap][64] values
-  float* sx = reinterpret_cast<float*>(attn_smem + lay.sx);       // kLnStage: residual row [D]
-  float* sg = reinterpret_cast<float*>(attn_smem + lay.sg);       //           LayerNorm weight [D]
-  float* sb = reinterpret_cast<float*>(attn_smem + lay.sb);       //           LayerNorm bias [D]
-  bf16* sbo = reinterpret_cast<bf16*>(attn_smem + lay.sbo);       //           out-projection bias [D]
-  bf16* sw = reinterpret_cast<bf16*>(attn_smem + lay.sw);         // fuse_q: this CTA's query weight rows [8][D]
+  float* sg = reinterpret_cast<float*>(attn_smem + lay.sg);       // fuse_q: input LayerNorm weight [D]
+  float* sb = reinterpret_cast<float*>(attn_smem + lay.sb);       //         input LayerNorm bias [D]
+  bf16* sbi = reinterpret_cast<bf16*>(attn_smem + lay.sbi);       //         previous out-projection bias [D]
+  bf16* sw = reinterpret_cast<bf16*>(attn_smem + lay.sw);         //         this CTA's query weight rows [8][D]
+  bf16* sxq = reinterpret_cast<bf16*>(attn_smem + lay.sxq);       //         the normalised input row [D]
   __shared__ float xred[2][kAttnMaxSplits];          // every rank's partial max and sum
   __shared__ float xo[kAttnMaxSplits][kHeadDim];      // every rank's partial output
-  __shared__ float wred[kAttnThreads / 32];
   __shared__ float wmax[kAttnThreads / 32], wsum[kAttnThreads / 32];
   __shared__ __align__(16) bf16 sq[kHeadDim];  // kStage: the row's query for this head
   __shared__ __align__(8) uint64_t xbar[4];           // exchanges received: max, sum, output, query
   __shared__ float sqx[kHeadDim];                     // fuse_q: the head's query, from every rank
-  __shared__ float ohead[kHeadDim];                   // kFuseOut: the head's output, bf16-rounded
-  __shared__ int is_last;
-  __shared__ __align__(8) uint64_t bars[2];           // kStage: [0] rows + weights, [1] residual row
+  __shared__ float ohead[kHeadDim];                   // kAccOut: the head's output, bf16-rounded
+  __shared__ float ln_red[kAttnQLnGroups + 2];        // fuse_q: LayerNorm reductions
+  __shared__ __align__(8) uint64_t bars[2];           // kStage: [0] key and value rows, [1] fuse_q operands
 
   pdl_launch_dependents();
   const int tid = threadIdx.x, grp = tid >> 3, sub = tid & 7;
@@ -199,12 +203,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   const int js = kStage ? min(j1, j0 + a.stage_cap) : j0;
   const int jbulk = kStage ? max(j0, min(js, fresh)) : j0;
   uint4 kpre[kU], vpre[kU];  // kAttnPreRegs (kU == kAttnUnroll there)
-  // kFuseOut: this CTA's out-projection features and their weights for head h
-  const int per = kFuseOut ? (a.D + C - 1) / C : 0, n0 = rank * per;
+  // kAccOut: this CTA's out-projection features and their weights for head h
+  const int per = kAccOut ? (a.D + C - 1) / C : 0, n0 = rank * per;
   uint4 wpre[kAttnOutPrefetch];
   // every rank receives the C maxima and sums; the partial outputs go to every
-  // rank with kFuseOut, else to rank 0 alone
-  const bool gets_o = kFuseOut || rank == 0;
+  // rank with kAccOut, else to rank 0 alone
+  const bool gets_o = kAccOut || rank == 0;
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 1);
     if constexpr (kStage) {
@@ -219,8 +223,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   }
   if constexpr (kStage) {
     if (tid == 0) {
-      mbar_expect_tx(&bars[0], (unsigned)(jbulk - j0) * (2 * kHeadDim * 2) + (kLnStage ? (unsigned)a.D * 10 : 0u) +
-                                   (fuse_q ? (unsigned)(kAttnQRows * a.D * 2) : 0u));
+      mbar_expect_tx(&bars[0], (unsigned)(jbulk - j0) * (2 * kHeadDim * 2));
+      mbar_expect_tx(&bars[1], fuse_q ? (unsigned)a.D * 10 + (unsigned)(kAttnQRows * a.D * 2) : 0u);
+      if (fuse_q) {  // first: what the query rows need
+        bulk_load(sg, a.ln_g, (unsigned)a.D * 4, &bars[1]);
+        bulk_load(sb, a.ln_b, (unsigned)a.D * 4, &bars[1]);
+        bulk_load(sbi, a.bias_in, (unsigned)a.D * 2, &bars[1]);
+        // the CTA's 8 query rows of head h: contiguous in Wq
+        bulk_load(sw, a.wq + (size_t)(h * kHeadDim + rank * kAttnQRows) * a.D, (unsigned)(kAttnQRows * a.D * 2),
+                  &bars[1]);
+      }
       // one copy per run of rows that is contiguous in memory (a page of the
       // self-attention pool; the whole range for cross-attention)
       for (int s = j0; s < jbulk;) {
@@ -230,17 +242,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         bulk_load(sv + (size_t)(s - j0) * kHeadDim, attn_row(a, a.v, slot, h, s), bytes, &bars[0]);
         s = e;
       }
-      if constexpr (kLnStage) {
-        bulk_load(sg, a.ln_g, (unsigned)a.D * 4, &bars[0]);
-        bulk_load(sb, a.ln_b, (unsigned)a.D * 4, &bars[0]);
-        bulk_load(sbo, a.bo, (unsigned)a.D * 2, &bars[0]);
-        if (fuse_q)  // the CTA's 8 query rows of head h: contiguous in Wq
-          bulk_load(sw, a.wq + (size_t)(h * kHeadDim + rank * kAttnQRows) * a.D, (unsigned)(kAttnQRows * a.D * 2),
-                    &bars[0]);
-      }
     }
   }
-  if constexpr (kFuseOut) {
+  if constexpr (kAccOut) {
 #pragma unroll
     for (int p = 0; p < kAttnOutPrefetch; ++p) {
       const int i = p * kAttnGroups + grp, n = n0 + i;
@@ -260,10 +264,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   }
   // kStage: whether this thread saw the copies land (if not, it waits for them
   // again, bounded, before the CTA exits; the error word is set either way)
-  bool staged = true, row_staged = true;
+  bool staged = true, q_staged = true;
   auto drain = [&]() {
     if (kStage && !staged) mbar_wait(&bars[0], 0);
-    if (kLnStage && !row_staged) mbar_wait(&bars[1], 0);
+    if (fuse_q && !q_staged) mbar_wait(&bars[1], 0);
   };
   __syncthreads();  // the barriers are initialised before anyone waits on them
   // First half of a barrier that proves every peer has started and initialised
@@ -272,49 +276,54 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   cluster_arrive_relaxed();
   pdl_wait();
 
-  if constexpr (kLnStage) {
-    if (tid == 0) {  // the residual row was written by the previous kernel
-      mbar_expect_tx(&bars[1], (unsigned)a.D * 4);
-      bulk_load(sx, a.x + (size_t)m * a.D, (unsigned)a.D * 4, &bars[1]);
-    }
-  }
   const uint4 qraw = fuse_q ? make_uint4(0, 0, 0, 0)
                             : *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);
-  if constexpr (kLnStage) {
-    if (fuse_q) {
-      // This CTA's 8 query rows of head h, one per warp, with the projection
-      // kernel's arithmetic (16-byte pieces of 8 products, pieces added in
-      // order, then the warp butterfly; + bias, rounded to bf16), sent to
-      // every rank of the cluster.
-      const int kch = a.D / 256;
-      const bf16* xrow = a.xq + (size_t)m * a.D;
-      uint4 xv[4];
+  if (fuse_q) {
+    // The input row, LayerNorm(x_in + bf16(acc_in + bias_in)), by the whole
+    // block in the order every LayerNorm of the step uses (thread t holds
+    // columns 8t .. 8t+7); CTA (rank 0, head 0) keeps the float32 row.
+    ProjArgs pa{};
+    pa.K = a.D;
+    pa.r = a.x_in;
+    pa.acc = a.acc_in;
+    pa.acc_bias = sbi;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int col = tid * 8;
+    q_staged = mbar_wait(&bars[1], 0);  // parameters, bias and weight rows
+    if (!q_staged) atomicExch(a.err, kErrAttnStage);
+    if (col < a.D) ln_inputs8<IN_ACC>(pa, m, col, v);
+    const float2 st = block_ln_stats<kAttnQLnGroups / 32, kAttnThreads>(v, a.D, ln_red);
+    if (col < a.D) {
+      float y[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        xv[c] = c < kch ? *reinterpret_cast<const uint4*>(xrow + c * 256 + lane * 8) : make_uint4(0, 0, 0, 0);
-      staged = mbar_wait(&bars[0], 0);  // the weight rows came with the stage
-      const bf16* wrow = sw + (size_t)warp * a.D;
-      float acc = 0.f;
+      for (int j = 0; j < 8; ++j) y[j] = ln_apply(v[j], st.x, st.y, sg[col + j], sb[col + j]);
+      *reinterpret_cast<uint4*>(sxq + col) =
+          make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+      if (rank == 0 && h == 0) {
+        float* dst = a.x_out + (size_t)m * a.D + col;
+        *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+      }
+    }
+    __syncthreads();
+    // This CTA's 8 query rows of head h, one per warp, with the projection
+    // kernel's arithmetic (16-byte pieces of 8 products, pieces added in
+    // order, then the warp butterfly; + bias, rounded to bf16), sent to
+    // every rank of the cluster.
+    const int kch = a.D / 256;
+    const bf16* wrow = sw + (size_t)warp * a.D;
+    float acc = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c >= kch) break;
-        const uint4 w = *reinterpret_cast<const uint4*>(wrow + c * 256 + lane * 8);
-        float d = bf_lo(w.x) * bf_lo(xv[c].x);
-        d = fmaf(bf_hi(w.x), bf_hi(xv[c].x), d);
-        d = fmaf(bf_lo(w.y), bf_lo(xv[c].y), d);
-        d = fmaf(bf_hi(w.y), bf_hi(xv[c].y), d);
-        d = fmaf(bf_lo(w.z), bf_lo(xv[c].z), d);
-        d = fmaf(bf_hi(w.z), bf_hi(xv[c].z), d);
-        d = fmaf(bf_lo(w.w), bf_lo(xv[c].w), d);
-        d = fmaf(bf_hi(w.w), bf_hi(xv[c].w), d);
-        acc += d;
-      }
-      acc = warp_sum(acc);
-      cluster_wait();  // every peer has started: the first store into its shared memory follows
-      if (lane == 0) {
-        const float qb = round_bf16(acc + qbias);
-        for (int r = 0; r < C; ++r) st_async_f32(&sqx[rank * kAttnQRows + warp], r, qb, &xbar[3]);
-      }
+    for (int c = 0; c < 4; ++c) {
+      if (c >= kch) break;
+      const uint4 w = *reinterpret_cast<const uint4*>(wrow + c * 256 + lane * 8);
+      acc += dot8(w, *reinterpret_cast<const uint4*>(sxq + c * 256 + lane * 8));
+    }
+    acc = warp_sum(acc);
+    cluster_wait();  // every peer has started: the first store into its shared memory follows
+    if (lane == 0) {
+      const float qb = round_bf16(acc + qbias);
+      for (int r = 0; r < C; ++r) st_async_f32(&sqx[rank * kAttnQRows + warp], r, qb, &xbar[3]);
     }
   }
   if constexpr (kStage) {
@@ -334,7 +343,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     }
     __syncthreads();
   }
-
   // ---- scores and local max
   float lmax = -INFINITY;
   if constexpr (kStage) {
@@ -475,7 +483,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   if (tid < kHeadDim) {
     float o = 0.f;
     for (int g = 0; g < kAttnGroups; ++g) o += part[g * kHeadDim + tid];
-    if (kFuseOut) {  // every rank needs the head's output
+    if (kAccOut) {  // every rank needs the head's output
       for (int r = 0; r < C; ++r) st_async_f32(&xo[rank][tid], r, o, &xbar[2]);
     } else {
       st_async_f32(&xo[rank][tid], 0, o, &xbar[2]);
@@ -487,7 +495,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   // the whole cluster to get here, so no CTA leaves while a store into it
   // could still be on its way.
   cluster_arrive_relaxed();
-  if constexpr (!kFuseOut) {
+  if constexpr (!kAccOut) {
     if (rank == 0 && tid < kHeadDim) {
       float o = 0.f;
       for (int r = 0; r < C; ++r) o += xo[r][tid];
@@ -505,6 +513,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     float oh[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) oh[t] = ohead[sub * 8 + t];
+    bool in_range = true;
     auto emit = [&](int p, uint4 w) {  // features of pass p: 32 of them, one per group of 8 lanes
       const int i = p * kAttnGroups + grp, n = n0 + i;
       float d = bf_lo(w.x) * oh[0];
@@ -518,7 +527,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       d += __shfl_xor_sync(0xffffffffu, d, 1);
       d += __shfl_xor_sync(0xffffffffu, d, 2);
       d += __shfl_xor_sync(0xffffffffu, d, 4);
-      if (i < per && n < a.D && sub == 0) a.part[((size_t)h * a.M + m) * a.D + n] = d;
+      if (i < per && n < a.D && sub == 0) in_range &= acc_add(a.acc_out + (size_t)m * a.D + n, d);
     };
     // pass counts are uniform across the block: the shuffles need every lane
 #pragma unroll
@@ -528,107 +537,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       const int i = p * kAttnGroups + grp, n = n0 + i;
       emit(p, (i < per && n < a.D) ? ld_stream(a.wo + (size_t)n * a.D + h * kHeadDim + sub * 8) : make_uint4(0, 0, 0, 0));
     }
-    // ---- the last CTA of the row: residual sum and LayerNorm
-    __syncthreads();  // the block's partials are written
-    if (tid == 0) {
-      // The residual row copy has landed before the ticket, so the last CTA's
-      // rewrite of the row cannot overtake it.
-      if (kLnStage) row_staged = mbar_wait(&bars[1], 0);
-      if (!row_staged) atomicExch(a.err, kErrAttnStage);
-      unsigned prev;
-      // release: the block's partials (ordered before by the barrier); acquire: everyone else's
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.ticket + m) : "memory");
-      is_last = prev == (unsigned)(a.H * C) - 1;
-      if (is_last) a.ticket[m] = 0u;
-    }
-    __syncthreads();
-    if (!is_last) {
-      drain();
-      cluster_wait();
-      return;
-    }
-    // completed already: the wait makes the row visible to every thread
-    if constexpr (kLnStage) row_staged = mbar_wait(&bars[1], 0);
-    constexpr int kCols = 16;  // columns per thread (width <= 4096)
-    float r[kCols];
-    float sum = 0.f;
-#pragma unroll
-    for (int c = 0; c < kCols / 4; ++c) {
-      const int col = c * 4 * kAttnThreads + tid * 4;
-      float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (col < a.D) {
-        // the head partials, all requested before the first is added (head order)
-        const float* pcol = a.part + (size_t)m * a.D + col;
-        const size_t hstride = (size_t)a.M * a.D;
-        float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 p4[kAttnLnHeads];
-        for (int h0 = 0; h0 < a.H; h0 += kAttnLnHeads) {
-#pragma unroll
-          for (int i = 0; i < kAttnLnHeads; ++i)
-            p4[i] = h0 + i < a.H ? __ldcg(reinterpret_cast<const float4*>(pcol + (h0 + i) * hstride))
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int i = 0; i < kAttnLnHeads; ++i) {
-            if (h0 + i >= a.H) break;
-            acc4.x += p4[i].x;
-            acc4.y += p4[i].y;
-            acc4.z += p4[i].z;
-            acc4.w += p4[i].w;
-          }
-        }
-        const float4 x4 = kLnStage ? *reinterpret_cast<const float4*>(sx + col)
-                                   : *reinterpret_cast<const float4*>(a.x + (size_t)m * a.D + col);
-        const bf16* bo = kLnStage ? sbo : a.bo;
-        v4.x = x4.x + round_bf16(acc4.x + __bfloat162float(bo[col + 0]));
-        v4.y = x4.y + round_bf16(acc4.y + __bfloat162float(bo[col + 1]));
-        v4.z = x4.z + round_bf16(acc4.z + __bfloat162float(bo[col + 2]));
-        v4.w = x4.w + round_bf16(acc4.w + __bfloat162float(bo[col + 3]));
-      }
-      r[c * 4 + 0] = v4.x;
-      r[c * 4 + 1] = v4.y;
-      r[c * 4 + 2] = v4.z;
-      r[c * 4 + 3] = v4.w;
-      sum += (v4.x + v4.y) + (v4.z + v4.w);
-    }
-    // LayerNorm (two-pass, biased variance), block sums in fixed warp order
-    sum = warp_sum(sum);
-    if (lane == 0) wred[warp] = sum;
-    __syncthreads();
-    float mean = 0.f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) mean += wred[w];
-    mean /= (float)a.D;
-    __syncthreads();
-    float sq = 0.f;
-#pragma unroll
-    for (int c = 0; c < kCols / 4; ++c) {
-      if (c * 4 * kAttnThreads + tid * 4 < a.D) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float d = r[c * 4 + j] - mean;
-          sq = fmaf(d, d, sq);
-        }
-      }
-    }
-    sq = warp_sum(sq);
-    if (lane == 0) wred[warp] = sq;
-    __syncthreads();
-    float var = 0.f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) var += wred[w];
-    const float rstd = rsqrtf(var / (float)a.D + kLnEps);
-    const float* g = kLnStage ? sg : a.ln_g;
-    const float* b = kLnStage ? sb : a.ln_b;
-#pragma unroll
-    for (int c = 0; c < kCols / 4; ++c) {
-      const int col = c * 4 * kAttnThreads + tid * 4;
-      if (col < a.D) {
-        float y[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) y[j] = (r[c * 4 + j] - mean) * rstd * g[col + j] + b[col + j];
-        *reinterpret_cast<float4*>(a.x + (size_t)m * a.D + col) = make_float4(y[0], y[1], y[2], y[3]);
-        *reinterpret_cast<uint2*>(a.xn + (size_t)m * a.D + col) =
-            make_uint2(pack_bf16_pair(y[0], y[1]), pack_bf16_pair(y[2], y[3]));
-      }
-    }
+    if (!in_range) atomicExch(a.err, kErrAccRange);
     drain();
     cluster_wait();
   }

@@ -65,6 +65,26 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Fixed-point sums across CTAs.  A float partial v is added to a 64-bit
+// accumulator as round(v * 2^32) with an integer atomic, so the total does
+// not depend on the order in which CTAs arrive (deterministic, batch- and
+// schedule-invariant) and is exact up to the one rounding per partial.
+// Partials must stay below 2^26 in magnitude (|total| < 2^31 for up to 32
+// of them); a larger or NaN partial is not added and reported by the caller.
+constexpr float kAccScale = 4294967296.0f;  // 2^32
+constexpr float kAccLimit = 67108864.0f;    // 2^26
+
+__device__ __forceinline__ bool acc_add(unsigned long long* p, float v) {
+  if (!(fabsf(v) < kAccLimit)) return false;
+  atomicAdd(p, (unsigned long long)__float2ll_rn(v * kAccScale));  // a reduction: no value returned
+  return true;
+}
+
+// The float value of an accumulator: the nearest float to the integer, scaled back.
+__device__ __forceinline__ float acc_value(unsigned long long u) {
+  return __ll2float_rn((long long)u) * (1.0f / kAccScale);
+}
+
 // Which slot, position and input token a row of the current launch stands for.
 // Decode: row r is slot r with the slot's own token and position.  Prefill:
 // every row belongs to one slot, rows are consecutive positions from pos0 and

@@ -159,11 +159,12 @@ struct s2r_ctx {
   // when `tc` (16 or more slots), the cross K/V projection at load when `tc_cross`
   bool tc = false, tc_cross = false;
   int tc_nb = 64;                  // rows per MMA tile of the step and prefill projections
-  // engines below 16 slots fuse each attention with its out-projection, residual and LayerNorm
+  // engines below 16 slots fuse each attention with its out-projection (fixed-point sums in
+  // acc_self / acc_cross); the next launch adds bias and residual and normalises (IN_ACC)
   bool fuse_out = false;
-  float* attn_part = nullptr;      // [H][maxM][D] out-projection partial sums by head
-  unsigned* attn_ticket = nullptr; // [maxM]
-  bf16* xn = nullptr;              // [maxM][D] LayerNorm output in bf16
+  unsigned long long* acc_self = nullptr;   // [maxM][D]
+  unsigned long long* acc_cross = nullptr;  // [maxM][D]
+  float* x_b = nullptr;                     // [maxM][D] the cross attention's residual input
   int attn_splits = 8;             // CTAs (one cluster) per (row, head) of the self-attention
   int attn_splits_cross = 8;       // ... and of the cross-attention
   int32_t *order_self = nullptr, *order_cross = nullptr;  // [B] decode rows, longest first (tensor-core engines)
@@ -345,6 +346,7 @@ void tc_split(int tiles, int k_tiles, int sms, int* splits, int* per) {
 // produces its bf16 rows (when the input is not bf16 already), then the GEMM
 // with the projection's epilogue.  `lg` is the logits epilogue's state.
 int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, const LogitsArgs* lg = nullptr) {
+  if (in == IN_ACC) return fail(S2R_ENOTSUP, "accumulated out-projection inputs run on the CUDA-core kernels only");
   const bool cross = epi == EPI_CROSSKV;
   const int nb = cross ? 128 : c->tc_nb;
   const void* x = a.xin;
@@ -391,7 +393,7 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
   if (!fn) return fail(S2R_ENOTSUP, "no projection kernel for in=%d epi=%d", in, epi);
   // staged rows, then the LayerNorm parameters for LayerNorm'd inputs
   const size_t smem = (size_t)(mc == 8 ? 8 : mc) * kch * 256 * sizeof(bf16) +
-                      ((in == IN_LN || in == IN_EMBED) ? 2 * (size_t)kch * 256 * sizeof(float) : 0);
+                      ((in == IN_LN || in == IN_EMBED || in == IN_ACC) ? 2 * (size_t)kch * 256 * sizeof(float) : 0);
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int threads = mc == 1 ? proj_threads<1>() : proj_threads<2>(), warps = threads / 32;
   const int blocks = (a.N + warps - 1) / warps;
@@ -463,7 +465,7 @@ AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
     const int ctas = M * c->H * p.C;
     const int per_sm = std::max(1, (ctas + c->num_sms - 1) / c->num_sms);
     const size_t budget = ((size_t)c->smem_per_sm - kAttnOtherSmem) / (2 * per_sm);
-    const size_t fixed = AttnSmem(p.chunk_cap, 0, c->D, c->fuse_out, can_fuse_q).total + kAttnStaticSmem;
+    const size_t fixed = AttnSmem(p.chunk_cap, 0, c->D, can_fuse_q).total + kAttnStaticSmem;
     if (budget > fixed) {
       const int cap = (int)std::min<size_t>(p.chunk_cap, (budget - fixed) / (2 * kHeadDim * 2));
       if (cap == p.chunk_cap || cap >= kAttnGroups * kAttnUnroll) {
@@ -473,7 +475,7 @@ AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
       }
     }
   }
-  p.smem = AttnSmem(p.chunk_cap, p.stage_cap, c->D, p.pre == kAttnPreStage && c->fuse_out, p.fuse_q).total;
+  p.smem = AttnSmem(p.chunk_cap, p.stage_cap, c->D, p.fuse_q).total;
   return p;
 }
 
@@ -501,17 +503,16 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
     const LayerBufs& w = c->layers[layer];
     a.D = c->D;
     a.wo = cross ? w.wco : w.wo;
-    a.bo = cross ? w.bco : w.bo;
-    a.ln_g = cross ? w.ln_cross_g : w.ln_self_g;
-    a.ln_b = cross ? w.ln_cross_b : w.ln_self_b;
-    a.part = c->attn_part;
-    a.ticket = c->attn_ticket;
-    a.x = c->x;
-    a.xn = c->xn;
-    if (plan.fuse_q) {
+    a.acc_out = cross ? c->acc_cross : c->acc_self;
+    if (plan.fuse_q) {  // the cross attention's input: self_attn_norm(x + bf16(self out-projection))
+      a.acc_in = c->acc_self;
+      a.bias_in = w.bo;
+      a.x_in = c->x;
+      a.x_out = c->x_b;
+      a.ln_g = w.ln_self_g;
+      a.ln_b = w.ln_self_b;
       a.wq = w.wcq;
       a.bq = w.bcq;
-      a.xq = c->xn;
       a.fuse_q = 1;
     }
   }
@@ -561,40 +562,50 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   }
   if (last_kv_only) return S2R_OK;
   if (c->fuse_out) {
-    // attention with its out-projection, residual and LayerNorm fused (attention.cuh); the
-    // projections after them read the bf16 LayerNorm output
-    TRY(launch_attn(c, rm, M, l, false, s));  // 2-3. self-attention ... self_attn_norm
+    // each attention fused with its out-projection (attention.cuh): fixed-point sums in
+    // acc_self / acc_cross; the launch after it adds bias and residual and normalises (IN_ACC)
+    TRY(launch_attn(c, rm, M, l, false, s));  // 2-3. self-attention + out-projection
     TRY(mark(c, K_SELF_ATTN, s));
-    if (!plan_attn(c, M, true).fuse_q) {  // 4. cross q (else the cross attention computes it)
+    if (!plan_attn(c, M, true).fuse_q) {  // 4. self_attn_norm -> cross q (else the cross attention does it)
       ProjArgs a = proj_base(c);
       a.rm = rm;
       a.M = M;
       a.K = D;
       a.N = D;
-      a.xin = c->xn;
-      a.ldx = D;
+      a.r = c->x;
+      a.acc = c->acc_self;
+      a.acc_bias = w.bo;
+      a.gamma = w.ln_self_g;
+      a.beta = w.ln_self_b;
+      a.x_out = c->x_b;
       a.W = w.wcq;
       a.bias = w.bcq;
       a.out = c->q;
       a.ldo = D;
-      TRY(launch_proj(c, a, IN_BF16, EPI_BF16, s));
+      TRY(launch_proj(c, a, IN_ACC, EPI_BF16, s));
       TRY(mark(c, K_CROSS_Q, s));
     }
-    TRY(launch_attn(c, rm, M, l, true, s));  // 5-6. cross-attention ... cross_attn_norm
+    TRY(launch_attn(c, rm, M, l, true, s));  // 5-6. cross-attention + out-projection
     TRY(mark(c, K_CROSS_ATTN, s));
-    {  // 7. fc1 + GELU
+    {  // 7. cross_attn_norm -> fc1 + GELU; acc_self has been read
       ProjArgs a = proj_base(c);
       a.rm = rm;
       a.M = M;
       a.K = D;
       a.N = c->FFN;
-      a.xin = c->xn;
-      a.ldx = D;
+      a.r = c->x_b;
+      a.acc = c->acc_cross;
+      a.acc_bias = w.bco;
+      a.gamma = w.ln_cross_g;
+      a.beta = w.ln_cross_b;
+      a.x_out = c->x;
       a.W = w.w1;
       a.bias = w.b1;
       a.out = c->hid;
       a.ldo = c->FFN;
-      TRY(launch_proj(c, a, IN_BF16, EPI_GELU, s));
+      a.zero = c->acc_self;
+      a.zero_n = M * D;
+      TRY(launch_proj(c, a, IN_ACC, EPI_GELU, s));
       TRY(mark(c, K_FC1, s));
     }
   } else {
@@ -667,7 +678,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     TRY(mark(c, K_FC1, s));
   }
   }
-  {  // 8. fc2 + residual
+  {  // 8. fc2 + residual; acc_cross has been read
     ProjArgs a = proj_base(c);
     a.rm = rm;
     a.M = M;
@@ -679,6 +690,10 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     a.bias = w.b2;
     a.r_out = c->r;
     a.x_res = c->x;
+    if (c->fuse_out) {
+      a.zero = c->acc_cross;
+      a.zero_n = M * D;
+    }
     TRY(launch_proj(c, a, IN_BF16, EPI_RESID, s));
     TRY(mark(c, K_FC2, s));
   }
@@ -929,13 +944,15 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   if (c->bar) CK(cudaMemsetAsync(c->bar, 0, 2 * sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->counter, 0, sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->keys, 0, c->B * sizeof(unsigned long long), s));
-  if (c->attn_ticket) CK(cudaMemsetAsync(c->attn_ticket, 0, c->maxM * sizeof(unsigned), s));
+  if (c->acc_self) CK(cudaMemsetAsync(c->acc_self, 0, (size_t)c->maxM * c->D * sizeof(unsigned long long), s));
+  if (c->acc_cross) CK(cudaMemsetAsync(c->acc_cross, 0, (size_t)c->maxM * c->D * sizeof(unsigned long long), s));
   return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
               err == kErrAttnCluster ? "attention launched without its cluster shape"
               : err == kErrAttnChunk ? "attention keys exceed the score buffer"
               : err == kErrAttnStage ? "a bulk copy of the attention kernel did not complete in time"
               : err == kErrAttnExchange ? "a value sent between attention CTAs did not arrive in time"
               : err == kErrGemmWait  ? "a wait of the tensor-core projection timed out"
+              : err == kErrAccRange  ? "an out-projection partial was too large (or NaN) for the fixed-point sum"
                                      : "a grid barrier of the persistent step timed out");
 }
 
@@ -1130,11 +1147,12 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   TRYC(setup_tensor_core(c));
   c->fuse_out = !c->tc && !c->persistent;
   if (c->fuse_out) {
-    TRYC(dalloc(c, &c->attn_part, (size_t)c->H * c->maxM * D));
-    TRYC(dalloc(c, &c->attn_ticket, c->maxM));
-    TRYC(dalloc(c, &c->xn, (size_t)c->maxM * D));
-    CKC(cudaMemset(c->attn_ticket, 0, c->maxM * sizeof(unsigned)));
-    CKC(cudaMemset(c->xn, 0, (size_t)c->maxM * D * sizeof(bf16)));
+    TRYC(dalloc(c, &c->acc_self, (size_t)c->maxM * D));
+    TRYC(dalloc(c, &c->acc_cross, (size_t)c->maxM * D));
+    TRYC(dalloc(c, &c->x_b, (size_t)c->maxM * D));
+    CKC(cudaMemset(c->acc_self, 0, (size_t)c->maxM * D * sizeof(unsigned long long)));
+    CKC(cudaMemset(c->acc_cross, 0, (size_t)c->maxM * D * sizeof(unsigned long long)));
+    CKC(cudaMemset(c->x_b, 0, (size_t)c->maxM * D * sizeof(float)));
   }
   c->attn_splits = attn_splits_for(c, 4);
   c->attn_splits_cross = attn_splits_for(c, 8);

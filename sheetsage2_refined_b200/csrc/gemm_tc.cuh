@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(128) ln_rows_kernel(const ProjArgs a, bf16* __
   pdl_wait();
   // one row per CTA, staged by the whole block
   const int m = blockIdx.x;
-  stage_ln_row_block<KCH, IN>(a, xb + (size_t)m * (KCH * 256), m, a.gamma, a.beta);
+  stage_ln_row_block<KCH, IN>(a, xb + (size_t)m * (KCH * 256), m, a.gamma, a.beta, true);
 }
 
 }  // namespace s2r

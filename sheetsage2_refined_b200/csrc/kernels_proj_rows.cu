@@ -5,8 +5,6 @@ namespace s2r {
 
 ProjFn proj_fn_rows(int in, int epi, int kch, int mc) {
   if (in == IN_BF16 && epi == EPI_RESID) return pick_proj<IN_BF16, EPI_RESID>(kch, mc);
-  if (in == IN_BF16 && epi == EPI_BF16) return pick_proj<IN_BF16, EPI_BF16>(kch, mc);  // cross q after a fused attention
-  if (in == IN_BF16 && epi == EPI_GELU) return pick_proj<IN_BF16, EPI_GELU>(kch, mc);  // fc1 after a fused attention
   if (in == IN_BF16 && epi == EPI_CROSSKV) return pick_proj<IN_BF16, EPI_CROSSKV>(kch, mc);
   if (in == IN_F32 && epi == EPI_CROSSKV) return pick_proj<IN_F32, EPI_CROSSKV>(kch, mc);
   return nullptr;

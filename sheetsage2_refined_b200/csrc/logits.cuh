@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
     if constexpr (MC == 1)
-      stage_ln_row_block<KCH, IN_LN, NW * 32>(pa, xs, m0, a.gamma, a.beta);
+      stage_ln_row_block<KCH, IN_LN, NW * 32>(pa, xs, m0, a.gamma, a.beta, false);
     else
       stage_ln_rows<KCH, IN_LN>(pa, xs, m0, mc, warp, lane, NW);
     for (int idx = threadIdx.x; idx < (MC - mc) * (KP / 8); idx += blockDim.x) {

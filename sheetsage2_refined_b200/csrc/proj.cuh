@@ -11,6 +11,9 @@
 //   IN_LN     LayerNorm of the residual sum r              (decoder.py:78,81,84)
 //   IN_BF16   bfloat16 rows (attention output, GELU hidden, encoder memory)
 //   IN_F32    float32 rows rounded to bfloat16 (float32 encoder memory)
+//   IN_ACC    LayerNorm of x + bf16(s + b), s the fixed-point out-projection sums
+//             an attention launch accumulated (decoder.py:81-84 after the
+//             attention, engine.py:312-313)
 // and the epilogue applies what follows it:
 //   EPI_QKV     q to a buffer, k/v appended to the paged self K/V cache (engine.py:310-311)
 //   EPI_RESID   r = x + bf16(acc + b): the residual sum before the next LayerNorm
@@ -26,7 +29,10 @@
 
 namespace s2r {
 
-enum InMode { IN_LN = 0, IN_EMBED = 1, IN_BF16 = 2, IN_F32 = 3 };
+enum InMode { IN_LN = 0, IN_EMBED = 1, IN_BF16 = 2, IN_F32 = 3, IN_ACC = 4 };
+
+template <int IN>
+__host__ __device__ constexpr bool ln_input() { return IN == IN_LN || IN == IN_EMBED || IN == IN_ACC; }
 enum EpiMode { EPI_QKV = 0, EPI_RESID = 1, EPI_BF16 = 2, EPI_GELU = 3, EPI_CROSSKV = 4 };
 
 struct ProjArgs {
@@ -34,7 +40,9 @@ struct ProjArgs {
   RowMap rm;
   SlotState st;
   // input
-  const float* r;      // IN_LN: [M, K] residual sums
+  const float* r;      // IN_LN: [M, K] residual sums; IN_ACC: [M, K] the residual input x
+  const unsigned long long* acc;  // IN_ACC: [M, K] fixed-point out-projection sums (acc_add)
+  const bf16* acc_bias;           // IN_ACC: [K] that projection's bias
   const float* gamma;  // IN_LN / IN_EMBED: LayerNorm weight [K]
   const float* beta;   //                   LayerNorm bias [K]
   const float* tok_emb;
@@ -56,6 +64,9 @@ struct ProjArgs {
   int pages_per_slot;
   int frames_cap;
   int cross_slot;
+  // words cleared after the wait: an accumulator whose reader has finished
+  unsigned long long* zero;
+  int zero_n;
 };
 
 __device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
@@ -114,9 +125,72 @@ __device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int m, int n, f
   proj_epilogue_biased<EPI>(a, m, n, acc + __bfloat162float(a.bias[n]));
 }
 
+// The 8 LayerNorm inputs at columns col .. col+7 (< K) of row m.
+template <int IN>
+__device__ __forceinline__ void ln_inputs8(const ProjArgs& a, int m, int col, float v[8]) {
+  if constexpr (IN == IN_ACC) {
+    const float* x = a.r + (size_t)m * a.K + col;
+    const ulonglong2* sum = reinterpret_cast<const ulonglong2*>(a.acc + (size_t)m * a.K + col);
+    const uint4 b = *reinterpret_cast<const uint4*>(a.acc_bias + col);
+    const float4 x0 = *reinterpret_cast<const float4*>(x), x1 = *reinterpret_cast<const float4*>(x + 4);
+    const ulonglong2 s0 = __ldcg(sum), s1 = __ldcg(sum + 1), s2 = __ldcg(sum + 2), s3 = __ldcg(sum + 3);
+    // the out-projection is a bf16 Linear output (bias added, rounded once), then added to x
+    v[0] = x0.x + round_bf16(acc_value(s0.x) + bf_lo(b.x));
+    v[1] = x0.y + round_bf16(acc_value(s0.y) + bf_hi(b.x));
+    v[2] = x0.z + round_bf16(acc_value(s1.x) + bf_lo(b.y));
+    v[3] = x0.w + round_bf16(acc_value(s1.y) + bf_hi(b.y));
+    v[4] = x1.x + round_bf16(acc_value(s2.x) + bf_lo(b.z));
+    v[5] = x1.y + round_bf16(acc_value(s2.y) + bf_hi(b.z));
+    v[6] = x1.z + round_bf16(acc_value(s3.x) + bf_lo(b.w));
+    v[7] = x1.w + round_bf16(acc_value(s3.y) + bf_hi(b.w));
+  } else {
+    const float* src0 = IN == IN_EMBED ? a.tok_emb + (size_t)row_token(a.rm, a.st, m) * a.K : a.r + (size_t)m * a.K;
+    float4 p0 = *reinterpret_cast<const float4*>(src0 + col);
+    float4 p1 = *reinterpret_cast<const float4*>(src0 + col + 4);
+    if constexpr (IN == IN_EMBED) {
+      const float* src1 = a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * a.K;  // POSITION_OFFSET
+      const float4 q0 = *reinterpret_cast<const float4*>(src1 + col);
+      const float4 q1 = *reinterpret_cast<const float4*>(src1 + col + 4);
+      p0.x += q0.x; p0.y += q0.y; p0.z += q0.z; p0.w += q0.w;
+      p1.x += q1.x; p1.y += q1.y; p1.z += q1.z; p1.w += q1.w;
+    }
+    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+  }
+}
+
+// LayerNorm statistics in one fixed order whatever the thread layout: the 8
+// values of each column group g (columns 8g .. 8g+7) are summed in column
+// order, lane l then adds the groups l, l + 32, l + 64, ... in that order, and
+// the 32 lanes are added by warp_sum's butterfly; the variance takes the same
+// order over (v - mean)^2.  Every LayerNorm of a step (projection prologues by
+// a warp or a whole block, the attention prologue, the tensor-core pre-pass,
+// the logits) uses it, so a row normalises to the same bits in a prefill chunk
+// and in a decode step.
+__device__ __forceinline__ float group_sum8(const float* v) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += v[j];
+  return s;
+}
+
+__device__ __forceinline__ float group_sq8(const float* v, float mean) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float d = v[j] - mean;
+    s = fmaf(d, d, s);
+  }
+  return s;
+}
+
+__device__ __forceinline__ float ln_apply(float v, float mean, float rstd, float g, float b) {
+  return fmaf((v - mean) * rstd, g, b);
+}
+
 // Normalise rows [m0, m0+mc) into xs (bfloat16, KP columns per row, zero
 // padded) and keep the float32 result in x_out.  One warp per row; each lane
-// holds its 8*KCH columns in registers (two-pass mean / variance).
+// holds its 8*KCH columns (groups lane + 32c) in registers.
 // sgamma / sbeta: the LayerNorm parameters already in shared memory (or null: read from a.gamma / a.beta).
 template <int KCH, int IN>
 __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m0, int mc, int warp, int lane,
@@ -129,31 +203,13 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
   for (int i = warp; i < mc; i += nwarps) {
     const int m = m0 + i;
     float v[KCH * 8];
-    const float* src0 = nullptr;
-    const float* src1 = nullptr;
-    if constexpr (IN == IN_EMBED) {
-      src0 = a.tok_emb + (size_t)row_token(a.rm, a.st, m) * K;
-      src1 = a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * K;  // POSITION_OFFSET, decoder.py:24-25
-    } else {
-      src0 = a.r + (size_t)m * K;
-    }
     float sum = 0.f;
 #pragma unroll
     for (int c = 0; c < KCH; ++c) {
       const int col = c * 256 + lane * 8;
       if (col < K) {
-        float4 p0 = *reinterpret_cast<const float4*>(src0 + col);
-        float4 p1 = *reinterpret_cast<const float4*>(src0 + col + 4);
-        if constexpr (IN == IN_EMBED) {
-          float4 q0 = *reinterpret_cast<const float4*>(src1 + col);
-          float4 q1 = *reinterpret_cast<const float4*>(src1 + col + 4);
-          p0.x += q0.x; p0.y += q0.y; p0.z += q0.z; p0.w += q0.w;
-          p1.x += q1.x; p1.y += q1.y; p1.z += q1.z; p1.w += q1.w;
-        }
-        v[c * 8 + 0] = p0.x; v[c * 8 + 1] = p0.y; v[c * 8 + 2] = p0.z; v[c * 8 + 3] = p0.w;
-        v[c * 8 + 4] = p1.x; v[c * 8 + 5] = p1.y; v[c * 8 + 6] = p1.z; v[c * 8 + 7] = p1.w;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sum += v[c * 8 + j];
+        ln_inputs8<IN>(a, m, col, v + c * 8);
+        sum += group_sum8(v + c * 8);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[c * 8 + j] = 0.f;
@@ -162,15 +218,8 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
     const float mean = warp_sum(sum) / (float)K;
     float sq = 0.f;
 #pragma unroll
-    for (int c = 0; c < KCH; ++c) {
-      if (c * 256 + lane * 8 < K) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float d = v[c * 8 + j] - mean;
-          sq = fmaf(d, d, sq);
-        }
-      }
-    }
+    for (int c = 0; c < KCH; ++c)
+      if (c * 256 + lane * 8 < K) sq += group_sq8(v + c * 8, mean);
     const float rstd = rsqrtf(warp_sum(sq) / (float)K + kLnEps);
     // x_out is written once per row: by this CTA when it owns the rows it
     // stages, else by CTA m % gridDim.x (every CTA stages every row)
@@ -182,7 +231,7 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
       if (col < K) {
         float y[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = (v[c * 8 + j] - mean) * rstd * gam[col + j] + bet[col + j];
+        for (int j = 0; j < 8; ++j) y[j] = ln_apply(v[c * 8 + j], mean, rstd, gam[col + j], bet[col + j]);
         packed = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
         if (keep) {
           float* dst = a.x_out + (size_t)m * K + col;
@@ -195,68 +244,70 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
   }
 }
 
-// One LayerNorm'd row (IN_LN or IN_EMBED) staged by all NT threads of the CTA
-// (8 columns per thread and pass, block sums in warp order), for launches of
-// a single row: the whole block shares the row's loads instead of one warp.
+// Mean and 1/sqrt(var + eps) of one row whose column groups are spread over
+// the NT threads of the block (thread t holds groups t + NT*c in v), in the
+// fixed order above.  red: shared memory for KCH*32 floats + 2.
+template <int KCH, int NT>
+__device__ __forceinline__ float2 block_ln_stats(const float* v, int K, float* red) {
+  constexpr int kG = (KCH * 32 + NT - 1) / NT;  // groups per thread
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+#pragma unroll
+  for (int c = 0; c < kG; ++c) {
+    const int g = t + NT * c;
+    if (g < KCH * 32 && g * 8 < K) red[g] = group_sum8(v + c * 8);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float p = 0.f;
+#pragma unroll
+    for (int c = 0; c < KCH; ++c)
+      if ((lane + 32 * c) * 8 < K) p += red[lane + 32 * c];
+    p = warp_sum(p);
+    if (lane == 0) red[KCH * 32] = p / (float)K;
+  }
+  __syncthreads();
+  const float mean = red[KCH * 32];
+#pragma unroll
+  for (int c = 0; c < kG; ++c) {
+    const int g = t + NT * c;
+    if (g < KCH * 32 && g * 8 < K) red[g] = group_sq8(v + c * 8, mean);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float p = 0.f;
+#pragma unroll
+    for (int c = 0; c < KCH; ++c)
+      if ((lane + 32 * c) * 8 < K) p += red[lane + 32 * c];
+    p = warp_sum(p);
+    if (lane == 0) red[KCH * 32 + 1] = rsqrtf(p / (float)K + kLnEps);
+  }
+  __syncthreads();
+  return make_float2(mean, red[KCH * 32 + 1]);
+}
+
+// One LayerNorm'd row (IN_LN, IN_EMBED or IN_ACC) staged by all NT threads of
+// the CTA (8 columns per thread and pass), for launches of a single row: the
+// whole block shares the row's loads instead of one warp.  `keep`: this CTA
+// writes the float32 row to x_out.
 template <int KCH, int IN, int NT = 128>
 __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, int m, const float* gam,
-                                                   const float* bet) {
+                                                   const float* bet, bool keep) {
   constexpr int kG = (KCH * 32 + NT - 1) / NT;  // 8-column groups per thread
-  constexpr int kW = NT / 32;
-  __shared__ float ln_red[2][kW];
-  const int K = a.K, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const float* src0 = IN == IN_EMBED ? a.tok_emb + (size_t)row_token(a.rm, a.st, m) * K : a.r + (size_t)m * K;
-  const float* src1 = IN == IN_EMBED ? a.pos_emb + (size_t)(row_pos(a.rm, a.st, m) + 2) * K : nullptr;  // POSITION_OFFSET
+  __shared__ float ln_red[KCH * 32 + 2];
+  const int K = a.K, t = threadIdx.x;
   float v[kG * 8];
-  float sum = 0.f;
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
     const int col = (t + NT * c) * 8;
     if (col < K) {
-      float4 p0 = *reinterpret_cast<const float4*>(src0 + col);
-      float4 p1 = *reinterpret_cast<const float4*>(src0 + col + 4);
-      if constexpr (IN == IN_EMBED) {
-        const float4 q0 = *reinterpret_cast<const float4*>(src1 + col);
-        const float4 q1 = *reinterpret_cast<const float4*>(src1 + col + 4);
-        p0.x += q0.x; p0.y += q0.y; p0.z += q0.z; p0.w += q0.w;
-        p1.x += q1.x; p1.y += q1.y; p1.z += q1.z; p1.w += q1.w;
-      }
-      v[c * 8 + 0] = p0.x; v[c * 8 + 1] = p0.y; v[c * 8 + 2] = p0.z; v[c * 8 + 3] = p0.w;
-      v[c * 8 + 4] = p1.x; v[c * 8 + 5] = p1.y; v[c * 8 + 6] = p1.z; v[c * 8 + 7] = p1.w;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sum += v[c * 8 + j];
+      ln_inputs8<IN>(a, m, col, v + c * 8);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[c * 8 + j] = 0.f;
     }
   }
-  sum = warp_sum(sum);
-  if (lane == 0) ln_red[0][warp] = sum;
-  __syncthreads();
-  float mean = 0.f;
-#pragma unroll
-  for (int w = 0; w < kW; ++w) mean += ln_red[0][w];
-  mean /= (float)K;
-  float sq = 0.f;
-#pragma unroll
-  for (int c = 0; c < kG; ++c) {
-    if ((t + NT * c) * 8 < K) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float d = v[c * 8 + j] - mean;
-        sq = fmaf(d, d, sq);
-      }
-    }
-  }
-  sq = warp_sum(sq);
-  if (lane == 0) ln_red[1][warp] = sq;
-  __syncthreads();
-  float var = 0.f;
-#pragma unroll
-  for (int w = 0; w < kW; ++w) var += ln_red[1][w];
-  const float rstd = rsqrtf(var / (float)K + kLnEps);
-  // x_out is written once per row, by CTA m % gridDim.x
-  const bool keep = a.x_out != nullptr && (m % gridDim.x) == blockIdx.x;
+  const float2 st = block_ln_stats<KCH, NT>(v, K, ln_red);
+  keep = keep && a.x_out != nullptr;
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
     const int col = (t + NT * c) * 8;
@@ -265,7 +316,7 @@ __device__ __forceinline__ void stage_ln_row_block(const ProjArgs& a, bf16* xs, 
       if (col < K) {
         float y[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = (v[c * 8 + j] - mean) * rstd * gam[col + j] + bet[col + j];
+        for (int j = 0; j < 8; ++j) y[j] = ln_apply(v[c * 8 + j], st.x, st.y, gam[col + j], bet[col + j]);
         packed = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
         if (keep) {
           float* dst = a.x_out + (size_t)m * K + col;
@@ -291,7 +342,7 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
   constexpr int kWarps = NT / 32;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int KP = KCH * 256;
-  constexpr bool kLn = IN == IN_LN || IN == IN_EMBED;
+  constexpr bool kLn = ln_input<IN>();
   bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MC][KP]
   float* sgamma = reinterpret_cast<float*>(smem_raw + (size_t)MC * KP * sizeof(bf16));  // [KP] (LayerNorm inputs)
   float* sbeta = sgamma + KP;
@@ -318,6 +369,9 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
   const float bias_first = first < a.N ? __bfloat162float(a.bias[first]) : 0.f;
   pdl_launch_dependents();
   pdl_wait();
+  if (a.zero) {  // the launch before this one has read the accumulator
+    for (int i = blockIdx.x * NT + threadIdx.x; i < a.zero_n; i += gridDim.x * NT) a.zero[i] = 0ull;
+  }
   // the residual input of this warp's first row, requested before the staging
   float xres_first = 0.f;
   if constexpr (EPI == EPI_RESID) {
@@ -328,9 +382,9 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
   for (int m0 = 0; m0 < a.M; m0 += MC) {
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
-    if constexpr ((IN == IN_LN || IN == IN_EMBED) && MC == 1) {
-      stage_ln_row_block<KCH, IN, NT>(a, xs, m0, sgamma, sbeta);
-    } else if constexpr (IN == IN_LN || IN == IN_EMBED) {
+    if constexpr (kLn && MC == 1) {
+      stage_ln_row_block<KCH, IN, NT>(a, xs, m0, sgamma, sbeta, (m0 % gridDim.x) == blockIdx.x);
+    } else if constexpr (kLn) {
       stage_ln_rows<KCH, IN>(a, xs, m0, mc, warp, lane, 4, false, sgamma, sbeta);
     } else {
       if constexpr (IN == IN_BF16 && MC == 1) {
@@ -364,7 +418,7 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
         *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = packed;
       }
     }
-    if constexpr (IN == IN_LN || IN == IN_EMBED) {
+    if constexpr (kLn) {
       // rows mc..MC-1 of the last chunk are not staged: zero them
       for (int idx = threadIdx.x; idx < (MC - mc) * (KP / 8); idx += blockDim.x) {
         const int i = mc + idx / (KP / 8), col = (idx % (KP / 8)) * 8;

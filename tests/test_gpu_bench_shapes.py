@@ -122,3 +122,27 @@ def test_single_song_long_rows_vs_oracle_bf16():
     for e in (eng, ora):
         loader(e, WIDE.width, 1500)(0, 801, prefix, None, 1500, 10_000)
     check("batch 1, 5050 positions", forced_compare(eng, ora, [0], 8, rng, WIDE.vocab_size))
+
+
+@pytest.mark.parametrize("batch", [1, 16], ids=["cuda-core", "tensor-core"])
+def test_wide_prefill_equals_token_by_token(batch):
+    """At the benchmark's width (d1024, K up to 4096) a 150-token prefix prefilled in chunks gives
+    bit-identical logits to forcing it one token at a time: every LayerNorm normalises in one fixed
+    order whatever kernel stages it, and the out-projection sums do not depend on arrival order."""
+
+    rng = np.random.default_rng(11)
+    seq = [SOS, OUT] + rng.integers(4, WIDE.vocab_size, 160).tolist()
+    a = cuda_engine(WIDE, SEED, grammar(), batch, 1500)
+    b = cuda_engine(WIDE, SEED, grammar(), batch, 1500)
+    slot = batch - 1
+    loader(a, WIDE.width, 1500)(slot, 3, seq[:152], None, 1200, 10_000)
+    loader(b, WIDE.width, 1500)(slot, 3, seq[:2], None, 1200, 10_000)
+    forced = np.full(batch, -1, np.int64)
+    for k in range(150):
+        forced[slot] = seq[2 + k]
+        b.step_debug(forced, want_logits=False)
+    for k in range(8):
+        forced[slot] = seq[152 + k]
+        la, ga = a.step_debug(forced)
+        lb, gb = b.step_debug(forced)
+        assert np.array_equal(la[slot], lb[slot]) and ga[slot] == gb[slot], k
