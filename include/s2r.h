@@ -212,6 +212,36 @@ int32_t s2r_poll_finished(s2r_ctx* ctx, uint8_t* finished, void* stream);
 int32_t s2r_take(s2r_ctx* ctx, int32_t slot, int64_t* tokens, int32_t capacity, int32_t* length,
                  int32_t* ended, void* stream);
 
+/* Asynchronous poll: enqueue on `stream`, behind the work already there, a
+ * copy of every slot's finished flag (and of the device error word) to host
+ * memory the engine owns, and return at once.  The host can queue more steps
+ * before it reads the flags with s2r_poll_finished_ready, so the GPU keeps
+ * decoding while a scheduler looks at finished slots.  No counterpart in the
+ * reference, whose BatchDecoder.finished synchronises the device
+ * (engine.py:248-252) after every transcribe_many poll (transcribe.py:360-361). */
+int32_t s2r_poll_finished_async(s2r_ctx* ctx, void* stream);
+
+/* The flags of the last s2r_poll_finished_async: `*ready` = 1 and
+ * `finished` [batch] filled once its copy has landed, else `*ready` = 0 (with
+ * `wait` = 0 it never blocks; with `wait` != 0 it waits for that copy only,
+ * not for the steps queued after it).  Fails with S2R_ESTATE without a
+ * pending poll, and with S2R_EDEVICE if a kernel had reported an error. */
+int32_t s2r_poll_finished_ready(s2r_ctx* ctx, uint8_t* finished, int32_t wait, int32_t* ready);
+
+/* Asynchronous take: enqueue on `stream` the copy of slot's tokens, position
+ * and end reason to host memory the engine owns, and free the slot at once
+ * (its K/V pages return to the pool; a load of the slot queued after the copy
+ * on the same stream is ordered behind it).  The tokens are read with
+ * s2r_take_ready.  Replaces BatchDecoder.take (engine.py:254-262) for
+ * schedulers that do not wait for the device. */
+int32_t s2r_take_async(s2r_ctx* ctx, int32_t slot, void* stream);
+
+/* The result of slot's s2r_take_async: as s2r_take (tokens ending in EOS,
+ * end reason), with `*ready` = 0 while the copy has not landed (`wait` as in
+ * s2r_poll_finished_ready).  S2R_ESTATE if the slot has no unread take. */
+int32_t s2r_take_ready(s2r_ctx* ctx, int32_t slot, int64_t* tokens, int32_t capacity, int32_t* length,
+                       int32_t* ended, int32_t wait, int32_t* ready);
+
 /* Device address, element count and dtype code (0 f32, 1 bf16, 2 i64, 3 u8,
  * 4 f64, 5 i32) of a named engine buffer, for zero-copy views: "token",
  * "position", "finished", "ended", "in_shift", "shift_run", "payload",

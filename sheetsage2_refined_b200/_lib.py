@@ -101,6 +101,11 @@ SIGNATURES = {
     "s2r_profile_step": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "s2r_step_launches": (C.c_int32, [C.c_void_p]),
     "s2r_free_pages": (C.c_int32, [C.c_void_p]),
+    "s2r_poll_finished_async": (C.c_int32, [C.c_void_p, C.c_void_p]),
+    "s2r_poll_finished_ready": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
+    "s2r_take_async": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p]),
+    "s2r_take_ready": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(C.c_int64), C.c_int32, C.POINTER(C.c_int32),
+                                   C.POINTER(C.c_int32), C.c_int32, C.POINTER(C.c_int32)]),
     "s2r_masked_argmax_noalloc": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                               C.c_void_p]),
 }

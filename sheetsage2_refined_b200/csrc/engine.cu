@@ -148,6 +148,16 @@ struct s2r_ctx {
   cudaGraphExec_t graph = nullptr;
   bool graph_dirty = true;
   cudaStream_t cap_stream = nullptr;
+  // asynchronous polls and takes (pinned host copies, allocated on first use)
+  uint8_t* h_fin = nullptr;      // [B] finished flags of the last asynchronous poll
+  int* h_err = nullptr;          // the device error word read with them
+  cudaEvent_t poll_ev = nullptr;  // the poll's copies have landed
+  cudaStream_t poll_stream = nullptr;
+  bool poll_pending = false;
+  int64_t* h_out = nullptr;      // [B][T] tokens of asynchronous takes
+  int64_t* h_pos_end = nullptr;  // [B][2] position and end reason of each
+  std::vector<cudaEvent_t> take_ev;
+  std::vector<uint8_t> take_pending;
   // persistent step kernel (live rows <= 8)
   bool persistent = false;
   int nclusters = 0, chunk_cap = 0, stages = 0;
@@ -1276,6 +1286,12 @@ int32_t s2r_destroy(s2r_ctx* c) {
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   if (c->order_copied) cudaEventDestroy(c->order_copied);
   if (c->h_order) cudaFreeHost(c->h_order);
+  if (c->poll_ev) cudaEventDestroy(c->poll_ev);
+  for (cudaEvent_t e : c->take_ev) cudaEventDestroy(e);
+  if (c->h_fin) cudaFreeHost(c->h_fin);
+  if (c->h_err) cudaFreeHost(c->h_err);
+  if (c->h_out) cudaFreeHost(c->h_out);
+  if (c->h_pos_end) cudaFreeHost(c->h_pos_end);
   for (void* p : c->allocs) cudaFree(p);
   delete c;
   return S2R_OK;
@@ -1569,6 +1585,98 @@ int32_t s2r_take(s2r_ctx* c, int32_t slot, int64_t* tokens, int32_t capacity, in
   *ended = (int32_t)end;
   c->loaded[slot] = 0;
   release_pages(c, slot);
+  return S2R_OK;
+}
+
+// Pinned host buffers and events of the asynchronous polls and takes.
+static int setup_async(s2r_ctx* c) {
+  if (c->h_fin) return S2R_OK;
+  CK(cudaMallocHost(&c->h_fin, c->B));
+  CK(cudaMallocHost(&c->h_err, sizeof(int)));
+  CK(cudaMallocHost(&c->h_out, (size_t)c->B * c->T * sizeof(int64_t)));
+  CK(cudaMallocHost(&c->h_pos_end, (size_t)c->B * 2 * sizeof(int64_t)));
+  CK(cudaEventCreateWithFlags(&c->poll_ev, cudaEventDisableTiming));
+  c->take_ev.assign(c->B, nullptr);
+  for (int b = 0; b < c->B; ++b) CK(cudaEventCreateWithFlags(&c->take_ev[b], cudaEventDisableTiming));
+  c->take_pending.assign(c->B, 0);
+  return S2R_OK;
+}
+
+int32_t s2r_poll_finished_async(s2r_ctx* c, void* stream) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  CK(cudaSetDevice(c->device));
+  TRY(setup_async(c));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaMemcpyAsync(c->h_fin, c->st.finished, c->B, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(c->h_err, c->dev_error, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(c->poll_ev, s));
+  c->poll_stream = s;
+  c->poll_pending = true;
+  return S2R_OK;
+}
+
+int32_t s2r_poll_finished_ready(s2r_ctx* c, uint8_t* finished, int32_t wait, int32_t* ready) {
+  if (!c || !finished || !ready) return fail(S2R_EINVAL, "NULL argument");
+  if (!c->poll_pending) return fail(S2R_ESTATE, "no asynchronous poll was requested (s2r_poll_finished_async)");
+  CK(cudaSetDevice(c->device));
+  *ready = 0;
+  cudaError_t q = wait ? cudaEventSynchronize(c->poll_ev) : cudaEventQuery(c->poll_ev);
+  if (q == cudaErrorNotReady) {
+    (void)cudaGetLastError();  // not an error: the copy is still queued
+    return S2R_OK;
+  }
+  CK(q);
+  c->poll_pending = false;
+  std::memcpy(finished, c->h_fin, c->B);
+  *ready = 1;
+  if (*c->h_err != 0) return check_device_error(c, c->poll_stream);
+  return S2R_OK;
+}
+
+int32_t s2r_take_async(s2r_ctx* c, int32_t slot, void* stream) {
+  if (!c) return fail(S2R_EINVAL, "NULL engine");
+  if (slot < 0 || slot >= c->B) return fail(S2R_EINVAL, "slot %d out of range [0, %d)", slot, c->B);
+  if (!c->loaded[slot]) return fail(S2R_ESTATE, "slot %d is not loaded", slot);
+  CK(cudaSetDevice(c->device));
+  TRY(setup_async(c));
+  if (c->take_pending[slot]) return fail(S2R_ESTATE, "slot %d has an asynchronous take whose tokens were not read", slot);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int64_t* dst = c->h_out + (size_t)slot * c->T;
+  CK(cudaMemcpyAsync(dst, c->st.out + (size_t)slot * c->T, (size_t)c->T * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(c->h_pos_end + 2 * slot, c->st.position + slot, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(c->h_pos_end + 2 * slot + 1, c->st.ended + slot, 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(c->take_ev[slot], s));
+  // the slot is free for the work queued after the copies (a load on the same stream)
+  c->take_pending[slot] = 1;
+  c->loaded[slot] = 0;
+  release_pages(c, slot);
+  return S2R_OK;
+}
+
+int32_t s2r_take_ready(s2r_ctx* c, int32_t slot, int64_t* tokens, int32_t capacity, int32_t* length, int32_t* ended,
+                       int32_t wait, int32_t* ready) {
+  if (!c || !length || !ended || !ready) return fail(S2R_EINVAL, "NULL argument");
+  if (slot < 0 || slot >= c->B) return fail(S2R_EINVAL, "slot %d out of range [0, %d)", slot, c->B);
+  if (c->take_pending.empty() || !c->take_pending[slot])
+    return fail(S2R_ESTATE, "slot %d has no asynchronous take (s2r_take_async)", slot);
+  CK(cudaSetDevice(c->device));
+  *ready = 0;
+  cudaError_t q = wait ? cudaEventSynchronize(c->take_ev[slot]) : cudaEventQuery(c->take_ev[slot]);
+  if (q == cudaErrorNotReady) {
+    (void)cudaGetLastError();
+    return S2R_OK;
+  }
+  CK(q);
+  const int64_t* row = c->h_out + (size_t)slot * c->T;
+  const int n = (int)c->h_pos_end[2 * slot] + 1;
+  const int total = n + (row[n - 1] != 2 ? 1 : 0);  // always ends in <eos> (engine.py:259-260)
+  *length = total;
+  *ready = 1;
+  if (!tokens || capacity < total) return fail(S2R_EINVAL, "capacity %d < %d tokens", capacity, total);
+  std::memcpy(tokens, row, (size_t)n * sizeof(int64_t));
+  if (total > n) tokens[n] = 2;
+  *ended = (int32_t)c->h_pos_end[2 * slot + 1];
+  c->take_pending[slot] = 0;
   return S2R_OK;
 }
 

@@ -348,6 +348,51 @@ class BatchDecoder:
         self.loaded[slot] = False
         return list(buf[: length.value]), ENDED[ended.value]
 
+    # ------------------------------------------------- asynchronous polling
+    def finished_async(self) -> None:
+        """Queue a copy of the finished flags behind the steps already queued; returns at once.
+
+        ``finished_ready`` reads it.  A scheduler can queue the next steps in
+        between, so the device never waits for the host's poll (the
+        reference's ``finished`` synchronises, engine.py:248-252).
+        """
+
+        _lib.check(self._lib.s2r_poll_finished_async(self._ctx, self._stream()))
+
+    def finished_ready(self, wait: bool = False) -> list[int] | None:
+        """Loaded slots finished as of the last ``finished_async``, or None while its copy is queued.
+
+        With ``wait`` it blocks until that copy lands (not for later steps).
+        """
+
+        done = np.zeros(self.batch, np.uint8)
+        ready = C.c_int32()
+        _lib.check(self._lib.s2r_poll_finished_ready(self._ctx, done.ctypes.data, int(wait), C.byref(ready)))
+        if not ready.value:
+            return None
+        return [slot for slot in range(self.batch) if self.loaded[slot] and done[slot]]
+
+    def take_async(self, slot: int) -> None:
+        """Queue the copy of a slot's tokens and free the slot at once (``take_ready`` reads them).
+
+        A ``load`` of the slot issued afterwards on the same stream runs after the copy.
+        """
+
+        _lib.check(self._lib.s2r_take_async(self._ctx, slot, self._stream()))
+        self.loaded[slot] = False
+
+    def take_ready(self, slot: int, wait: bool = False) -> tuple[list[int], str] | None:
+        """The ``(tokens, ended)`` of the slot's ``take_async``, or None while its copy is queued."""
+
+        cap = self.max_tokens + 1
+        buf = (C.c_int64 * cap)()
+        length, ended, ready = C.c_int32(), C.c_int32(), C.c_int32()
+        _lib.check(self._lib.s2r_take_ready(self._ctx, slot, buf, cap, C.byref(length), C.byref(ended), int(wait),
+                                            C.byref(ready)))
+        if not ready.value:
+            return None
+        return list(buf[: length.value]), ENDED[ended.value]
+
     # ------------------------------------------------------------ extras
     @property
     def step_launches(self) -> int:

@@ -101,13 +101,24 @@ class DecodeStats:
         return max(0.0, self.polls[-1][0] - self.drained_at)
 
 
-def decode_songs(engine, songs: dict, poll_every: int = 32, stats: DecodeStats | None = None) -> dict:
+def decode_songs(engine, songs: dict, poll_every: int = 32, stats: DecodeStats | None = None,
+                 overlap: bool = False) -> dict:
     """Decode ``songs`` (``{key: Song}``, in queue order) on ``engine``; returns ``{key: (tokens, ended)}``.
 
     Continuous batching as the reference scheduler does it: fill every free
     slot, run ``poll_every`` steps, take the finished slots (one device read per
     poll, ``finished``), refill them, until every song has ended.
+
+    ``overlap`` (engines with ``finished_async``): the host never waits for the
+    device to drain.  The next ``poll_every`` steps are queued before the
+    flags of the previous ones are read, finished slots are taken
+    asynchronously and refilled behind the steps in flight.  A window's
+    tokens do not depend on which slot it runs in or when it starts, so the
+    results equal the synchronous loop's.
     """
+
+    if overlap and hasattr(engine, "finished_async"):
+        return _decode_songs_overlapped(engine, songs, poll_every, stats)
 
     queue = list(songs)
     live: dict[int, Any] = {}
@@ -139,6 +150,60 @@ def decode_songs(engine, songs: dict, poll_every: int = 32, stats: DecodeStats |
         for slot in done:
             results[live.pop(slot)] = engine.take(slot)
         refill()
+    return results
+
+
+def _decode_songs_overlapped(engine, songs: dict, poll_every: int, stats: DecodeStats | None) -> dict:
+    queue = list(songs)
+    live: dict[int, Any] = {}
+    pending: dict[int, Any] = {}  # slot -> key of an asynchronous take not yet read
+    results: dict = {}
+    t0 = time.perf_counter()
+
+    def collect(wait=False):
+        for slot in list(pending):
+            got = engine.take_ready(slot, wait=wait)
+            if got is not None:
+                results[pending.pop(slot)] = got
+
+    def refill():
+        for slot in engine.free_slots():
+            if not queue:
+                break
+            if slot in pending:  # its tokens must be read before the slot's next take
+                results[pending.pop(slot)] = engine.take_ready(slot, wait=True)
+            key = queue.pop(0)
+            song = songs[key]
+            kwargs = {"frame_logp": song.frame_logp} if song.frame_logp is not None else {}
+            if song.target is not None:
+                kwargs["target"] = song.target
+            engine.load(slot, song.memory, list(song.prefix), song.stop_seconds, song.frames, **kwargs)
+            live[slot] = key
+            if stats is not None:
+                stats.loads += 1
+        if stats is not None and not queue and stats.drained_at is None:
+            stats.drained_at = time.perf_counter() - t0
+
+    refill()
+    engine.run(poll_every)
+    engine.finished_async()
+    snapshot = dict(live)  # the window of every slot when the poll was queued
+    while live:
+        engine.run(poll_every)
+        done = engine.finished_ready(wait=True)
+        polled, snapshot = snapshot, dict(live)
+        engine.finished_async()
+        if stats is not None:
+            stats.polls.append((time.perf_counter() - t0, len(live)))
+        for slot in done:
+            # a slot refilled after the poll was queued still shows its old window's flag
+            if slot in live and polled.get(slot) == live[slot]:
+                engine.take_async(slot)
+                pending[slot] = live.pop(slot)
+        refill()
+        collect()
+    engine.finished_ready(wait=True)  # the last queued poll
+    collect(wait=True)
     return results
 
 

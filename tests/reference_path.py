@@ -117,3 +117,51 @@ def set_target(engine, slot: int, target: int | None) -> None:
 
     if target is not None:
         engine.state["target"][slot] = target
+
+
+def tiny_sheetsage(ref, seed: int = 0, decoder_seed: int = 5):
+    """A small random-init ``SheetSage`` (model.py:18-51) with the real 32,576-token vocabulary.
+
+    The encoder keeps the reference's structure (mel front end, three
+    ConvNeXt stages with strides 1-2-2, Conformer blocks; 960 samples per
+    frame) at width 128 with two blocks; its mel filterbank buffer gets seeded
+    positive values so that the memory varies over time.  The decoder (2
+    layers, width 128, 2 heads, FFN 256) takes this repository's seeded
+    synthetic weights, with the token-embedding rows of the shift tokens
+    scaled by 4: the reference's ``Vocab.decode`` (vocab.py:322-349) rejects a
+    window whose first event has no subbeat shift, which the grammar allows
+    but a trained decoder never emits, so untrained weights must prefer
+    shifts.  Windows are encoded at their own length (``pad_encoder = False``,
+    as for the fine-tuned decoders).
+    """
+
+    from sheetsage2_refined_b200.weights import DecoderConfig, synthetic_state_dict
+
+    torch.manual_seed(seed)
+    enc = ref.encoder.EncoderConfig(n_mels=32, stage_channels=(32, 64, 128), stage_depths=(1, 1, 1), width=128,
+                                    ffn_width=256, layers=2, heads=2, conv_kernel=7)
+    vocab_size = ref.vocab.Vocab().size
+    config = DecoderConfig(vocab_size=vocab_size, width=128, layers=2, heads=2, ffn_width=256, max_tokens=5120)
+    dc = ref.decoder.DecoderConfig(vocab_size=vocab_size, width=128, layers=2, heads=2, ffn_width=256, max_tokens=5120)
+    model = ref.model.SheetSage(enc, dc)
+    with torch.no_grad():
+        fb = model.encoder.frontend.mel_fb
+        fb.copy_(torch.rand(fb.shape, generator=torch.Generator().manual_seed(seed + 1)) * 1e-3)
+        state = {k: torch.from_numpy(v) for k, v in synthetic_state_dict(config, decoder_seed).items()}
+        model.decoder.load_state_dict(state, strict=True)
+        vocab = ref.vocab.Vocab()
+        model.decoder.token_embedding.weight[vocab.start["shift"]:vocab.end["shift"]] *= 4.0
+    model.pad_encoder = False
+    return model.eval()
+
+
+def seeded_waveforms(seconds, seed: int = 0, rate: int = 24_000):
+    """Seeded noise bursts as mono 24 kHz waveforms, one per length in ``seconds``."""
+
+    gen = torch.Generator().manual_seed(seed)
+    out = []
+    for s in seconds:
+        n = int(s * rate)
+        env = (torch.sin(torch.arange(n) * (2 * np.pi * 2.0 / rate)) > 0).float()  # 2 Hz on/off
+        out.append((torch.randn(n, generator=gen) * 0.1 * (0.2 + env)).float())
+    return out

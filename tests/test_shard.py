@@ -184,3 +184,40 @@ def test_two_rank_box_job_over_gloo():
     assert sorted(merged) == list(range(len(targets)))
     for i, (tokens, ended) in merged.items():
         assert tokens == [1, 3] + [1000 + i] * targets[i] + [2]
+
+
+class FakeAsyncEngine(FakeEngine):
+    """FakeEngine with the asynchronous poll and take: a poll reports the flags as they were when
+    it was queued, and a take frees the slot at once."""
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        self.polled = None
+        self.taken = {}
+
+    def finished_async(self):
+        self.polled = self.finished()
+
+    def finished_ready(self, wait=False):
+        done, self.polled = self.polled, None
+        return [s for s in done if self.loaded[s] is not None]
+
+    def take_async(self, slot):
+        self.taken[slot] = self.take(slot)
+
+    def take_ready(self, slot, wait=False):
+        return self.taken.pop(slot)
+
+
+def test_overlapped_decode_songs_matches_the_synchronous_loop():
+    from sheetsage2_refined_b200.shard import DecodeStats, Song, decode_songs
+
+    import numpy as np
+
+    rng = np.random.default_rng(6)
+    targets = rng.integers(5, 150, 41).tolist()
+    songs = {i: Song(memory=1000 + i, prefix=[1, 3], target=t) for i, t in enumerate(targets)}
+    sync = decode_songs(FakeEngine(6), songs, poll_every=8)
+    stats = DecodeStats()
+    over = decode_songs(FakeAsyncEngine(6), songs, poll_every=8, stats=stats, overlap=True)
+    assert over == sync and sorted(over) == list(range(41)) and stats.loads == 41
