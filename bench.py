@@ -757,7 +757,10 @@ class RealBatched(Batched):
         return real_config(world, BATCH, "64 slots with refill, real frames U[3000, 7500]")
 
     def _window(self):
-        return int(self.rng.integers(3000, REAL_FRAMES + 1)), int(self.rng.integers(512, 4097))
+        frames, length = int(self.rng.integers(3000, REAL_FRAMES + 1)), int(self.rng.integers(512, 4097))
+        if self.k < BATCH:  # the first windows start part-way through, as in a batch that has been running
+            length = max(16, int(length * self.rng.random()))
+        return frames, length
 
     def _load(self, slot, frames, target, mem):
         tables = (self.tables_pinned if mem.device.type == "cpu" else self.tables)[self.k % 2]

@@ -67,6 +67,8 @@ struct AttnArgs {
   const bf16* wq;  // [D, D]
   const bf16* bq;  // [D]
   int fuse_q;
+  unsigned long long* zero;  // cleared after the wait (an accumulator the launch before has read)
+  int zero_n;
 };
 
 constexpr int kAttnOutPrefetch = 4;  // out-projection passes (32 features each) loaded before the wait
@@ -75,7 +77,6 @@ constexpr int kErrAttnCluster = 1;  // launched without the expected cluster sha
 constexpr int kErrAttnChunk = 2;    // a row's keys do not fit the score buffer
 constexpr int kErrAttnStage = 5;    // a bulk copy into shared memory did not complete in time
 constexpr int kErrAttnExchange = 6; // a value from a peer CTA did not arrive in time
-constexpr int kErrAccRange = 7;     // an out-projection partial too large (or NaN) for the fixed-point sum
 
 // How a CTA gets its keys and values ahead of the PDL wait.
 constexpr int kAttnPreNone = 0;   // read in the loops (batched engines, which keep occupancy)
@@ -275,6 +276,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   // just before that store).
   cluster_arrive_relaxed();
   pdl_wait();
+  if (a.zero) {
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    for (int i = cta * kAttnThreads + tid; i < a.zero_n; i += gridDim.x * gridDim.y * gridDim.z * kAttnThreads)
+      a.zero[i] = 0ull;
+  }
 
   const uint4 qraw = fuse_q ? make_uint4(0, 0, 0, 0)
                             : *reinterpret_cast<const uint4*>(a.q + (size_t)m * a.ldq + h * kHeadDim + sub * 8);

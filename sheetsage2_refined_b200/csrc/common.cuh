@@ -71,6 +71,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // schedule-invariant) and is exact up to the one rounding per partial.
 // Partials must stay below 2^26 in magnitude (|total| < 2^31 for up to 32
 // of them); a larger or NaN partial is not added and reported by the caller.
+constexpr int kErrAccRange = 7;             // device error word: a partial out of the fixed-point range
 constexpr float kAccScale = 4294967296.0f;  // 2^32
 constexpr float kAccLimit = 67108864.0f;    // 2^26
 

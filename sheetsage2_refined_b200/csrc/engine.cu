@@ -25,6 +25,7 @@
 
 #include "../../include/s2r.h"
 #include "attention.cuh"
+#include "ffn.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.h"
@@ -100,6 +101,7 @@ struct LayerBufs {
   float *ln_self_g, *ln_self_b, *ln_cross_g, *ln_cross_b, *ln_final_g, *ln_final_b;
   bf16 *kpool, *vpool, *ck, *cv;
   bf16 *wo_hb, *wco_hb;  // out-projections by head for the persistent step kernel
+  bf16* w2s;             // fc2 weight slice-major [FFN/32][D][32] for the fused FFN of one-slot engines
 };
 
 struct s2r_ctx {
@@ -174,7 +176,10 @@ struct s2r_ctx {
   bool fuse_out = false;
   unsigned long long* acc_self = nullptr;   // [maxM][D]
   unsigned long long* acc_cross = nullptr;  // [maxM][D]
+  unsigned long long* acc_ffn = nullptr;    // [maxM][D] fc2 sums (EPI_SLICES), read by the next LayerNorm
   float* x_b = nullptr;                     // [maxM][D] the cross attention's residual input
+  float* x_c = nullptr;                     // [maxM][D] the FFN's residual input
+  bool fuse_ffn = false;                    // one-slot engines: decode steps run the FFN as one kernel
   int attn_splits = 8;             // CTAs (one cluster) per (row, head) of the self-attention
   int attn_splits_cross = 8;       // ... and of the cross-attention
   int32_t *order_self = nullptr, *order_cross = nullptr;  // [B] decode rows, longest first (tensor-core engines)
@@ -260,6 +265,18 @@ __global__ void head_block_kernel(const bf16* __restrict__ in, bf16* __restrict_
   }
 }
 
+// out[s][n][j] = in[n][32s + j] for the [D, FFN] fc2 weight: each 32-column
+// slice of every row made contiguous for the fused FFN kernel.
+__global__ void slice_major_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int D, int FFN) {
+  const size_t total = (size_t)D * FFN;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % kSliceCols);
+    const size_t rest = i / kSliceCols;
+    const int n = (int)(rest % D), sl = (int)(rest / D);
+    out[i] = in[(size_t)n * FFN + sl * kSliceCols + j];
+  }
+}
+
 int head_block_bf16(const bf16* in, bf16* out, int D) {
   head_block_kernel<<<1024, 256>>>(in, out, D);
   CK(cudaGetLastError());
@@ -295,6 +312,7 @@ bool next_pdl(s2r_ctx* c) {
 
 ProjArgs proj_base(s2r_ctx* c) {
   ProjArgs a{};
+  a.err = c->dev_error;
   a.st = c->st;
   a.heads = c->H;
   a.pages_per_slot = c->pps;
@@ -514,6 +532,10 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
     a.D = c->D;
     a.wo = cross ? w.wco : w.wo;
     a.acc_out = cross ? c->acc_cross : c->acc_self;
+    if (cross && plan.fuse_q && c->fuse_ffn && !rm.prefill) {  // QKV has read acc_ffn; the fused FFN adds into it
+      a.zero = c->acc_ffn;
+      a.zero_n = M * c->D;
+    }
     if (plan.fuse_q) {  // the cross attention's input: self_attn_norm(x + bf16(self out-projection))
       a.acc_in = c->acc_self;
       a.bias_in = w.bo;
@@ -550,11 +572,20 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     a.M = M;
     a.K = D;
     a.N = 3 * D;
+    int in = IN_LN;
     if (l == 0) {
+      in = IN_EMBED;
       a.tok_emb = c->tok_emb;
       a.pos_emb = c->pos_emb;
       a.gamma = c->emb_ln_g;
       a.beta = c->emb_ln_b;
+    } else if (c->fuse_out) {  // final_norm(x + bf16(fc2 sums + b2)) of the layer before
+      in = IN_ACC;
+      a.r = c->x_c;
+      a.acc = c->acc_ffn;
+      a.acc_bias = c->layers[l - 1].b2;
+      a.gamma = c->layers[l - 1].ln_final_g;
+      a.beta = c->layers[l - 1].ln_final_b;
     } else {
       a.r = c->r;
       a.gamma = c->layers[l - 1].ln_final_g;
@@ -567,7 +598,11 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     a.ldo = D;
     a.k_dst = w.kpool;
     a.v_dst = w.vpool;
-    TRY(launch_proj(c, a, l == 0 ? IN_EMBED : IN_LN, EPI_QKV, s));
+    if (c->fuse_out) {  // the FFN before (or the last step's) has read acc_cross
+      a.zero = c->acc_cross;
+      a.zero_n = M * D;
+    }
+    TRY(launch_proj(c, a, in, EPI_QKV, s));
     TRY(mark(c, K_QKV, s));
   }
   if (last_kv_only) return S2R_OK;
@@ -592,11 +627,41 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
       a.bias = w.bcq;
       a.out = c->q;
       a.ldo = D;
+      if (c->fuse_ffn && !rm.prefill) {  // the QKV projection has read acc_ffn; the fused FFN adds into it
+        a.zero = c->acc_ffn;
+        a.zero_n = M * D;
+      }
       TRY(launch_proj(c, a, IN_ACC, EPI_BF16, s));
       TRY(mark(c, K_CROSS_Q, s));
     }
     TRY(launch_attn(c, rm, M, l, true, s));  // 5-6. cross-attention + out-projection
     TRY(mark(c, K_CROSS_ATTN, s));
+    if (c->fuse_ffn && !rm.prefill) {  // 7-8. cross_attn_norm, fc1, GELU and fc2 in one launch
+      FfnArgs f{};
+      f.D = D;
+      f.FFN = c->FFN;
+      f.m = 0;
+      f.x_in = c->x_b;
+      f.acc_in = c->acc_cross;
+      f.bias_in = w.bco;
+      f.ln_g = w.ln_cross_g;
+      f.ln_b = w.ln_cross_b;
+      f.x_out = c->x_c;
+      f.w1 = w.w1;
+      f.b1 = w.b1;
+      f.w2s = w.w2s;
+      f.acc_out = c->acc_ffn;
+      f.zero = c->acc_self;
+      f.zero_n = M * D;
+      f.err = c->dev_error;
+      const int kch = kch_for(D);
+      void (*fn)(const FfnArgs) = kch == 1 ? ffn_row_kernel<1> : kch == 2 ? ffn_row_kernel<2> : ffn_row_kernel<4>;
+      const size_t smem = ffn_smem_bytes(D);
+      CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      CK(launch_ex(fn, dim3(c->FFN / kFfnSlice), dim3(kFfnThreads), smem, s, next_pdl(c), 0, f));
+      TRY(mark(c, K_FC1, s));
+      return S2R_OK;
+    }
     {  // 7. cross_attn_norm -> fc1 + GELU; acc_self has been read
       ProjArgs a = proj_base(c);
       a.rm = rm;
@@ -608,7 +673,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
       a.acc_bias = w.bco;
       a.gamma = w.ln_cross_g;
       a.beta = w.ln_cross_b;
-      a.x_out = c->x;
+      a.x_out = c->x_c;
       a.W = w.w1;
       a.bias = w.b1;
       a.out = c->hid;
@@ -688,7 +753,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     TRY(mark(c, K_FC1, s));
   }
   }
-  {  // 8. fc2 + residual; acc_cross has been read
+  {  // 8. fc2 (+ residual); acc_cross has been read
     ProjArgs a = proj_base(c);
     a.rm = rm;
     a.M = M;
@@ -698,13 +763,16 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     a.ldx = c->FFN;
     a.W = w.w2;
     a.bias = w.b2;
-    a.r_out = c->r;
-    a.x_res = c->x;
-    if (c->fuse_out) {
+    if (c->fuse_out) {  // fixed-point sums; the next LayerNorm adds bias and residual (IN_ACC)
+      a.acc_out = c->acc_ffn;
       a.zero = c->acc_cross;
       a.zero_n = M * D;
+      TRY(launch_proj(c, a, IN_BF16, EPI_SLICES, s));
+    } else {
+      a.r_out = c->r;
+      a.x_res = c->x;
+      TRY(launch_proj(c, a, IN_BF16, EPI_RESID, s));
     }
-    TRY(launch_proj(c, a, IN_BF16, EPI_RESID, s));
     TRY(mark(c, K_FC2, s));
   }
   return S2R_OK;
@@ -817,6 +885,11 @@ int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logit
   a.st = c->st;
   a.gr = c->gr;
   a.r = c->r;
+  if (c->fuse_out) {  // final_norm(x + bf16(fc2 sums + b2))
+    a.r = c->x_c;
+    a.acc = c->acc_ffn;
+    a.acc_bias = c->layers[c->L - 1].b2;
+  }
   a.gamma = c->layers[c->L - 1].ln_final_g;
   a.beta = c->layers[c->L - 1].ln_final_b;
   a.emb = c->emb_bf16;
@@ -953,15 +1026,17 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   CK(cudaMemsetAsync(c->dev_error, 0, sizeof(int), s));
   if (c->bar) CK(cudaMemsetAsync(c->bar, 0, 2 * sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->counter, 0, sizeof(unsigned), s));
-  CK(cudaMemsetAsync(c->keys, 0, c->B * sizeof(unsigned long long), s));
+  CK(cudaMemsetAsync(c->keys, 0, (size_t)c->B * kKeyStride * sizeof(unsigned long long), s));
   if (c->acc_self) CK(cudaMemsetAsync(c->acc_self, 0, (size_t)c->maxM * c->D * sizeof(unsigned long long), s));
   if (c->acc_cross) CK(cudaMemsetAsync(c->acc_cross, 0, (size_t)c->maxM * c->D * sizeof(unsigned long long), s));
+  if (c->acc_ffn) CK(cudaMemsetAsync(c->acc_ffn, 0, (size_t)c->maxM * c->D * sizeof(unsigned long long), s));
   return fail(S2R_EDEVICE, "a kernel reported error %d (%s); its work was skipped", err,
               err == kErrAttnCluster ? "attention launched without its cluster shape"
               : err == kErrAttnChunk ? "attention keys exceed the score buffer"
               : err == kErrAttnStage ? "a bulk copy of the attention kernel did not complete in time"
               : err == kErrAttnExchange ? "a value sent between attention CTAs did not arrive in time"
               : err == kErrGemmWait  ? "a wait of the tensor-core projection timed out"
+              : err == kErrFfnStage  ? "a bulk copy of the fused FFN did not complete in time"
               : err == kErrAccRange  ? "an out-projection partial was too large (or NaN) for the fixed-point sum"
                                      : "a grid barrier of the persistent step timed out");
 }
@@ -1156,10 +1231,24 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   TRYC(dalloc(c, &c->prefill_tokens, kPrefillRows));
   TRYC(setup_tensor_core(c));
   c->fuse_out = !c->tc && !c->persistent;
+  c->fuse_ffn = c->fuse_out && c->B == 1 && c->D <= 1024 && c->FFN % kFfnSlice == 0 &&
+                ffn_smem_bytes(c->D) + 4096 <= (size_t)227 * 1024;
+  if (c->fuse_ffn) {
+    for (int l = 0; l < c->L; ++l) {
+      LayerBufs& b = c->layers[l];
+      TRYC(dalloc(c, &b.w2s, FFN * D));
+      slice_major_kernel<<<1024, 256>>>(b.w2, b.w2s, (int)D, (int)FFN);
+      CKC(cudaGetLastError());
+    }
+  }
   if (c->fuse_out) {
     TRYC(dalloc(c, &c->acc_self, (size_t)c->maxM * D));
     TRYC(dalloc(c, &c->acc_cross, (size_t)c->maxM * D));
     TRYC(dalloc(c, &c->x_b, (size_t)c->maxM * D));
+    TRYC(dalloc(c, &c->x_c, (size_t)c->maxM * D));
+    TRYC(dalloc(c, &c->acc_ffn, (size_t)c->maxM * D));
+    CKC(cudaMemset(c->x_c, 0, (size_t)c->maxM * D * sizeof(float)));
+    CKC(cudaMemset(c->acc_ffn, 0, (size_t)c->maxM * D * sizeof(unsigned long long)));
     CKC(cudaMemset(c->acc_self, 0, (size_t)c->maxM * D * sizeof(unsigned long long)));
     CKC(cudaMemset(c->acc_cross, 0, (size_t)c->maxM * D * sizeof(unsigned long long)));
     CKC(cudaMemset(c->x_b, 0, (size_t)c->maxM * D * sizeof(float)));
@@ -1177,7 +1266,7 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     CKC(cudaMemcpy(c->order_self, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
     CKC(cudaMemcpy(c->order_cross, ident.data(), c->B * sizeof(int32_t), cudaMemcpyHostToDevice));
   }
-  TRYC(dalloc(c, &c->keys, c->B));
+  TRYC(dalloc(c, &c->keys, (size_t)c->B * kKeyStride));
   TRYC(dalloc(c, &c->counter, 1));
   TRYC(dalloc(c, &c->dev_error, 1));
   CKC(cudaMemset(c->dev_error, 0, sizeof(int)));
@@ -1185,7 +1274,7 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   TRYC(dalloc(c, &c->dbg_forced, c->B));
   TRYC(dalloc(c, &c->dbg_logits, (size_t)c->B * V));
   TRYC(dalloc(c, &c->dbg_greedy, c->B));
-  CKC(cudaMemset(c->keys, 0, c->B * sizeof(unsigned long long)));
+  CKC(cudaMemset(c->keys, 0, (size_t)c->B * kKeyStride * sizeof(unsigned long long)));
   CKC(cudaMemset(c->counter, 0, sizeof(unsigned int)));
   CKC(cudaMemset(c->bias, 0, V * sizeof(float)));
   CKC(cudaMemset(c->r, 0, M * D * sizeof(float)));
@@ -1752,6 +1841,10 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
       per[K_CROSS_ATTN] += per[K_CROSS_Q];
       per[K_CROSS_Q] = 0.0;
     }
+    if (c->fuse_ffn) {  // fc1 and fc2 in one launch
+      per[K_FC1] += per[K_FC2];
+      per[K_FC2] = 0.0;
+    }
   }
   for (int b = 0; b < c->B; ++b) {
     if (!c->loaded[b]) continue;
@@ -1822,7 +1915,8 @@ int32_t s2r_step_launches(s2r_ctx* c) {
   if (!c->fuse_out) return 8 * c->L + 1;
   // attention fused with its out-projection; the cross q launch folds into
   // the cross attention when that computes its own query rows
-  return (plan_attn(c, c->B, true).fuse_q ? 5 : 6) * c->L + 1;
+  // and one-slot engines run the FFN as one launch
+  return ((plan_attn(c, c->B, true).fuse_q ? 5 : 6) - (c->fuse_ffn ? 1 : 0)) * c->L + 1;
 }
 
 int32_t s2r_free_pages(s2r_ctx* c) { return c ? (int32_t)c->free_pages.size() : 0; }

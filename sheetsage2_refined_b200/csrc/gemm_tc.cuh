@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint32_t tmem_base;
   __shared__ int aborted, good, is_last;
   __shared__ uint32_t rule[EPI == EPI_LOGITS ? NB : 1];
+  __shared__ unsigned long long row_best[EPI == EPI_LOGITS ? NB : 1];  // this CTA's best key per row
   __shared__ float sbias[kTcBlockN];  // bias of this CTA's features (weights: read before the wait)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -258,7 +259,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tmem_fence_after();
   pdl_wait();  // the previous kernel may read what the epilogue overwrites until it completes
   if constexpr (EPI == EPI_LOGITS) {
-    for (int r = threadIdx.x; r < NB; r += kTcThreads) rule[r] = m0 + r < M ? row_rule(t.lg.gr, t.lg.st, m0 + r) : 0u;
+    for (int r = threadIdx.x; r < NB; r += kTcThreads) {
+      rule[r] = m0 + r < M ? row_rule(t.lg.gr, t.lg.st, m0 + r) : 0u;
+      row_best[r] = 0ull;
+    }
     __syncthreads();
   }
 
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if constexpr (EPI == EPI_LOGITS) {
           unsigned long long key = (m < M && n < N) ? tc_logit_key(t, rule[c + j], m, n, v) : 0ull;
           key = warp_max_u64(key);
-          if (lane == 0 && key) atomicMax(t.lg.keys + m, key);
+          if (lane == 0 && key) atomicMax(&row_best[c + j], key);
         } else {
           if (m < M && n < N) tc_store<EPI>(t, m, n, v + sbias[f_own]);
         }
@@ -362,7 +366,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
           key = warp_max_u64(key);  // the warp covers the row's 128 features
-          if (lane == 0 && key) atomicMax(t.lg.keys + m, key);
+          if (lane == 0 && key) atomicMax(&row_best[r], key);
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -374,7 +378,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   if constexpr (EPI == EPI_LOGITS) {
-    // ---- the last CTA of the grid commits the step
+    // ---- one global atomic per row and CTA (rows on separate lines), then the
+    // last CTA of the grid commits the step
+    __syncthreads();
+    for (int r = threadIdx.x; r < NB; r += kTcThreads)
+      if (row_best[r] && m0 + r < M) atomicMax(t.lg.keys + (size_t)(m0 + r) * kKeyStride, row_best[r]);
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0)

@@ -5,6 +5,7 @@ namespace s2r {
 
 ProjFn proj_fn_rows(int in, int epi, int kch, int mc) {
   if (in == IN_BF16 && epi == EPI_RESID) return pick_proj<IN_BF16, EPI_RESID>(kch, mc);
+  if (in == IN_BF16 && epi == EPI_SLICES) return pick_proj<IN_BF16, EPI_SLICES>(kch, mc);  // fc2 into fixed-point sums
   if (in == IN_BF16 && epi == EPI_CROSSKV) return pick_proj<IN_BF16, EPI_CROSSKV>(kch, mc);
   if (in == IN_F32 && epi == EPI_CROSSKV) return pick_proj<IN_F32, EPI_CROSSKV>(kch, mc);
   return nullptr;

@@ -58,12 +58,14 @@ struct LogitsArgs {
   int M, V, D, max_tokens;
   SlotState st;
   Grammar gr;
-  const float* r;  // [M, D] residual sums before the last final_norm
+  const float* r;  // [M, D] residual sums before the last final_norm; with acc: the residual input x
+  const unsigned long long* acc;  // null, or [M, D] fixed-point fc2 sums: the input is x + bf16(acc + acc_bias)
+  const bf16* acc_bias;           // [D] fc2 bias
   const float* gamma;
   const float* beta;
   const bf16* emb;    // tied output embedding [V, D], bfloat16
   const float* bias;  // [V] or null
-  unsigned long long* keys;  // [M], zero between steps
+  unsigned long long* keys;  // [M * kKeyStride] (row m at m * kKeyStride), zero between steps
   unsigned int* counter;     // zero between steps
   const int64_t* forced;     // [M] or null: commit forced[m] >= 0 instead of the greedy token
   float* logits_out;         // [M, V] or null: raw logits
@@ -209,7 +211,7 @@ __device__ __forceinline__ void rescore_commit(const Rescore& r, const Grammar& 
 // advances and the keys return to zero.  Run by one CTA.
 __device__ __forceinline__ void commit_rows(const LogitsArgs& a) {
   for (int s = threadIdx.x; s < a.M; s += blockDim.x) {
-    const unsigned long long k = atomicExch(a.keys + s, 0ull);
+    const unsigned long long k = atomicExch(a.keys + (size_t)s * kKeyStride, 0ull);
     const int64_t greedy = key_token(k);
     if (a.greedy_out) a.greedy_out[s] = greedy;
     const bool active = a.st.finished[s] == 0;
@@ -265,6 +267,8 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
   pa.M = a.M;
   pa.K = D;
   pa.r = a.r;
+  pa.acc = a.acc;
+  pa.acc_bias = a.acc_bias;
   pa.gamma = a.gamma;
   pa.beta = a.beta;
   pa.x_out = nullptr;
@@ -272,10 +276,16 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
   for (int m0 = 0; m0 < a.M; m0 += MC) {
     const int mc = min(MC, a.M - m0);
     if (m0 > 0) __syncthreads();
-    if constexpr (MC == 1)
-      stage_ln_row_block<KCH, IN_LN, NW * 32>(pa, xs, m0, a.gamma, a.beta, false);
-    else
+    if constexpr (MC == 1) {
+      if (a.acc)
+        stage_ln_row_block<KCH, IN_ACC, NW * 32>(pa, xs, m0, a.gamma, a.beta, false);
+      else
+        stage_ln_row_block<KCH, IN_LN, NW * 32>(pa, xs, m0, a.gamma, a.beta, false);
+    } else if (a.acc) {
+      stage_ln_rows<KCH, IN_ACC>(pa, xs, m0, mc, warp, lane, NW);
+    } else {
       stage_ln_rows<KCH, IN_LN>(pa, xs, m0, mc, warp, lane, NW);
+    }
     for (int idx = threadIdx.x; idx < (MC - mc) * (KP / 8); idx += blockDim.x) {
       const int i = mc + idx / (KP / 8), col = (idx % (KP / 8)) * 8;
       *reinterpret_cast<uint4*>(xs + (size_t)i * KP + col) = make_uint4(0, 0, 0, 0);
@@ -325,7 +335,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
     if (threadIdx.x < mc) {
       unsigned long long k = 0ull;
       for (int ww = 0; ww < NW; ++ww) k = wbest[ww][threadIdx.x] > k ? wbest[ww][threadIdx.x] : k;
-      if (k) atomicMax(a.keys + m0 + threadIdx.x, k);
+      if (k) atomicMax(a.keys + (size_t)(m0 + threadIdx.x) * kKeyStride, k);
     }
   }
 

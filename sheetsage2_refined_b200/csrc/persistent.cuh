@@ -855,7 +855,7 @@ __global__ void __launch_bounds__(kPThreads, 1) step_persistent_kernel(const PAr
       if (tid < a.M) {
         unsigned long long k = 0ull;
         for (int w = 0; w < kPWarps; ++w) k = wbest[w][tid] > k ? wbest[w][tid] : k;
-        if (k) atomicMax(a.keys + tid, k);
+        if (k) atomicMax(a.keys + (size_t)tid * kKeyStride, k);
       }
       __threadfence();
       csync();
@@ -865,7 +865,7 @@ __global__ void __launch_bounds__(kPThreads, 1) step_persistent_kernel(const PAr
         __threadfence();
         const bool bad = *(volatile int*)a.err != 0;  // a wait gave up: leave the slots as they were
         for (int sl = tid; sl < a.M; sl += kPConsumers) {
-          const unsigned long long k = atomicExch(a.keys + sl, 0ull);
+          const unsigned long long k = atomicExch(a.keys + (size_t)sl * kKeyStride, 0ull);
           if (bad) continue;
           const int64_t greedy = key_token(k);
           if (a.greedy_out) a.greedy_out[sl] = greedy;

@@ -20,6 +20,11 @@
 //   EPI_BF16    bf16(acc + b)
 //   EPI_GELU    bf16(gelu(bf16(acc + b)))  (exact erf GELU on the bfloat16 value, decoder.py:83)
 //   EPI_CROSSKV cross K/V of one slot's encoder frames (decoder.py:108-113)
+//   EPI_SLICES  the fixed-point sum, over 32-column slices of K, of each
+//               slice's float32 partial product (no bias): fc2 into the
+//               accumulator the next LayerNorm reads (IN_ACC), so that the
+//               fused FFN kernel, which adds the same slice partials with
+//               integer atomics, gives the same bits
 // Rounding follows the reference's CUDA autocast: the Linear input is the
 // bfloat16 rounding of the float32 activation, accumulation is float32 and the
 // output is rounded once after the bias is added.
@@ -33,7 +38,9 @@ enum InMode { IN_LN = 0, IN_EMBED = 1, IN_BF16 = 2, IN_F32 = 3, IN_ACC = 4 };
 
 template <int IN>
 __host__ __device__ constexpr bool ln_input() { return IN == IN_LN || IN == IN_EMBED || IN == IN_ACC; }
-enum EpiMode { EPI_QKV = 0, EPI_RESID = 1, EPI_BF16 = 2, EPI_GELU = 3, EPI_CROSSKV = 4 };
+enum EpiMode { EPI_QKV = 0, EPI_RESID = 1, EPI_BF16 = 2, EPI_GELU = 3, EPI_CROSSKV = 4, EPI_SLICES = 5 };
+
+constexpr int kSliceCols = 32;  // EPI_SLICES: columns of K per fixed-point partial (4 lanes x 8)
 
 struct ProjArgs {
   int M, K, N;
@@ -67,7 +74,18 @@ struct ProjArgs {
   // words cleared after the wait: an accumulator whose reader has finished
   unsigned long long* zero;
   int zero_n;
+  unsigned long long* acc_out;  // EPI_SLICES: [M, N]
+  int* err;                     // device error word (a slice partial out of the fixed-point range)
 };
+
+// One 32-column slice partial of an EPI_SLICES row: the 8-product pieces of
+// lanes 4t .. 4t+3 (columns 256c + 32t .. +31) added as (d0 + d1) + (d2 + d3);
+// every lane of the group ends with the same value.
+__device__ __forceinline__ float slice_partial(float d) {
+  d += __shfl_xor_sync(0xffffffffu, d, 1);
+  d += __shfl_xor_sync(0xffffffffu, d, 2);
+  return d;
+}
 
 __device__ __forceinline__ float dot8(const uint4 w, const uint4 x) {
   float s = bf_lo(w.x) * bf_lo(x.x);
@@ -366,7 +384,7 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
       *reinterpret_cast<float4*>(sbeta + i) = *reinterpret_cast<const float4*>(a.beta + i);
     }
   }
-  const float bias_first = first < a.N ? __bfloat162float(a.bias[first]) : 0.f;
+  const float bias_first = (EPI != EPI_SLICES && first < a.N) ? __bfloat162float(a.bias[first]) : 0.f;
   pdl_launch_dependents();
   pdl_wait();
   if (a.zero) {  // the launch before this one has read the accumulator
@@ -434,6 +452,32 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
           const int col = c * 256 + lane * 8;
           w[c] = col < K ? ld_stream(a.W + (size_t)n * K + col) : make_uint4(0, 0, 0, 0);
         }
+      }
+      if constexpr (EPI == EPI_SLICES) {
+        // per 32-column slice: partial product, rounded to fixed point, summed as integers
+        long long isum[MC];
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < MC; ++i) isum[i] = 0;
+#pragma unroll
+        for (int c = 0; c < KCH; ++c) {
+#pragma unroll
+          for (int i = 0; i < MC; ++i) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)i * KP + c * 256 + lane * 8);
+            const float p = slice_partial(dot8(w[c], xv));
+            ok &= fabsf(p) < kAccLimit;
+            isum[i] += __float2ll_rn(p * kAccScale);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < MC; ++i) {
+          // the 4 lanes of a slice group hold the same sum: add one lane per group
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) isum[i] += __shfl_xor_sync(0xffffffffu, isum[i], o);
+          if (lane == i && i < mc) a.acc_out[(size_t)(m0 + i) * a.N + n] = (unsigned long long)isum[i];
+        }
+        if (__any_sync(0xffffffffu, !ok) && lane == 0 && a.err) atomicExch(a.err, kErrAccRange);
+        continue;
       }
       float acc[MC];
 #pragma unroll

@@ -16,6 +16,10 @@
 
 namespace s2r {
 
+// Row m's key lives at keys[m * kKeyStride]: one 128-byte line per row, so
+// that the atomics of different rows go to different L2 lines.
+constexpr int kKeyStride = 16;
+
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   uint32_t u = __float_as_uint(v);
   if (u == 0x80000000u) u = 0u;        // -0 ties with +0

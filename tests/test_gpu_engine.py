@@ -137,9 +137,9 @@ def test_one_kernel_and_multi_kernel_steps_agree():
     g = np.load(GOLDEN / "c2_head.npz")
     tokens = g["tokens"].tolist()
     engines = [cuda_engine(sc.C2, sc.C2_SEED, sc.c2_grammar(), 1, sc.C2_FRAMES, flags=f) for f in (4, 0)]
-    # attention fused with its out-projection, residual and LayerNorm, the cross attention
-    # computing its own query rows: 5 launches per layer + logits
-    assert engines[0].step_launches == 1 and engines[1].step_launches == 5 * sc.C2.layers + 1
+    # attention fused with its out-projection, the cross attention computing its own query
+    # rows, one-slot engines running the FFN as one kernel: 4 launches per layer + logits
+    assert engines[0].step_launches == 1 and engines[1].step_launches == 4 * sc.C2.layers + 1
     for e in engines:
         loader(e, sc.C2.width, sc.C2_FRAMES)(0, sc.C2_MEMORY_SEED, tokens[:2], None, sc.C2_FRAMES, 24)
     err, same = 0.0, 0
