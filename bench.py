@@ -300,7 +300,8 @@ def load_launches(eng, layers: int, prefix_len: int = 2) -> int:
     prefix positions before the last (one chunk for short prefixes): a full
     layer but only the K/V projection in the last one (5 or 6 launches per
     layer on the CUDA-core path, 11 on tensor-core engines); the one-kernel
-    step engine prefills with one launch.
+    step engine prefills with one launch.  One-slot engines decode with a
+    fused FFN (4 launches per layer) but prefill with fc1 and fc2 (5).
     """
 
     L, per_step = layers, eng.step_launches
@@ -311,6 +312,8 @@ def load_launches(eng, layers: int, prefix_len: int = 2) -> int:
     if per_step == 11 * L + 2:
         return L + 11 * (L - 1) + 2
     per_layer = (per_step - 1) // L
+    if per_layer == 4:  # fused FFN in decode only
+        per_layer = 5
     return L + per_layer * (L - 1) + 1
 
 
@@ -1098,10 +1101,11 @@ def main():
     ap.add_argument("--max-tokens", type=int, default=None, help="override the context length (profiling cases)")
     ap.add_argument("--batch-frames", type=int, default=None, help="override the batched frames cap (profiling cases)")
     args = ap.parse_args()
-    global CONFIG, BATCH_FRAMES, OVERRIDES
+    global CONFIG, REAL, BATCH_FRAMES, OVERRIDES
     if args.layers or args.max_tokens:
         CONFIG = dataclasses.replace(CONFIG, layers=args.layers or CONFIG.layers,
                                      max_tokens=args.max_tokens or CONFIG.max_tokens)
+        REAL = dataclasses.replace(REAL, layers=args.layers or REAL.layers)
         OVERRIDES.update(layers=CONFIG.layers, max_tokens=CONFIG.max_tokens)
     if args.batch_frames:
         BATCH_FRAMES = args.batch_frames

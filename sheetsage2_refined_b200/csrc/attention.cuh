@@ -266,10 +266,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   // kStage: whether this thread saw the copies land (if not, it waits for them
   // again, bounded, before the CTA exits; the error word is set either way)
   bool staged = true, q_staged = true;
-  auto drain = [&]() {
-    if (kStage && !staged) mbar_wait(&bars[0], 0);
-    if (fuse_q && !q_staged) mbar_wait(&bars[1], 0);
-  };
   __syncthreads();  // the barriers are initialised before anyone waits on them
   // First half of a barrier that proves every peer has started and initialised
   // its barriers before the first store into its shared memory (the wait comes
@@ -507,7 +503,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       for (int r = 0; r < C; ++r) o += xo[r][tid];
       a.out[(size_t)m * a.ldo + h * kHeadDim + tid] = __float2bfloat16_rn(o);
     }
-    drain();
+    // no copy may still be landing in this CTA's shared memory when it exits (bounded waits)
+    if (kStage && !staged) mbar_wait(&bars[0], 0);
+    if (fuse_q && !q_staged) mbar_wait(&bars[1], 0);
     cluster_wait();
   } else {
     if (tid < kHeadDim) {
@@ -544,7 +542,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       emit(p, (i < per && n < a.D) ? ld_stream(a.wo + (size_t)n * a.D + h * kHeadDim + sub * 8) : make_uint4(0, 0, 0, 0));
     }
     if (!in_range) atomicExch(a.err, kErrAccRange);
-    drain();
+    // no copy may still be landing in this CTA's shared memory when it exits (bounded waits)
+    if (kStage && !staged) mbar_wait(&bars[0], 0);
+    if (fuse_q && !q_staged) mbar_wait(&bars[1], 0);
     cluster_wait();
   }
 }

@@ -52,7 +52,7 @@ constexpr int kTcBlockK = 64;   // K per stage: 128 bytes of bf16, one swizzle r
 constexpr int kTcStages = 4;
 constexpr int kErrGemmWait = 4;                          // an mbarrier wait of the tensor-core GEMM timed out
 
-constexpr int EPI_LOGITS = 5;  // tied-embedding logits + grammar mask + greedy argmax (+ commit)
+constexpr int EPI_LOGITS = 6;  // (after the EpiMode values) tied-embedding logits + grammar mask + greedy argmax (+ commit)
 constexpr int kTcMaxSplits = 8;
 
 struct TcArgs {
@@ -137,11 +137,12 @@ __device__ __forceinline__ void tc_store(const TcArgs& t, int m, int n, float v)
 
 // EPI_LOGITS: the logit of token n for row m (stored when requested) and its
 // argmax key, 0 when the grammar masks the token.
-__device__ __forceinline__ unsigned long long tc_logit_key(const TcArgs& t, uint32_t rule, int m, int n, float v) {
+__device__ __forceinline__ unsigned long long tc_logit_key(const TcArgs& t, uint32_t rule, const RescoreRow& rr, int m,
+                                                           int n, float v, float bias) {
   const float logit = round_bf16(v);
   if (t.lg.logits_out) t.lg.logits_out[(size_t)m * t.lg.V + n] = logit;
   if (!token_allowed(t.lg.gr, rule, t.lg.V, n)) return 0ull;
-  return argmax_key(rescore_logit(t.lg.rs, t.lg.st, m, n, logit + (t.lg.bias ? t.lg.bias[n] : 0.f)), n);
+  return argmax_key(rescore_logit_row(t.lg.rs, rr, m, n, logit + bias), n);
 }
 
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ int aborted, good, is_last;
   __shared__ uint32_t rule[EPI == EPI_LOGITS ? NB : 1];
   __shared__ unsigned long long row_best[EPI == EPI_LOGITS ? NB : 1];  // this CTA's best key per row
+  __shared__ RescoreRow rrow[EPI == EPI_LOGITS ? NB : 1];              // rescoring state per row
   __shared__ float sbias[kTcBlockN];  // bias of this CTA's features (weights: read before the wait)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -261,6 +263,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if constexpr (EPI == EPI_LOGITS) {
     for (int r = threadIdx.x; r < NB; r += kTcThreads) {
       rule[r] = m0 + r < M ? row_rule(t.lg.gr, t.lg.st, m0 + r) : 0u;
+      rrow[r] = m0 + r < M ? rescore_row(t.lg.rs, t.lg.st, m0 + r) : RescoreRow{0, -1, 0, 0};
       row_best[r] = 0ull;
     }
     __syncthreads();
@@ -282,16 +285,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = 0u;
       }
+      if constexpr (EPI == EPI_LOGITS) {
+        // the 32 rows' keys first (independent loads of the grammar and rescoring tables), then
+        // the warp reductions
+        const float bias = (n < N && t.lg.bias) ? t.lg.bias[n] : 0.f;
+        unsigned long long key[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int m = m0 + c + j;
-        const float v = __uint_as_float(r[j]);
-        if constexpr (EPI == EPI_LOGITS) {
-          unsigned long long key = (m < M && n < N) ? tc_logit_key(t, rule[c + j], m, n, v) : 0ull;
-          key = warp_max_u64(key);
-          if (lane == 0 && key) atomicMax(&row_best[c + j], key);
-        } else {
-          if (m < M && n < N) tc_store<EPI>(t, m, n, v + sbias[f_own]);
+        for (int j = 0; j < 32; ++j) {
+          const int m = m0 + c + j;
+          key[j] = (m < M && n < N) ? tc_logit_key(t, rule[c + j], rrow[c + j], m, n, __uint_as_float(r[j]), bias) : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const unsigned long long k = warp_max_u64(key[j]);
+          if (lane == 0 && k) atomicMax(&row_best[c + j], k);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = m0 + c + j;
+          if (m < M && n < N) tc_store<EPI>(t, m, n, __uint_as_float(r[j]) + sbias[f_own]);
         }
       }
     }
@@ -361,7 +374,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (m < M && n0 + f + j < N) {
-              const unsigned long long kj = tc_logit_key(t, rule[r], m, n0 + f + j, a4[j]);
+              const int n = n0 + f + j;
+              const unsigned long long kj =
+                  tc_logit_key(t, rule[r], rrow[r], m, n, a4[j], t.lg.bias ? t.lg.bias[n] : 0.f);
               key = kj > key ? kj : key;
             }
           }

@@ -153,12 +153,31 @@ __host__ __device__ constexpr int frame_term_width(int term, int no_chord) {
                             : 1;
 }
 
+// The per-slot rescoring state a row's logits read: loaded once per row.
+struct RescoreRow {
+  int now;            // current frame
+  int active;         // active meter, -1 none
+  uint8_t key_seen;   // a key has been stated
+  uint8_t no_eighth;  // the last token changed the meter (eighth positions after 0 are barred)
+};
+
+__device__ __forceinline__ RescoreRow rescore_row(const Rescore& r, const SlotState& st, int s) {
+  RescoreRow rr{0, -1, 0, 0};
+  if (r.on) {
+    rr.now = r.frame_now[s];
+    rr.active = r.active_meter[s];
+    rr.key_seen = r.key_seen[s];
+    rr.no_eighth = st.incomplete[s] == kAfterMeter && r.meter_changed[s];
+  }
+  return rr;
+}
+
 // x = logit + mode bias of token v for slot s, plus the rescoring terms in
 // the reference's order (engine.py:318-347); -inf for the eighth positions
 // after a meter change.  Terms with a zero weight are not added at all.
-__device__ __forceinline__ float rescore_logit(const Rescore& r, const SlotState& st, int s, int v, float x) {
+__device__ __forceinline__ float rescore_logit_row(const Rescore& r, const RescoreRow& rr, int s, int v, float x) {
   if (!r.on) return x;
-  const int now = r.frame_now[s];
+  const int now = rr.now;
   auto row = [&](int term) {
     return r.table[term] + ((size_t)s * r.frames + now) * frame_term_width(term, r.d1 - r.d0);
   };
@@ -172,21 +191,26 @@ __device__ __forceinline__ float rescore_logit(const Rescore& r, const SlotState
   if (v >= r.k0 && v < r.k1) {
     if (r.w[FT_KEY] != 0.f) x += r.w[FT_KEY] * row(FT_KEY)[v - r.k0];
     if (r.w[FT_KEY_BOUNDARY] != 0.f)
-      x += r.w[FT_KEY_BOUNDARY] * row(FT_KEY_BOUNDARY)[0] * (r.key_seen[s] ? 1.f : 0.f);
+      x += r.w[FT_KEY_BOUNDARY] * row(FT_KEY_BOUNDARY)[0] * (rr.key_seen ? 1.f : 0.f);
   }
   if (v == r.e0 && r.w[FT_DOWNBEAT] != 0.f) x += r.w[FT_DOWNBEAT] * row(FT_DOWNBEAT)[0];
   if (r.w[FT_METER] != 0.f) {
     if (v >= r.m0 && v < r.m1) {
-      const int m = v - r.m0, act = r.active_meter[s], a = act < 0 ? 0 : act;
+      const int m = v - r.m0, act = rr.active, a = act < 0 ? 0 : act;
       const bool change = act >= 0 && m != a;
       const bool same_unit = r.meter_unit[m] == r.meter_unit[a];
       const float* t = row(FT_METER);
       x += r.w[FT_METER] * (t[r.meter_beats[m]] - t[r.meter_beats[a]]) * ((change && same_unit) ? 1.f : 0.f);
       if (r.w[FT_DOWNBEAT] != 0.f) x += r.w[FT_DOWNBEAT] * row(FT_DOWNBEAT)[0] * (change ? 1.f : 0.f);
     }
-    if (v > r.e0 && v < r.e1 && st.incomplete[s] == kAfterMeter && r.meter_changed[s]) x = -INFINITY;
+    if (v > r.e0 && v < r.e1 && rr.no_eighth) x = -INFINITY;
   }
   return x;
+}
+
+__device__ __forceinline__ float rescore_logit(const Rescore& r, const SlotState& st, int s, int v, float x) {
+  if (!r.on) return x;
+  return rescore_logit_row(r, rescore_row(r, st, s), s, v, x);
 }
 
 // Rescoring state after slot s committed `tok` (engine.py:358-369).
@@ -246,6 +270,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
   constexpr int NW = kLogitsThreads / 32;
   bf16* xs = reinterpret_cast<bf16*>(smem_raw);  // [MC][KP]
   __shared__ uint32_t rule[MC];                   // class mask or table state per row
+  __shared__ RescoreRow rrow[MC];                 // rescoring state per row
   __shared__ unsigned long long wbest[NW][MC];
   __shared__ int is_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -293,6 +318,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
     if (threadIdx.x < MC) {
       const int s = m0 + threadIdx.x;
       rule[threadIdx.x] = threadIdx.x < mc ? row_rule(a.gr, a.st, s) : 0u;
+      rrow[threadIdx.x] = threadIdx.x < mc ? rescore_row(a.rs, a.st, s) : RescoreRow{0, -1, 0, 0};
     }
     __syncthreads();
 
@@ -321,7 +347,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
           if (a.logits_out && lane == 0) a.logits_out[(size_t)(m0 + i) * a.V + v] = logit;
           const bool ok = a.gr.kind == 1 ? a.gr.table[(size_t)rule[i] * a.V + v] != 0 : ((rule[i] >> cls) & 1u) != 0;
           if (ok) {
-            const unsigned long long k = argmax_key(rescore_logit(a.rs, a.st, m0 + i, v, logit + bias), v);
+            const unsigned long long k = argmax_key(rescore_logit_row(a.rs, rrow[i], m0 + i, v, logit + bias), v);
             best[i] = k > best[i] ? k : best[i];
           }
         }
