@@ -142,7 +142,8 @@ __device__ __forceinline__ unsigned long long tc_logit_key(const TcArgs& t, uint
   const float logit = round_bf16(v);
   if (t.lg.logits_out) t.lg.logits_out[(size_t)m * t.lg.V + n] = logit;
   if (!token_allowed(t.lg.gr, rule, t.lg.V, n)) return 0ull;
-  return argmax_key(rescore_logit_row(t.lg.rs, rr, m, n, logit + bias), n);
+  const float x = rescored_token(t.lg.rs, n) ? rescore_logit_call(t.lg.rs, rr, m, n, logit + bias) : logit + bias;
+  return argmax_key(x, n);
 }
 
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
@@ -157,7 +158,7 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k)
 template <int NB, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
-                   const TcArgs t) {
+                   const __grid_constant__ TcArgs t) {
   static_assert(NB == 64 || NB == 128 || NB == 256, "NB: 64, 128 or 256 rows");
   constexpr uint32_t kBytesW = kTcBlockN * kTcBlockK * 2;
   constexpr uint32_t kBytesX = NB * kTcBlockK * 2;

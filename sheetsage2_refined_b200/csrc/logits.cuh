@@ -213,6 +213,19 @@ __device__ __forceinline__ float rescore_logit(const Rescore& r, const SlotState
   return rescore_logit_row(r, rescore_row(r, st, s), s, v, x);
 }
 
+// Token v lies in a span some rescoring term can move.
+__device__ __forceinline__ bool rescored_token(const Rescore& r, int v) {
+  return r.on && ((v >= r.d0 && v < r.d1) || (v >= r.b0 && v < r.b1) || (v >= r.k0 && v < r.k1) ||
+                  (v >= r.e0 && v < r.e1) || (v >= r.m0 && v < r.m1));
+}
+
+// The rescoring terms as one out-of-line function: the logits epilogues call it
+// from loops unrolled over rows, which inlined copies would make too large for
+// the instruction cache.  Only tokens in a rescored span call it.
+static __device__ __noinline__ float rescore_logit_call(const Rescore& r, const RescoreRow& rr, int s, int v, float x) {
+  return rescore_logit_row(r, rr, s, v, x);
+}
+
 // Rescoring state after slot s committed `tok` (engine.py:358-369).
 __device__ __forceinline__ void rescore_commit(const Rescore& r, const Grammar& gr, int s, int64_t tok, bool active) {
   if (!r.on || !active) return;
@@ -264,7 +277,7 @@ __device__ __forceinline__ bool token_allowed(const Grammar& gr, uint32_t rule, 
 constexpr int kLogitsThreads = 256;
 
 template <int KCH, int MC>
-__global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs a) {
+__global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const __grid_constant__ LogitsArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int KP = KCH * 256;
   constexpr int NW = kLogitsThreads / 32;
@@ -335,6 +348,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
       }
       const float bias = a.bias ? a.bias[v] : 0.f;
       const int cls = a.gr.kind == 1 ? 0 : a.gr.token_class[v];
+      const bool rescored = rescored_token(a.rs, v);
 #pragma unroll
       for (int i = 0; i < MC; ++i) {
         float acc = 0.f;
@@ -347,7 +361,8 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const LogitsArgs
           if (a.logits_out && lane == 0) a.logits_out[(size_t)(m0 + i) * a.V + v] = logit;
           const bool ok = a.gr.kind == 1 ? a.gr.table[(size_t)rule[i] * a.V + v] != 0 : ((rule[i] >> cls) & 1u) != 0;
           if (ok) {
-            const unsigned long long k = argmax_key(rescore_logit_row(a.rs, rrow[i], m0 + i, v, logit + bias), v);
+            const float x = rescored ? rescore_logit_call(a.rs, rrow[i], m0 + i, v, logit + bias) : logit + bias;
+            const unsigned long long k = argmax_key(x, v);
             best[i] = k > best[i] ? k : best[i];
           }
         }
