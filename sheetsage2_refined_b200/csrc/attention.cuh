@@ -69,6 +69,7 @@ struct AttnArgs {
   int fuse_q;
   unsigned long long* zero;  // cleared after the wait (an accumulator the launch before has read)
   int zero_n;
+  L2Ahead ahead;  // what the next kernel reads, prefetched into the L2 before the wait
 };
 
 constexpr int kAttnOutPrefetch = 4;  // out-projection passes (32 features each) loaded before the wait
@@ -243,6 +244,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         bulk_load(sv + (size_t)(s - j0) * kHeadDim, attn_row(a, a.v, slot, h, s), bytes, &bars[0]);
         s = e;
       }
+      // rows past the stage that were written before the step: into the L2
+      // now, so that the loops' reads of them after the wait hit it
+      const int jl = min(j1, fresh);
+      for (int s = js; s < jl;) {
+        const int e = a.cross ? jl : min(jl, (s / kPageTokens + 1) * kPageTokens);
+        const uint64_t bytes = (uint64_t)(e - s) * kHeadDim * 2;
+        l2_prefetch_bytes(attn_row(a, a.k, slot, h, s), bytes);
+        l2_prefetch_bytes(attn_row(a, a.v, slot, h, s), bytes);
+        s = e;
+      }
     }
   }
   if constexpr (kAccOut) {
@@ -263,6 +274,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       vpre[u] = ok ? ld_stream(attn_row(a, a.v, slot, h, j) + sub * 8) : make_uint4(0, 0, 0, 0);
     }
   }
+  if (tid == 0)
+    l2_ahead(a.ahead, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x, gridDim.x * gridDim.y * gridDim.z);
   // kStage: whether this thread saw the copies land (if not, it waits for them
   // again, bounded, before the CTA exits; the error word is set either way)
   bool staged = true, q_staged = true;
@@ -422,7 +435,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     for (int w = 1; w < kAttnThreads / 32; ++w) v = fmaxf(v, wmax[w]);
     st_async_f32(&xred[0][rank], tid, v, &xbar[0]);
   }
-  bool exchanged = mbar_wait(&xbar[0], 0);
+  if (!mbar_wait(&xbar[0], 0)) atomicExch(a.err, kErrAttnExchange);
   float gmax = -INFINITY;
   for (int r = 0; r < C; ++r) gmax = fmaxf(gmax, xred[0][r]);
 
@@ -441,7 +454,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     for (int w = 0; w < kAttnThreads / 32; ++w) v += wsum[w];
     st_async_f32(&xred[1][rank], tid, v, &xbar[1]);
   }
-  exchanged &= mbar_wait(&xbar[1], 0);
+  if (!mbar_wait(&xbar[1], 0)) atomicExch(a.err, kErrAttnExchange);
   float gsum = 0.f;
   for (int r = 0; r < C; ++r) gsum += xred[1][r];
   // p = bf16(e / sum), once per key (each thread divides the values it wrote)
@@ -491,8 +504,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
       st_async_f32(&xo[rank][tid], 0, o, &xbar[2]);
     }
   }
-  if (gets_o) exchanged &= mbar_wait(&xbar[2], 0);
-  if (!exchanged) atomicExch(a.err, kErrAttnExchange);
+  if (gets_o && !mbar_wait(&xbar[2], 0)) atomicExch(a.err, kErrAttnExchange);
   // Everything sent to this CTA has landed.  Every CTA waits at its exit for
   // the whole cluster to get here, so no CTA leaves while a store into it
   // could still be on its way.

@@ -53,6 +53,45 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
 
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
+// Byte ranges the next kernel of the stream reads that nothing writes during
+// a decode step (weights; a window's cross keys and values).  Each CTA of the
+// kernel before it asks the L2 for its share ahead of its own PDL wait, so
+// the next kernel's loads hit the L2 even where it cannot start beside this
+// one (its shared memory does not fit next to this kernel's).  Ranges start
+// 16-byte aligned and their lengths are multiples of 16 (the host drops a
+// range that is not); n = 0 marks an unused entry.
+constexpr int kL2AheadRanges = 4;
+constexpr uint32_t kL2AheadPiece = 32768;  // bytes per bulk prefetch instruction
+
+struct L2Ahead {
+  const void* p[kL2AheadRanges];
+  uint32_t n[kL2AheadRanges];
+};
+
+// Ask the L2 for n bytes at p (16-byte aligned, n a multiple of 16); no data
+// reaches the SM and nothing waits for it.
+__device__ __forceinline__ void l2_prefetch_bytes(const void* p, uint64_t n) {
+  const char* base = static_cast<const char*>(p);
+  for (uint64_t o = 0; o < n; o += kL2AheadPiece) {
+    const uint32_t len = (uint32_t)(n - o < kL2AheadPiece ? n - o : kL2AheadPiece);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + o), "r"(len) : "memory");
+  }
+}
+
+// CTA `cta` of `ctas` prefetches its 16-byte-aligned share of every range.
+__device__ __forceinline__ void l2_ahead(const L2Ahead& pf, unsigned cta, unsigned ctas) {
+#pragma unroll
+  for (int i = 0; i < kL2AheadRanges; ++i) {
+    const uint64_t n = pf.n[i];
+    if (n == 0) continue;
+    const uint64_t per = (n / 16 + ctas - 1) / ctas * 16;
+    const uint64_t s = (uint64_t)cta * per;
+    if (s >= n) continue;
+    const uint64_t e = s + per < n ? s + per : n;
+    l2_prefetch_bytes(static_cast<const char*>(pf.p[i]) + s, e - s);
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

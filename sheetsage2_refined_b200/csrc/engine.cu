@@ -507,9 +507,49 @@ AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
   return p;
 }
 
-int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s) {
+// What a kernel of a one-slot decode step reads that no kernel of the step
+// writes, for the kernel before it to prefetch into the L2 (l2_ahead).  Only
+// where the kernel cannot load it ahead of its own PDL wait: the fused FFN
+// (its shared memory does not fit beside the cross attention's, so it starts
+// late), the logits (the same for the product vocabulary's 33 MB) and the
+// step's first QKV projection (the step boundary has no programmatic
+// overlap).  The other kernels load their weights before their wait while
+// the kernel before them runs; prefetching those as well was slower.
+enum AheadOf { kAheadFfn, kAheadQkv, kAheadLogits };
+
+void add_ahead(L2Ahead& pf, int& i, const void* p, size_t n) {
+  n &= ~(size_t)15;
+  if (!p || n == 0 || (reinterpret_cast<uintptr_t>(p) & 15) || n > 0xffffffffu || i >= kL2AheadRanges) return;
+  pf.p[i] = p;
+  pf.n[i] = (uint32_t)n;
+  ++i;
+}
+
+L2Ahead l2_ahead_of(const s2r_ctx* c, int l, AheadOf next) {
+  L2Ahead pf{};
+  int i = 0;
+  if (!c->fuse_ffn) return pf;
+  const size_t D = c->D, w = D * D * sizeof(bf16);
+  const LayerBufs& lb = c->layers[l];
+  switch (next) {
+    case kAheadFfn:
+      add_ahead(pf, i, lb.w1, (size_t)c->FFN * D * sizeof(bf16));
+      add_ahead(pf, i, lb.w2s, (size_t)c->FFN * D * sizeof(bf16));
+      break;
+    case kAheadQkv:
+      add_ahead(pf, i, lb.wqkv, 3 * w);
+      break;
+    case kAheadLogits:
+      add_ahead(pf, i, c->emb_bf16, (size_t)c->V * D * sizeof(bf16));
+      break;
+  }
+  return pf;
+}
+
+int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s, L2Ahead ahead = L2Ahead{}) {
   const AttnPlan plan = plan_attn(c, M, cross);
   AttnArgs a{};
+  a.ahead = ahead;
   a.M = M;
   a.H = c->H;
   a.rm = rm;
@@ -552,10 +592,13 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   a.stage_cap = plan.stage_cap;
   const int pre = plan.pre;
   const size_t smem = plan.smem;
-  void (*fn)(const AttnArgs) =
-      pre == kAttnPreNone    ? attn_kernel<kAttnPreNone, false>
-      : pre == kAttnPreRegs  ? (c->fuse_out ? attn_kernel<kAttnPreRegs, true> : attn_kernel<kAttnPreRegs, false>)
-                             : (c->fuse_out ? attn_kernel<kAttnPreStage, true> : attn_kernel<kAttnPreStage, false>);
+  // tensor-core engines read keys in the loops and keep their out-projection a GEMM; the
+  // others load keys ahead of the wait and fuse the out-projection (persistent engines do
+  // not launch this kernel)
+  if ((pre == kAttnPreNone) == c->fuse_out) return fail(S2R_ENOTSUP, "no attention kernel for this engine");
+  void (*fn)(const AttnArgs) = pre == kAttnPreNone   ? attn_kernel<kAttnPreNone, false>
+                               : pre == kAttnPreRegs ? attn_kernel<kAttnPreRegs, true>
+                                                     : attn_kernel<kAttnPreStage, true>;
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CK(launch_ex(fn, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
   return S2R_OK;
@@ -609,6 +652,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   if (c->fuse_out) {
     // each attention fused with its out-projection (attention.cuh): fixed-point sums in
     // acc_self / acc_cross; the launch after it adds bias and residual and normalises (IN_ACC)
+    const bool ahead = c->fuse_ffn && !rm.prefill;
     TRY(launch_attn(c, rm, M, l, false, s));  // 2-3. self-attention + out-projection
     TRY(mark(c, K_SELF_ATTN, s));
     if (!plan_attn(c, M, true).fuse_q) {  // 4. self_attn_norm -> cross q (else the cross attention does it)
@@ -634,7 +678,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
       TRY(launch_proj(c, a, IN_ACC, EPI_BF16, s));
       TRY(mark(c, K_CROSS_Q, s));
     }
-    TRY(launch_attn(c, rm, M, l, true, s));  // 5-6. cross-attention + out-projection
+    TRY(launch_attn(c, rm, M, l, true, s, ahead ? l2_ahead_of(c, l, kAheadFfn) : L2Ahead{}));  // 5-6. cross-attention + out-projection
     TRY(mark(c, K_CROSS_ATTN, s));
     if (c->fuse_ffn && !rm.prefill) {  // 7-8. cross_attn_norm, fc1, GELU and fc2 in one launch
       FfnArgs f{};
@@ -654,6 +698,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
       f.zero = c->acc_self;
       f.zero_n = M * D;
       f.err = c->dev_error;
+      if (l + 1 == c->L) f.ahead = l2_ahead_of(c, l, kAheadLogits);
       const int kch = kch_for(D);
       void (*fn)(const FfnArgs) = kch == 1 ? ffn_row_kernel<1> : kch == 2 ? ffn_row_kernel<2> : ffn_row_kernel<4>;
       const size_t smem = ffn_smem_bytes(D);
@@ -900,6 +945,7 @@ int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logit
   a.logits_out = logits;
   a.greedy_out = greedy;
   a.rs = c->rs;
+  a.ahead = l2_ahead_of(c, 0, kAheadQkv);  // the next step's first kernel
   if (c->tc) {
     ProjArgs p = proj_base(c);
     p.rm = rm;

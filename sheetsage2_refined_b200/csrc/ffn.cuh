@@ -47,6 +47,7 @@ struct FfnArgs {
   unsigned long long* zero;          // cleared after the wait (an accumulator already read)
   int zero_n;
   int* err;
+  L2Ahead ahead;  // what the next kernel reads, prefetched into the L2 before the wait
 };
 
 // Dynamic shared memory: W1 rows [32][D], W2 slice [D][32] (bf16), LayerNorm
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(kFfnThreads) ffn_row_kernel(const FfnArgs a) {
   }
   // fc1 bias of this warp's 4 hidden units (lane j < 4 holds unit 4 * warp + j)
   const float b1 = lane < 4 ? __bfloat162float(a.b1[s * kFfnSlice + warp * 4 + lane]) : 0.f;
+  if (tid == 0) l2_ahead(a.ahead, blockIdx.x, gridDim.x);
   __syncthreads();  // the barrier is initialised
   pdl_launch_dependents();
   pdl_wait();

@@ -71,6 +71,7 @@ struct LogitsArgs {
   float* logits_out;         // [M, V] or null: raw logits
   int64_t* greedy_out;       // [M] or null
   Rescore rs;                // frame-head rescoring (rs.on == 0: none)
+  L2Ahead ahead;              // what the next step's first kernel reads, prefetched into the L2
 };
 
 // Class grammar constants (grammar.py:19-55).
@@ -297,6 +298,7 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const __grid_con
     const int col = c * 256 + lane * 8;
     w[c] = (first < a.V && col < D) ? ld_stream(a.emb + (size_t)first * D + col) : make_uint4(0, 0, 0, 0);
   }
+  if (threadIdx.x == 0) l2_ahead(a.ahead, blockIdx.x, gridDim.x);
   pdl_launch_dependents();
   pdl_wait();
 

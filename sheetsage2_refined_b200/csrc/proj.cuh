@@ -76,6 +76,7 @@ struct ProjArgs {
   int zero_n;
   unsigned long long* acc_out;  // EPI_SLICES: [M, N]
   int* err;                     // device error word (a slice partial out of the fixed-point range)
+  L2Ahead ahead;                // what the next kernel reads, prefetched into the L2 before the wait
 };
 
 // One 32-column slice partial of an EPI_SLICES row: the 8-product pieces of
@@ -385,6 +386,7 @@ __global__ void __launch_bounds__(proj_threads<MC>()) proj_kernel(const ProjArgs
     }
   }
   const float bias_first = (EPI != EPI_SLICES && first < a.N) ? __bfloat162float(a.bias[first]) : 0.f;
+  if (threadIdx.x == 0) l2_ahead(a.ahead, blockIdx.x, gridDim.x);
   pdl_launch_dependents();
   pdl_wait();
   if (a.zero) {  // the launch before this one has read the accumulator
