@@ -91,6 +91,7 @@ constexpr size_t kAttnOtherSmem = 32768;
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxSplits = 8;  // CTAs per (row, head) at most
 constexpr int kAttnGroups = kAttnThreads / 8;  // 8 lanes x 16 bytes per key row
+static_assert(kAttnThreads == 4 * kHeadDim && kAttnGroups % 4 == 0, "the partial-output sum takes 4 threads per dimension");
 constexpr int kAttnUnroll = 4;  // keys per group and pass (kAttnPreNone / kAttnPreRegs)
 constexpr int kAttnQRows = 8;  // fuse_q: query rows computed per CTA (one per warp)
 constexpr int kAttnQLnGroups = 128;  // fuse_q: 8-column groups of the input row (D <= 1024)
@@ -150,8 +151,12 @@ struct AttnSmem {
 // the order in which the H*C CTAs of a row arrive, and nothing waits for the
 // last of them.  The next launch adds the bias and the residual and
 // normalises the row (IN_ACC), as reference's self_attn_norm / cross_attn_norm.
+// Register budget: the fused kernels (kAccOut) at most 104 a thread (two
+// attention CTAs and a projection CTA share an SM's 64K), the batched one 48
+// (five CTAs an SM).  Left to itself ptxas chose 80 for the fused kernels and
+// spilled.
 template <int kPre, bool kAccOut>
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
+__global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
   constexpr bool kStage = kPre == kAttnPreStage;
   constexpr int kU = kStage ? kAttnUnrollStaged : kAttnUnroll;
   cg::cluster_group cluster = cg::this_cluster();
@@ -495,13 +500,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
 #pragma unroll
   for (int t = 0; t < 8; ++t) part[grp * kHeadDim + sub * 8 + t] = acc[t];
   __syncthreads();
-  if (tid < kHeadDim) {
+  {
+    // The 32 groups' partial outputs of dimension d: thread 4d + q adds groups
+    // q, q + 4, ..., q + 28 in order, then the four sums meet in a butterfly,
+    // (s0 + s1) + (s2 + s3), in the lanes of one warp.
+    const int d = tid >> 2, q = tid & 3;
     float o = 0.f;
-    for (int g = 0; g < kAttnGroups; ++g) o += part[g * kHeadDim + tid];
-    if (kAccOut) {  // every rank needs the head's output
-      for (int r = 0; r < C; ++r) st_async_f32(&xo[rank][tid], r, o, &xbar[2]);
-    } else {
-      st_async_f32(&xo[rank][tid], 0, o, &xbar[2]);
+#pragma unroll
+    for (int i = 0; i < kAttnGroups / 4; ++i) o += part[(q + 4 * i) * kHeadDim + d];
+    o += __shfl_xor_sync(0xffffffffu, o, 1);
+    o += __shfl_xor_sync(0xffffffffu, o, 2);
+    if (q == 0) {
+      if (kAccOut) {  // every rank needs the head's output
+        for (int r = 0; r < C; ++r) st_async_f32(&xo[rank][d], r, o, &xbar[2]);
+      } else {
+        st_async_f32(&xo[rank][d], 0, o, &xbar[2]);
+      }
     }
   }
   if (gets_o && !mbar_wait(&xbar[2], 0)) atomicExch(a.err, kErrAttnExchange);

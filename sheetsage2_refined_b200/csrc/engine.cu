@@ -19,6 +19,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
 #include <string>
 #include <utility>
 #include <vector>
@@ -60,10 +61,27 @@ constexpr int kPrefillRows = 64;
 int kch_for(int k) { return k <= 256 ? 1 : k <= 512 ? 2 : k <= 1024 ? 4 : k <= 2048 ? 8 : 16; }
 int mc_for(int m) { return m >= 5 ? 8 : m >= 3 ? 4 : m; }
 
+// Every kernel prefers the largest shared-memory carveout.  An SM changes its
+// L1 / shared-memory split only while it is idle, so kernels with different
+// splits do not share an SM: the next launch's CTAs (started early under PDL)
+// wait for SMs to drain, and a cluster of the attention, which needs 8 SMs
+// with room in one GPC, can wait for a second wave.  Set once per kernel and
+// device.
+void prefer_max_shared(const void* kernel) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.insert({dev, kernel}).second)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+}
+
 // Launch with optional programmatic dependent launch and cluster shape.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
                       int cluster, Args&&... args) {
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
