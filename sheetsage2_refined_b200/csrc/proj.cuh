@@ -265,43 +265,42 @@ __device__ __forceinline__ void stage_ln_rows(const ProjArgs& a, bf16* xs, int m
 
 // Mean and 1/sqrt(var + eps) of one row whose column groups are spread over
 // the NT threads of the block (thread t holds groups t + NT*c in v), in the
-// fixed order above.  red: shared memory for KCH*32 floats + 2.
+// fixed order above, returned to every thread.  red: shared memory for KCH*32
+// floats; warps may still be reading it when the first returns, so a caller
+// that calls again with the same `red` synchronises the block in between.
 template <int KCH, int NT>
 __device__ __forceinline__ float2 block_ln_stats(const float* v, int K, float* red) {
   constexpr int kG = (KCH * 32 + NT - 1) / NT;  // groups per thread
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int t = threadIdx.x, lane = t & 31;
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
     const int g = t + NT * c;
     if (g < KCH * 32 && g * 8 < K) red[g] = group_sum8(v + c * 8);
   }
   __syncthreads();
-  if (warp == 0) {
+  // every warp adds the group sums itself, in the same order: the same mean in
+  // each, with no second barrier to broadcast it
+  float mean;
+  {
     float p = 0.f;
 #pragma unroll
     for (int c = 0; c < KCH; ++c)
       if ((lane + 32 * c) * 8 < K) p += red[lane + 32 * c];
-    p = warp_sum(p);
-    if (lane == 0) red[KCH * 32] = p / (float)K;
+    mean = warp_sum(p) / (float)K;
   }
-  __syncthreads();
-  const float mean = red[KCH * 32];
+  __syncthreads();  // every warp has read the sums before they are overwritten
 #pragma unroll
   for (int c = 0; c < kG; ++c) {
     const int g = t + NT * c;
     if (g < KCH * 32 && g * 8 < K) red[g] = group_sq8(v + c * 8, mean);
   }
   __syncthreads();
-  if (warp == 0) {
-    float p = 0.f;
+  float p = 0.f;
 #pragma unroll
-    for (int c = 0; c < KCH; ++c)
-      if ((lane + 32 * c) * 8 < K) p += red[lane + 32 * c];
-    p = warp_sum(p);
-    if (lane == 0) red[KCH * 32 + 1] = rsqrtf(p / (float)K + kLnEps);
-  }
-  __syncthreads();
-  return make_float2(mean, red[KCH * 32 + 1]);
+  for (int c = 0; c < KCH; ++c)
+    if ((lane + 32 * c) * 8 < K) p += red[lane + 32 * c];
+  p = warp_sum(p);
+  return make_float2(mean, rsqrtf(p / (float)K + kLnEps));
 }
 
 // One LayerNorm'd row (IN_LN, IN_EMBED or IN_ACC) staged by all NT threads of
