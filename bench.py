@@ -72,7 +72,7 @@ REAL_PROMPTS = ("timestamp", "downbeat_meter", "chord_detail", "key_mode", "melo
 REAL_MODE_BIAS = [0.0, 1.5, -0.5, 2.0, 0.25, -1.0, 3.0, 0.5, -2.0]
 REAL_FRAME_WEIGHT = {"root": 0.5, "bass": 0.4, "detail": 0.3, "quality": 0.3, "downbeat": 2.0, "meter": 2.0}
 OVERRIDES: dict = {}  # profiling-case overrides of the workload, reported in "config"
-CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits", "step")
+CLASS_NAMES = ("qkv", "self_attn", "self_out", "cross_q", "cross_attn", "cross_out", "fc1", "fc2", "logits")
 
 
 def peaks():

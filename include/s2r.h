@@ -68,9 +68,7 @@ typedef struct s2r_config {
 
 #define S2R_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
 #define S2R_FLAG_NO_GRAPH 2u /* issue steps as plain launches, no CUDA graph */
-#define S2R_FLAG_ONE_KERNEL_STEP 4u /* batch <= 8: run a step as one persistent kernel */
-#define S2R_FLAG_TRACE 8u          /* one-kernel step records globaltimer marks (ns) per phase ("trace" buffer) */
-/* 16u: unused (was a no-op switch) */
+/* 4u, 8u, 16u: not flags (s2r_create rejects any bit but these three) */
 #define S2R_FLAG_NO_TENSOR_CORE 32u /* every projection on the CUDA-core kernel (by default the cross K/V
                                        projection at load, and with batch >= 16 the step and prefill
                                        projections, run on tcgen05 tensor cores) */
@@ -246,7 +244,7 @@ int32_t s2r_take_ready(s2r_ctx* ctx, int32_t slot, int64_t* tokens, int32_t capa
  * 4 f64, 5 i32) of a named engine buffer, for zero-copy views: "token",
  * "position", "finished", "ended", "in_shift", "shift_run", "payload",
  * "last_field", "incomplete", "g", "count", "target", "stop", "out",
- * "frames", "trace" (with S2R_FLAG_TRACE), "cross_k" / "cross_v" (layer 0's cross K/V, bf16
+ * "frames", "cross_k" / "cross_v" (layer 0's cross K/V, bf16
  * [batch][heads][frames][64], for inspection). Replaces reads of BatchDecoder.state / .out
  * (engine.py:138-144). */
 int32_t s2r_get_buffer(s2r_ctx* ctx, const char* name, void** ptr, int64_t* numel, int32_t* dtype);
@@ -255,10 +253,9 @@ int32_t s2r_get_buffer(s2r_ctx* ctx, const char* name, void** ptr, int64_t* nume
  * with an event node after every kernel and no overlap between kernels, and
  * report per kernel
  * class — 0 qkv, 1 self attention, 2 self out-projection, 3 cross q,
- * 4 cross attention, 5 cross out-projection, 6 fc1, 7 fc2, 8 logits,
- * 9 the persistent one-kernel step — the
+ * 4 cross attention, 5 cross out-projection, 6 fc1, 7 fc2, 8 logits — the
  * summed device time in ms, the algorithmic bytes of one launch and the
- * launch count (host arrays of 10).  Synchronises `stream`.  Measurement only;
+ * launch count (host arrays of 9).  Synchronises `stream`.  Measurement only;
  * no counterpart in the reference. */
 int32_t s2r_profile_step(s2r_ctx* ctx, float* ms, double* bytes, int32_t* launches, void* stream);
 

@@ -15,7 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libs2r.so"
 S2R_OK, S2R_EINVAL, S2R_ECUDA, S2R_ENOMEM, S2R_ESTATE, S2R_ENOTSUP, S2R_EDEVICE = range(7)
 S2R_F32, S2R_BF16 = 0, 1
 S2R_NO_TARGET = (1 << 63) - 1
-S2R_FLAG_NO_PDL, S2R_FLAG_NO_GRAPH, S2R_FLAG_ONE_KERNEL_STEP, S2R_FLAG_TRACE = 1, 2, 4, 8
+S2R_FLAG_NO_PDL, S2R_FLAG_NO_GRAPH = 1, 2
 S2R_FLAG_NO_TENSOR_CORE = 32
 DTYPE_CODES = {0: "<f4", 1: "<V2", 2: "<i8", 3: "|u1", 4: "<f8", 5: "<i4"}
 

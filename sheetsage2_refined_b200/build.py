@@ -20,8 +20,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libs2r.so"
 SOURCES = [CSRC / "engine.cu", CSRC / "noalloc.cu", CSRC / "kernels_select.cu", CSRC / "kernels_tc.cu",
-           CSRC / "kernels_proj_ln.cu", CSRC / "kernels_proj_rows.cu", CSRC / "kernels_step_1.cu",
-           CSRC / "kernels_step_2.cu", CSRC / "kernels_step_4.cu"]
+           CSRC / "kernels_proj_ln.cu", CSRC / "kernels_proj_rows.cu"]
 HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "s2r.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

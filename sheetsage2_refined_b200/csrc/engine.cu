@@ -31,7 +31,6 @@
 #include "gemm_tc.cuh"
 #include "kernels.h"
 #include "logits.cuh"
-#include "persistent.cuh"
 #include "proj.cuh"
 
 using namespace s2r;
@@ -118,7 +117,6 @@ struct LayerBufs {
   bf16 *wqkv, *bqkv, *wo, *bo, *wcq, *bcq, *wckv, *bckv, *wco, *bco, *w1, *b1, *w2, *b2;
   float *ln_self_g, *ln_self_b, *ln_cross_g, *ln_cross_b, *ln_final_g, *ln_final_b;
   bf16 *kpool, *vpool, *ck, *cv;
-  bf16 *wo_hb, *wco_hb;  // out-projections by head for the persistent step kernel
   bf16* w2s;             // fc2 weight slice-major [FFN/32][D][32] for the fused FFN of one-slot engines
 };
 
@@ -178,13 +176,6 @@ struct s2r_ctx {
   int64_t* h_pos_end = nullptr;  // [B][2] position and end reason of each
   std::vector<cudaEvent_t> take_ev;
   std::vector<uint8_t> take_pending;
-  // persistent step kernel (live rows <= 8)
-  bool persistent = false;
-  int nclusters = 0, chunk_cap = 0, stages = 0;
-  PLayer* d_layers = nullptr;
-  float *part_o = nullptr, *part_c = nullptr;
-  unsigned* bar = nullptr;
-  long long* trace = nullptr;  // S2R_FLAG_TRACE: clock64 marks of the persistent step
   // tensor-core projections (tcgen05 GEMM): the step and prefill projections
   // when `tc` (16 or more slots), the cross K/V projection at load when `tc_cross`
   bool tc = false, tc_cross = false;
@@ -250,7 +241,7 @@ int dalloc(s2r_ctx* c, T** p, size_t count) {
     if (rc_ != S2R_OK) return rc_; \
   } while (0)
 
-enum KernelClass { K_QKV = 0, K_SELF_ATTN, K_SELF_OUT, K_CROSS_Q, K_CROSS_ATTN, K_CROSS_OUT, K_FC1, K_FC2, K_LOGITS, K_STEP, K_CLASSES };
+enum KernelClass { K_QKV = 0, K_SELF_ATTN, K_SELF_OUT, K_CROSS_Q, K_CROSS_ATTN, K_CROSS_OUT, K_FC1, K_FC2, K_LOGITS, K_CLASSES };
 
 int mark(s2r_ctx* c, int cls, cudaStream_t s) {
   if (!c->prof) return S2R_OK;
@@ -271,18 +262,6 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restri
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-// out[h][n][d] = in[n][64h + d] for a [D, D] bf16 matrix (an out-projection
-// regrouped so that head h's inputs of every output feature are contiguous).
-__global__ void head_block_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int D) {
-  const size_t n_total = (size_t)D * D;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_total; i += (size_t)gridDim.x * blockDim.x) {
-    const int d = (int)(i % kHeadDim);
-    const size_t rest = i / kHeadDim;
-    const int n = (int)(rest % D), h = (int)(rest / D);
-    out[i] = in[(size_t)n * D + h * kHeadDim + d];
-  }
-}
-
 // out[s][n][j] = in[n][32s + j] for the [D, FFN] fc2 weight: each 32-column
 // slice of every row made contiguous for the fused FFN kernel.
 __global__ void slice_major_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int D, int FFN) {
@@ -293,12 +272,6 @@ __global__ void slice_major_kernel(const bf16* __restrict__ in, bf16* __restrict
     const int n = (int)(rest % D), sl = (int)(rest / D);
     out[i] = in[(size_t)n * FFN + sl * kSliceCols + j];
   }
-}
-
-int head_block_bf16(const bf16* in, bf16* out, int D) {
-  head_block_kernel<<<1024, 256>>>(in, out, D);
-  CK(cudaGetLastError());
-  return S2R_OK;
 }
 
 // Copy float32 weights (host or device) into `dst` as bfloat16, through a
@@ -612,8 +585,7 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   const int pre = plan.pre;
   const size_t smem = plan.smem;
   // tensor-core engines read keys in the loops and keep their out-projection a GEMM; the
-  // others load keys ahead of the wait and fuse the out-projection (persistent engines do
-  // not launch this kernel)
+  // others load keys ahead of the wait and fuse the out-projection
   if ((pre == kAttnPreNone) == c->fuse_out) return fail(S2R_ENOTSUP, "no attention kernel for this engine");
   void (*fn)(const AttnArgs) = pre == kAttnPreNone   ? attn_kernel<kAttnPreNone, false>
                                : pre == kAttnPreRegs ? attn_kernel<kAttnPreRegs, true>
@@ -842,104 +814,9 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   return S2R_OK;
 }
 
-// Dynamic shared memory of the persistent kernel for mr rows (the ring not
-// included): it mirrors the carve-up at the top of step_persistent_kernel.
-size_t persistent_smem_fixed(const s2r_ctx* c, int mr) {
-  auto r = [](size_t b) { return (b + 127) & ~size_t(127); };
-  const size_t D = c->D, KP = (size_t)kch_for(c->D) * 256, FP = (size_t)(c->FFN + 255) / 256 * 256;
-  return r(4 * mr * D) + r(2 * mr * KP) + r(std::max(4 * (size_t)mr * c->chunk_cap, 2 * (size_t)mr * FP)) +
-         2 * r(4 * mr * kHeadDim) + r(4 * 2 * kPClus * mr * 2) + r(4 * 2 * kPClus * mr * kHeadDim) +
-         r(4 * kPWarps * kHeadDim);
-}
-
-int launch_persistent(s2r_ctx* c, RowMap rm, int M, bool logits, const int64_t* forced, float* logits_out,
-                      int64_t* greedy_out, cudaStream_t s) {
-  PArgs a{};
-  a.M = M;
-  a.rm = rm;
-  a.st = c->st;
-  a.gr = c->gr;
-  a.D = c->D;
-  a.H = c->H;
-  a.FFN = c->FFN;
-  a.V = c->V;
-  a.L = c->L;
-  a.T = c->T;
-  a.F = c->F;
-  a.pps = c->pps;
-  a.chunk_cap = c->chunk_cap;
-  a.stages = c->stages;
-  a.logits = logits ? 1 : 0;
-  a.layers = c->d_layers;
-  a.tok_emb = c->tok_emb;
-  a.pos_emb = c->pos_emb;
-  a.emb_g = c->emb_ln_g;
-  a.emb_b = c->emb_ln_b;
-  a.emb = c->emb_bf16;
-  a.bias = c->has_bias ? c->bias : nullptr;
-  a.part_o = c->part_o;
-  a.part_c = c->part_c;
-  a.r = c->r;
-  a.q = c->q;
-  a.hid = c->hid;
-  a.bar = c->bar;
-  a.keys = c->keys;
-  a.counter = c->counter;
-  a.err = c->dev_error;
-  a.forced = forced;
-  a.logits_out = logits_out;
-  a.greedy_out = greedy_out;
-  a.trace = c->trace;
-  a.rs = c->rs;
-  const int mr = mc_for(M);
-  StepFn fn = step_fn(kch_for(c->D), mr);
-  const size_t smem = persistent_smem_fixed(c, mr) + (size_t)c->stages * kPStage;
-  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  CK(launch_ex(fn, dim3(c->nclusters * kPClus), dim3(kPThreads), smem, s, false, kPClus, a));
-  return S2R_OK;
-}
-
-// Decide whether the persistent kernel can run: rows <= 8, width <= 1024, a ring of at least 3 stages next to the kernel's other
-// shared memory, and at least one cluster of 4 CTAs resident.  Sets
-// nclusters, chunk_cap and stages.
-int setup_persistent(s2r_ctx* c) {
-  c->persistent = false;
-  if (!(c->cfg.flags & S2R_FLAG_ONE_KERNEL_STEP) || c->B > kPMaxRows || c->D > 1024) return S2R_OK;
-  c->chunk_cap = std::max((c->T + kPClus - 1) / kPClus, (c->F + kPClus - 1) / kPClus);
-  const size_t fixed = persistent_smem_fixed(c, 8);
-  const size_t budget = 227 * 1024 - 2048;  // less the kernel's static shared memory
-  if (fixed + 3 * (size_t)kPStage > budget) return S2R_OK;
-  c->stages = (int)std::min<size_t>(kPMaxStages, (budget - fixed) / kPStage);
-  StepFn fn = step_fn(kch_for(c->D), 8);
-  const size_t smem = fixed + (size_t)c->stages * kPStage;
-  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kPClus * 64);
-  cfg.blockDim = dim3(kPThreads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = kPClus;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  CK(cudaOccupancyMaxActiveClusters(&n, fn, &cfg));
-  if (n < 1) return S2R_OK;
-  c->nclusters = std::min(n, 64);
-  c->persistent = true;
-  return S2R_OK;
-}
-
 int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logits, int64_t* greedy) {
   RowMap rm{0, 0, 0, nullptr};
   c->fence_next = true;
-  if (c->persistent) {
-    TRY(launch_persistent(c, rm, c->B, true, forced, logits, greedy, s));
-    TRY(mark(c, K_STEP, s));
-    return S2R_OK;
-  }
   for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, c->B, l, false, s));
   LogitsArgs a{};
   a.M = c->B;
@@ -1071,7 +948,7 @@ int setup_tensor_core(s2r_ctx* c) {
   const bool allowed = !(c->cfg.flags & S2R_FLAG_NO_TENSOR_CORE);
   if (allowed && !tensor_map_encoder()) return fail(S2R_ECUDA, "the driver has no cuTensorMapEncodeTiled");
   c->tc_cross = allowed;
-  c->tc = allowed && !c->persistent && c->B >= kTcMinBatch && c->D >= kTcBlockN;
+  c->tc = allowed && c->B >= kTcMinBatch && c->D >= kTcBlockN;
   c->tc_nb = c->maxM <= 64 ? 64 : c->maxM <= 128 ? 128 : 256;
   if (!allowed) return S2R_OK;
   if (c->tc) {
@@ -1089,7 +966,6 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
   CK(cudaStreamSynchronize(s));
   if (err == 0) return S2R_OK;
   CK(cudaMemsetAsync(c->dev_error, 0, sizeof(int), s));
-  if (c->bar) CK(cudaMemsetAsync(c->bar, 0, 2 * sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->counter, 0, sizeof(unsigned), s));
   CK(cudaMemsetAsync(c->keys, 0, (size_t)c->B * kKeyStride * sizeof(unsigned long long), s));
   if (c->acc_self) CK(cudaMemsetAsync(c->acc_self, 0, (size_t)c->maxM * c->D * sizeof(unsigned long long), s));
@@ -1103,7 +979,7 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
               : err == kErrGemmWait  ? "a wait of the tensor-core projection timed out"
               : err == kErrFfnStage  ? "a bulk copy of the fused FFN did not complete in time"
               : err == kErrAccRange  ? "an out-projection partial was too large (or NaN) for the fixed-point sum"
-                                     : "a grid barrier of the persistent step timed out");
+                                     : "unknown code");
 }
 
 template <typename T>
@@ -1141,6 +1017,8 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   if (g->kind == S2R_GRAMMAR_TABLE && (!g->table || g->states <= 0))
     return fail(S2R_EINVAL, "table grammar needs a table and states > 0");
   if (!w->layers) return fail(S2R_EINVAL, "weights.layers is NULL");
+  if ((uint32_t)k.flags & ~(S2R_FLAG_NO_PDL | S2R_FLAG_NO_GRAPH | S2R_FLAG_NO_TENSOR_CORE))
+    return fail(S2R_EINVAL, "unknown flag bits 0x%x", (unsigned)k.flags);
 
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
@@ -1256,33 +1134,6 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     CKC(cudaMemset(b.ck, 0, cross * sizeof(bf16)));
     CKC(cudaMemset(b.cv, 0, cross * sizeof(bf16)));
   }
-  TRYC(setup_persistent(c));
-  if (c->persistent) {
-    std::vector<PLayer> pl(c->L);
-    for (int l = 0; l < c->L; ++l) {
-      LayerBufs& b = c->layers[l];
-      TRYC(dalloc(c, &b.wo_hb, D * D));
-      TRYC(dalloc(c, &b.wco_hb, D * D));
-      TRYC(head_block_bf16(b.wo, b.wo_hb, (int)D));
-      TRYC(head_block_bf16(b.wco, b.wco_hb, (int)D));
-      PLayer& p = pl[l];
-      p.wqkv = b.wqkv; p.bqkv = b.bqkv; p.wo_hb = b.wo_hb; p.bo = b.bo; p.wcq = b.wcq; p.bcq = b.bcq;
-      p.wco_hb = b.wco_hb; p.bco = b.bco; p.w1 = b.w1; p.b1 = b.b1; p.w2 = b.w2; p.b2 = b.b2;
-      p.ln_self_g = b.ln_self_g; p.ln_self_b = b.ln_self_b; p.ln_cross_g = b.ln_cross_g;
-      p.ln_cross_b = b.ln_cross_b; p.ln_final_g = b.ln_final_g; p.ln_final_b = b.ln_final_b;
-      p.kpool = b.kpool; p.vpool = b.vpool; p.ck = b.ck; p.cv = b.cv;
-    }
-    TRYC(dalloc(c, &c->d_layers, c->L));
-    CKC(cudaMemcpy(c->d_layers, pl.data(), c->L * sizeof(PLayer), cudaMemcpyHostToDevice));
-    TRYC(dalloc(c, &c->part_o, (size_t)c->H * kPMaxRows * D));
-    TRYC(dalloc(c, &c->part_c, (size_t)c->H * kPMaxRows * D));
-    TRYC(dalloc(c, &c->bar, 2));
-    CKC(cudaMemset(c->bar, 0, 2 * sizeof(unsigned)));
-    if (c->cfg.flags & S2R_FLAG_TRACE) {
-      TRYC(dalloc(c, &c->trace, (size_t)kTraceCtas * kTraceSlots));
-      CKC(cudaMemset(c->trace, 0, (size_t)kTraceCtas * kTraceSlots * sizeof(long long)));
-    }
-  }
   // activations
   const size_t M = c->maxM;
   TRYC(dalloc(c, &c->r, M * D));
@@ -1295,7 +1146,7 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   c->mem_stage = mem_stage;
   TRYC(dalloc(c, &c->prefill_tokens, kPrefillRows));
   TRYC(setup_tensor_core(c));
-  c->fuse_out = !c->tc && !c->persistent;
+  c->fuse_out = !c->tc;
   c->fuse_ffn = c->fuse_out && c->B == 1 && c->D <= 1024 && c->FFN % kFfnSlice == 0 &&
                 ffn_smem_bytes(c->D) + 4096 <= (size_t)227 * 1024;
   if (c->fuse_ffn) {
@@ -1637,22 +1488,15 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
     TRY(launch_proj(c, a, memory_dtype == S2R_F32 ? IN_F32 : IN_BF16, EPI_CROSSKV, s));
   }
   // prefix prefill: K/V of prefix[0 .. n-2] at positions 0 .. n-2 (engine.py:199-205)
-  // With the persistent kernel the prefill runs through it too, 8 rows at a
-  // time, so that prefilled K/V are bit-identical to token-by-token decoding.
-  const int chunk_rows = c->persistent ? kPMaxRows : kPrefillRows;
   std::vector<int32_t> toks(kPrefillRows);
-  for (int p0 = 0; p0 < n_prefix - 1; p0 += chunk_rows) {
-    const int rows = std::min(chunk_rows, n_prefix - 1 - p0);
+  for (int p0 = 0; p0 < n_prefix - 1; p0 += kPrefillRows) {
+    const int rows = std::min(kPrefillRows, n_prefix - 1 - p0);
     for (int i = 0; i < rows; ++i) toks[i] = (int32_t)prefix[p0 + i];
-    int32_t* dst = c->prefill_tokens + (c->persistent ? (p0 / chunk_rows) % (kPrefillRows / kPMaxRows) * kPMaxRows : 0);
+    int32_t* dst = c->prefill_tokens;
     CK(cudaMemcpyAsync(dst, toks.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     RowMap rm{1, slot, p0, dst};
-    if (c->persistent) {
-      TRY(launch_persistent(c, rm, rows, false, nullptr, nullptr, nullptr, s));
-    } else {
-      c->fence_next = true;
-      for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
-    }
+    c->fence_next = true;
+    for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
   }
   CK(cudaGetLastError());
   c->loaded[slot] = 1;
@@ -1849,7 +1693,6 @@ int32_t s2r_get_buffer(s2r_ctx* c, const char* name, void** ptr, int64_t* numel,
       {"payload", st.payload, B, 2},      {"last_field", st.last_field, B, 2}, {"incomplete", st.incomplete, B, 2},
       {"g", st.g, B, 2},                  {"count", st.count, B, 2},         {"target", st.target, B, 2},
       {"stop", st.stop, B, 4},            {"out", st.out, B * c->T, 2},      {"frames", st.frames, B, 5},
-      {"trace", c->trace, c->trace ? kTraceCtas * kTraceSlots : 0, 2},
       {"cross_k", c->layers[0].ck, B * c->H * c->F * kHeadDim, 1},
       {"cross_v", c->layers[0].cv, B * c->H * c->F * kHeadDim, 1},
   };
@@ -1894,10 +1737,7 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
       FFN * D * 2 + FFN * 2 + M * D * 8 + M * FFN * 2,        // fc1
       D * FFN * 2 + D * 2 + M * FFN * 2 + M * D * 8,          // fc2
       V * D * 2 + M * D * 4 + V,                              // logits: E, r in, grammar column
-      0.0,                                                    // persistent step: filled below
   };
-  double step_bytes = 0.0;
-  for (int k = 0; k < K_STEP; ++k) step_bytes += per[k] * (k == K_LOGITS ? 1 : c->L);
   if (c->fuse_out) {  // the out-projections run inside the attention launches
     per[K_SELF_ATTN] += per[K_SELF_OUT];
     per[K_CROSS_ATTN] += per[K_CROSS_OUT];
@@ -1956,7 +1796,7 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
   }
   for (int k = 0; k < K_CLASSES; ++k) {
     ms[k] = 0.f;
-    bytes[k] = k == K_STEP ? step_bytes : per[k];
+    bytes[k] = per[k];
     launches[k] = 0;
   }
   cudaEvent_t prev = start;
@@ -1974,10 +1814,8 @@ int32_t s2r_profile_step(s2r_ctx* c, float* ms, double* bytes, int32_t* launches
 
 int32_t s2r_step_launches(s2r_ctx* c) {
   if (!c) return 0;
-  if (c->persistent) return 1;
   // tensor-core engines add a LayerNorm launch before each LayerNorm'd projection and the logits
   if (c->tc) return 11 * c->L + 2;
-  if (!c->fuse_out) return 8 * c->L + 1;
   // attention fused with its out-projection; the cross q launch folds into
   // the cross attention when that computes its own query rows
   // and one-slot engines run the FFN as one launch

@@ -8,7 +8,6 @@
 
 #include "gemm_tc.cuh"
 #include "logits.cuh"
-#include "persistent.cuh"
 #include "proj.cuh"
 
 namespace s2r {
@@ -17,7 +16,6 @@ typedef void (*ProjFn)(const ProjArgs);
 typedef void (*LogitsFn)(const LogitsArgs);
 typedef void (*GemmFn)(CUtensorMap, CUtensorMap, TcArgs);
 typedef void (*LnFn)(const ProjArgs, bf16*);
-typedef void (*StepFn)(const PArgs);
 
 // CUDA-core projection for in (InMode) x epi (EpiMode), K in kch 256-column
 // chunks, mc rows per pass; nullptr for a combination the engine never runs.
@@ -28,8 +26,6 @@ LogitsFn logits_fn(int kch, int mc);
 GemmFn gemm_fn(int nb, int epi);
 // LayerNorm rows into the tensor-core GEMM's bf16 operand (in: IN_LN or IN_EMBED).
 LnFn ln_fn(int in, int kch);
-// The persistent one-kernel decode step.
-StepFn step_fn(int kch, int mr);
 
 // ---- template pickers shared by the kernels_*.cu translation units
 
@@ -64,21 +60,8 @@ LogitsFn pick_logits_mc(int mc) {
   }
 }
 
-template <int KCH>
-StepFn pick_step_mr(int mr) {
-  switch (mr) {
-    case 1: return step_persistent_kernel<KCH, 1>;
-    case 2: return step_persistent_kernel<KCH, 2>;
-    case 4: return step_persistent_kernel<KCH, 4>;
-    default: return step_persistent_kernel<KCH, 8>;
-  }
-}
-
 // Per-translation-unit parts of the selectors above.
 ProjFn proj_fn_ln(int in, int epi, int kch, int mc);    // kernels_proj_ln.cu: LayerNorm'd inputs
 ProjFn proj_fn_rows(int in, int epi, int kch, int mc);  // kernels_proj_rows.cu: bf16 / f32 rows
-StepFn step_fn_kch1(int mr);                            // kernels_step_1.cu
-StepFn step_fn_kch2(int mr);                            // kernels_step_2.cu
-StepFn step_fn_kch4(int mr);                            // kernels_step_4.cu
 
 }  // namespace s2r

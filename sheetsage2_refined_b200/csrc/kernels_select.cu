@@ -8,12 +8,4 @@ ProjFn proj_fn(int in, int epi, int kch, int mc) {
   return proj_fn_rows(in, epi, kch, mc);
 }
 
-StepFn step_fn(int kch, int mr) {
-  switch (kch) {
-    case 1: return step_fn_kch1(mr);
-    case 2: return step_fn_kch2(mr);
-    default: return step_fn_kch4(mr);
-  }
-}
-
 }  // namespace s2r
