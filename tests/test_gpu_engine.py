@@ -77,7 +77,9 @@ def test_c1_free_running_greedy():
         assert near_tie(ml, tokens[k], ref[k]), k
 
 
-STEP_PATHS = pytest.mark.parametrize("flags", [0, 4], ids=["multi-kernel-step", "one-kernel-step"])
+# the step as a CUDA graph with programmatic dependent launch, and as plain launches
+# (S2R_FLAG_NO_PDL | S2R_FLAG_NO_GRAPH, the mode the profiles are captured in)
+STEP_PATHS = pytest.mark.parametrize("flags", [0, 3], ids=["graph", "plain-launches"])
 
 
 @STEP_PATHS
