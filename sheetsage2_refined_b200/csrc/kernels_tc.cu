@@ -16,8 +16,7 @@ GemmFn pick_gemm(int epi) {
 }
 
 GemmFn gemm_fn(int nb, int epi) {
-  if (epi == EPI_CROSSKV)
-    return nb == 128 ? gemm_tc_kernel<128, EPI_CROSSKV> : nb == 256 ? gemm_tc_kernel<256, EPI_CROSSKV> : nullptr;
+  if (epi == EPI_CROSSKV) return nb == 128 ? gemm_tc_kernel<128, EPI_CROSSKV> : nullptr;
   switch (nb) {
     case 64: return pick_gemm<64>(epi);
     case 128: return pick_gemm<128>(epi);
