@@ -122,20 +122,29 @@ __global__ void __launch_bounds__(kFfnThreads) ffn_row_kernel(const FfnArgs a) {
   }
   __syncthreads();
 
-  // ---- fc1 + GELU: 4 hidden units per warp, the projection kernel's order
+  // ---- fc1 + GELU: 4 hidden units per warp, each in the projection kernel's order (16-byte
+  // pieces in order, then the butterfly); the four units' chains interleaved, and lane u
+  // applies unit u's bias and GELU
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const bf16* wrow = sw1 + (size_t)(warp * 4 + u) * D;
-    float acc = 0.f;
+  for (int c = 0; c < KCH; ++c) {
+    const int cc = c * 256 + lane * 8;
+    const uint4 xv = *reinterpret_cast<const uint4*>(sx + cc);
 #pragma unroll
-    for (int c = 0; c < KCH; ++c) {
-      const int cc = c * 256 + lane * 8;
+    for (int u = 0; u < 4; ++u) {
+      const bf16* wrow = sw1 + (size_t)(warp * 4 + u) * D;
       const uint4 w = cc < D ? *reinterpret_cast<const uint4*>(wrow + cc) : make_uint4(0, 0, 0, 0);
-      acc += dot8(w, *reinterpret_cast<const uint4*>(sx + cc));
+      acc[u] += dot8(w, xv);
     }
-    acc = warp_sum(acc);
-    const float bias = __shfl_sync(0xffffffffu, b1, u);
-    if (lane == 0) sh[warp * 4 + u] = __float2bfloat16_rn(gelu_erf(round_bf16(acc + bias)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+  }
+  if (lane < 4) {
+    const float mine = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+    sh[warp * 4 + lane] = __float2bfloat16_rn(gelu_erf(round_bf16(mine + b1)));
   }
   __syncthreads();
 
