@@ -17,6 +17,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -197,6 +198,7 @@ struct s2r_ctx {
   std::vector<int32_t> h_frames;                          // real frames per slot
   bf16* xln = nullptr;             // [maxM][KP] LayerNorm'd rows, the X operand of LN'd projections
   bf16* mem_bf16 = nullptr;        // [F][D] float32 encoder memory rounded to bf16
+  bf16* wckv_all = nullptr;        // [L][2D][D]: every layer's [Wck; Wcv] (layers[l].wckv points into it)
   // profiling: when set, an event is recorded after every launch of a step
   std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 };
@@ -362,13 +364,13 @@ void tc_split(int tiles, int k_tiles, int sms, int* splits, int* per) {
   *splits = sp;
 }
 
-// One projection on tensor cores: the LayerNorm or float32 conversion that
-// produces its bf16 rows (when the input is not bf16 already), then the GEMM
-// with the projection's epilogue.  `lg` is the logits epilogue's state.
+// One step or prefill projection on tensor cores: the LayerNorm that produces
+// its bf16 rows (when the input is not bf16 already), then the GEMM with the
+// projection's epilogue.  `lg` is the logits epilogue's state.
 int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, const LogitsArgs* lg = nullptr) {
-  if (in == IN_ACC) return fail(S2R_ENOTSUP, "accumulated out-projection inputs run on the CUDA-core kernels only");
-  const bool cross = epi == EPI_CROSSKV;
-  const int nb = cross ? 128 : c->tc_nb;
+  if (in != IN_LN && in != IN_EMBED && in != IN_BF16)
+    return fail(S2R_ENOTSUP, "tensor-core projections take LayerNorm'd or bf16 rows (input mode %d)", in);
+  const int nb = c->tc_nb;
   const void* x = a.xin;
   int ldx = a.ldx;
   if (in == IN_LN || in == IN_EMBED) {
@@ -377,18 +379,11 @@ int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, cons
     CK(launch_ex(fn, dim3(a.M), dim3(128), 0, s, next_pdl(c), 0, a, c->xln));
     x = c->xln;
     ldx = kch * 256;
-  } else if (in == IN_F32) {
-    if (a.ldx != a.K || a.K % 8) return fail(S2R_ENOTSUP, "float32 rows must be dense with K a multiple of 8");
-    const size_t n = (size_t)a.M * a.K;
-    f32_to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4 * (size_t)c->num_sms), 256, 0, s>>>(
-        static_cast<const float*>(a.xin), c->mem_bf16, n);
-    CK(cudaGetLastError());
-    x = c->mem_bf16;
   }
   const int n_tiles = (a.N + kTcBlockN - 1) / kTcBlockN, m_tiles = (a.M + nb - 1) / nb;
   const int k_tiles = (a.K + kTcBlockK - 1) / kTcBlockK;
   int splits = 1, per = k_tiles;
-  tc_split(cross ? n_tiles * m_tiles : n_tiles, k_tiles, c->num_sms, &splits, &per);
+  tc_split(n_tiles, k_tiles, c->num_sms, &splits, &per);
   GemmFn fn = gemm_fn(nb, epi);
   if (!fn) return fail(S2R_ENOTSUP, "no tensor-core projection for epilogue %d with %d-row tiles", epi, nb);
   CUtensorMap map_w, map_x;
@@ -407,7 +402,7 @@ int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, cons
 }
 
 int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
-  if (epi == EPI_CROSSKV ? c->tc_cross : c->tc) return launch_proj_tc(c, a, in, epi, s);
+  if (c->tc && epi != EPI_CROSSKV) return launch_proj_tc(c, a, in, epi, s);
   const int kch = kch_for(a.K), mc = mc_for(std::min(a.M, 8));
   ProjFn fn = proj_fn(in, epi, kch, mc);
   if (!fn) return fail(S2R_ENOTSUP, "no projection kernel for in=%d epi=%d", in, epi);
@@ -418,6 +413,42 @@ int launch_proj(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s) {
   const int threads = mc == 1 ? proj_threads<1>() : proj_threads<2>(), warps = threads / 32;
   const int blocks = (a.N + warps - 1) / warps;
   CK(launch_ex(fn, dim3(blocks), dim3(threads), smem, s, next_pdl(c), 0, a));
+  return S2R_OK;
+}
+
+// Cross K/V of one window for every layer (decoder.py:98-116): one
+// persistent tcgen05 launch per group of up to kCkvMaxLayers layers, over the
+// stacked [Wck; Wcv] of the group.  x: the window's frames as bf16 rows [frames, D].
+int launch_crosskv(s2r_ctx* c, const bf16* x, int frames, int slot, cudaStream_t s) {
+  CrossKvFn fn = crosskv_fn();
+  const size_t smem = ckv_smem_bytes(kCkvStages);
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const uint64_t D = c->D;
+  CUtensorMap map_x;
+  TRY(encode_rows(&map_x, x, D, (uint64_t)frames, D * sizeof(bf16), kCkvBlockM));
+  for (int l0 = 0; l0 < c->L; l0 += kCkvMaxLayers) {
+    const int nl = std::min(kCkvMaxLayers, c->L - l0);
+    CUtensorMap map_w;
+    TRY(encode_rows(&map_w, c->wckv_all + (size_t)l0 * 2 * D * D, D, (uint64_t)nl * 2 * D, D * sizeof(bf16),
+                    kCkvBlockN));
+    CrossKvArgs a{};
+    a.frames = frames;
+    a.D = c->D;
+    a.heads = c->H;
+    a.layers = nl;
+    a.frames_cap = c->F;
+    a.slot = slot;
+    a.err = c->dev_error;
+    for (int i = 0; i < nl; ++i) {
+      a.bias[i] = c->layers[l0 + i].bckv;
+      a.k_dst[i] = c->layers[l0 + i].ck;
+      a.v_dst[i] = c->layers[l0 + i].cv;
+    }
+    const long long tiles =
+        (long long)((frames + kCkvBlockM - 1) / kCkvBlockM) * ((nl * 2 * c->D + kCkvBlockN - 1) / kCkvBlockN);
+    const int grid = (int)std::min<long long>(tiles, c->num_sms);
+    CK(launch_ex(fn, dim3(grid), dim3(kCkvThreads), smem, s, next_pdl(c), 0, map_x, map_w, a));
+  }
   return S2R_OK;
 }
 
@@ -1074,6 +1105,9 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   TRYC(upload_f32(c->emb_ln_b, w->embedding_norm_b, D));
   TRYC(upload_bf16(c, c->emb_bf16, w->token_embedding, V * D, stage));
   c->layers.resize(c->L);
+  // the cross key/value weights of every layer, stacked [L * 2D, D], so that one
+  // launch projects a window for all layers
+  TRYC(dalloc(c, &c->wckv_all, (size_t)c->L * 2 * D * D));
   const size_t pool = (size_t)c->n_pages * c->H * kPageTokens * kHeadDim;
   const size_t cross = (size_t)c->B * c->H * c->F * kHeadDim;
   for (int l = 0; l < c->L; ++l) {
@@ -1085,7 +1119,7 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
     TRYC(dalloc(c, &b.bo, D));
     TRYC(dalloc(c, &b.wcq, D * D));
     TRYC(dalloc(c, &b.bcq, D));
-    TRYC(dalloc(c, &b.wckv, 2 * D * D));
+    b.wckv = c->wckv_all + (size_t)l * 2 * D * D;
     TRYC(dalloc(c, &b.bckv, 2 * D));
     TRYC(dalloc(c, &b.wco, D * D));
     TRYC(dalloc(c, &b.bco, D));
@@ -1473,7 +1507,18 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
   // cross K/V of the window (decoder.py:98-116), written straight into the slot
   const size_t elem = memory_dtype == S2R_F32 ? 4 : 2;
   CK(cudaMemcpyAsync(c->mem_stage, memory, (size_t)frames * D * elem, cudaMemcpyDefault, s));
-  for (int l = 0; l < c->L; ++l) {
+  if (c->tc_cross) {
+    const bf16* x = static_cast<const bf16*>(c->mem_stage);
+    if (memory_dtype == S2R_F32) {
+      const size_t n = (size_t)frames * D;
+      f32_to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4 * (size_t)c->num_sms), 256, 0, s>>>(
+          static_cast<const float*>(c->mem_stage), c->mem_bf16, n);
+      CK(cudaGetLastError());
+      x = c->mem_bf16;
+    }
+    TRY(launch_crosskv(c, x, frames, slot, s));
+  }
+  for (int l = 0; l < c->L && !c->tc_cross; ++l) {
     ProjArgs a = proj_base(c);
     a.M = frames;
     a.K = D;
@@ -1696,6 +1741,19 @@ int32_t s2r_get_buffer(s2r_ctx* c, const char* name, void** ptr, int64_t* numel,
       {"cross_k", c->layers[0].ck, B * c->H * c->F * kHeadDim, 1},
       {"cross_v", c->layers[0].cv, B * c->H * c->F * kHeadDim, 1},
   };
+  // "cross_k.<layer>" / "cross_v.<layer>": any layer's cross K/V
+  for (const char* which : {"cross_k.", "cross_v."}) {
+    const size_t n = std::strlen(which);
+    if (std::strncmp(name, which, n) == 0) {
+      char* end = nullptr;
+      const long l = std::strtol(name + n, &end, 10);
+      if (end == name + n || *end != '\0' || l < 0 || l >= c->L) return fail(S2R_EINVAL, "no buffer named '%s'", name);
+      *ptr = which[6] == 'k' ? c->layers[l].ck : c->layers[l].cv;
+      *numel = B * c->H * c->F * kHeadDim;
+      *dtype = 1;
+      return S2R_OK;
+    }
+  }
   for (const Entry& e : table)
     if (std::strcmp(e.name, name) == 0 && e.p != nullptr) {
       *ptr = e.p;

@@ -6,6 +6,7 @@
 
 #include <cuda.h>
 
+#include "crosskv.cuh"
 #include "gemm_tc.cuh"
 #include "logits.cuh"
 #include "proj.cuh"
@@ -16,6 +17,7 @@ typedef void (*ProjFn)(const ProjArgs);
 typedef void (*LogitsFn)(const LogitsArgs);
 typedef void (*GemmFn)(CUtensorMap, CUtensorMap, TcArgs);
 typedef void (*LnFn)(const ProjArgs, bf16*);
+typedef void (*CrossKvFn)(CUtensorMap, CUtensorMap, CrossKvArgs);
 
 // CUDA-core projection for in (InMode) x epi (EpiMode), K in kch 256-column
 // chunks, mc rows per pass; nullptr for a combination the engine never runs.
@@ -26,6 +28,8 @@ LogitsFn logits_fn(int kch, int mc);
 GemmFn gemm_fn(int nb, int epi);
 // LayerNorm rows into the tensor-core GEMM's bf16 operand (in: IN_LN or IN_EMBED).
 LnFn ln_fn(int in, int kch);
+// Cross K/V projection of a window for a group of layers (persistent tcgen05 GEMM).
+CrossKvFn crosskv_fn();
 
 // ---- template pickers shared by the kernels_*.cu translation units
 

@@ -1,4 +1,5 @@
-// Instantiations of the tensor-core GEMM and its LayerNorm pre-pass.
+// Instantiations of the tensor-core GEMM, its LayerNorm pre-pass and the
+// all-layer cross K/V projection.
 #include "kernels.h"
 
 namespace s2r {
@@ -16,7 +17,6 @@ GemmFn pick_gemm(int epi) {
 }
 
 GemmFn gemm_fn(int nb, int epi) {
-  if (epi == EPI_CROSSKV) return nb == 128 ? gemm_tc_kernel<128, EPI_CROSSKV> : nullptr;
   switch (nb) {
     case 64: return pick_gemm<64>(epi);
     case 128: return pick_gemm<128>(epi);
@@ -36,6 +36,8 @@ LnFn pick_ln(int kch) {
     default: return ln_rows_kernel<16, IN>;
   }
 }
+
+CrossKvFn crosskv_fn() { return crosskv_kernel<kCkvStages>; }
 
 LnFn ln_fn(int in, int kch) { return in == IN_EMBED ? pick_ln<IN_EMBED>(kch) : pick_ln<IN_LN>(kch); }
 
