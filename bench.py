@@ -65,6 +65,8 @@ CONFIG = DecoderConfig(vocab_size=2048, width=1024, layers=12, heads=16, ffn_wid
 REAL = DecoderConfig(vocab_size=32576, width=512, layers=6, heads=8, ffn_width=2048, max_tokens=5120)
 WEIGHT_SEED, MEMORY_SEED, GRAMMAR_SEED, REAL_SEED = 1, 101, 8, 6
 SINGLE_FRAMES, SINGLE_TOKENS = 1500, 2048
+PREFILL_LENGTHS = (512, 2048)  # prefix lengths of the load timings (overlap-primed windows)
+PREFIX_SEED = 23
 BATCH, BATCH_FRAMES = 64, 3000
 SONGS, SONGS_SEED = 512, 2024
 REAL_FRAMES, REAL_B1_TOKENS = 7500, 512
@@ -294,27 +296,27 @@ def run_reference(args, world, rank):
 
 # ---------------------------------------------------------------- GPU arm: workloads
 def load_launches(eng, layers: int, prefix_len: int = 2) -> int:
-    """Kernel launches of one ``load`` of a [SOS, OUT]-style prefix.
+    """Kernel launches of one ``load`` of a bfloat16 window and a prefix of ``prefix_len`` tokens.
 
-    The cross K/V projection (one launch per layer), then the prefill of the
-    prefix positions before the last (one chunk for short prefixes): a full
-    layer but only the K/V projection in the last one (5 or 6 launches per
-    layer on the CUDA-core path, 11 on tensor-core engines); the one-kernel
-    step engine prefills with one launch.  One-slot engines decode with a
-    fused FFN (4 launches per layer) but prefill with fc1 and fc2 (5).
+    The cross K/V projection (one launch for up to 32 layers), then the prefill
+    of the prefix positions before the last in chunks of 64 rows: each chunk a
+    full layer but only the K/V projection in the last one (5 or 6 launches per
+    layer on the CUDA-core path, 11 on tensor-core engines).  One-slot engines
+    decode with a fused FFN (4 launches per layer) but prefill with fc1 and
+    fc2 (5).
     """
 
     L, per_step = layers, eng.step_launches
-    if prefix_len <= 1:
-        return L
-    if per_step == 1:
-        return L + 1
+    cross = (L + 31) // 32
+    chunks = (prefix_len - 1 + 63) // 64
+    if chunks <= 0:
+        return cross
     if per_step == 11 * L + 2:
-        return L + 11 * (L - 1) + 2
+        return cross + chunks * (11 * (L - 1) + 2)
     per_layer = (per_step - 1) // L
     if per_layer == 4:  # fused FFN in decode only
         per_layer = 5
-    return L + per_layer * (L - 1) + 1
+    return cross + chunks * (per_layer * (L - 1) + 1)
 
 
 class SingleSong:
@@ -373,10 +375,27 @@ class SingleSong:
             torch.cuda.synchronize(self.device)
             ms.append(start.elapsed_time(end))
         flop = 2.0 * SINGLE_FRAMES * CONFIG.width * 2 * CONFIG.width * CONFIG.layers
-        return {"ms": statistics.median(ms), "loads": k, "frames": SINGLE_FRAMES, "prefix_tokens": 2,
+        info = {"ms": statistics.median(ms), "loads": k, "frames": SINGLE_FRAMES, "prefix_tokens": 2,
                 "cross_kv_gflop": flop / 1e9,
-                "what": "one window's load: memory copy, cross K/V projection of every layer on the tcgen05 GEMM, "
+                "what": "one window's load: memory copy, cross K/V projection of every layer in one tcgen05 launch, "
                         "slot state, prefill of position 0"}
+        # a window primed with the overlap of the window before it (transcribe.overlap_prefix): the
+        # prefix's K/V are prefilled at load
+        rng = np.random.default_rng(PREFIX_SEED)
+        for n in PREFILL_LENGTHS:
+            prefix = [SOS, OUT] + rng.integers(4, CONFIG.vocab_size, n - 2).tolist()
+            ms = []
+            for _ in range(3):
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                self.eng.load(0, self.mem_dev, prefix, None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+                end.record(stream)
+                torch.cuda.synchronize(self.device)
+                ms.append(start.elapsed_time(end))
+            t = statistics.median(ms)
+            info.setdefault("prefill", []).append(
+                {"prefix_tokens": n, "load_ms": t, "prefill_us_per_token": 1000.0 * (t - info["ms"]) / (n - 1)})
+        return info
 
     def prepare_profile(self):
         self.eng.load(0, self.mem_dev, [SOS, OUT], None, SINGLE_FRAMES, target=SINGLE_TOKENS)

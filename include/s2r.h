@@ -70,8 +70,9 @@ typedef struct s2r_config {
 #define S2R_FLAG_NO_GRAPH 2u /* issue steps as plain launches, no CUDA graph */
 /* 4u, 8u, 16u: not flags (s2r_create rejects any bit but these three) */
 #define S2R_FLAG_NO_TENSOR_CORE 32u /* every projection on the CUDA-core kernel (by default the cross K/V
-                                       projection at load, and with batch >= 16 the step and prefill
-                                       projections, run on tcgen05 tensor cores) */
+                                       projection at load, prefill chunks of more than 8 rows, and
+                                       with batch >= 16 the step projections run on tcgen05 tensor
+                                       cores) */
 
 /* One decoder layer's float32 parameters, named as in
  * TokenDecoder.state_dict() (decoder.py:28-84).  Linear weights are

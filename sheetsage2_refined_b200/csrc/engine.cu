@@ -57,6 +57,11 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 constexpr int kPrefillRows = 64;
+// Prefill chunks of at most this many rows run on the engine's decode kernels (for engines
+// below 16 slots: the CUDA-core kernels, one pass over the weights for up to 8 rows, and the
+// same arithmetic as a decode step, so a short prefix gives bit-identical K/V to forcing it
+// token by token); longer chunks run on tensor cores.
+constexpr int kFusedPrefillMaxRows = 8;
 
 int kch_for(int k) { return k <= 256 ? 1 : k <= 512 ? 2 : k <= 1024 ? 4 : k <= 2048 ? 8 : 16; }
 int mc_for(int m) { return m >= 5 ? 8 : m >= 3 ? 4 : m; }
@@ -180,6 +185,10 @@ struct s2r_ctx {
   // tensor-core projections (tcgen05 GEMM): the step and prefill projections
   // when `tc` (16 or more slots), the cross K/V projection at load when `tc_cross`
   bool tc = false, tc_cross = false;
+  // engines below 16 slots decode on the CUDA-core kernels but run prefill chunks of more
+  // than kFusedPrefillMaxRows rows through the tensor-core layer (load_slot switches the
+  // engine to it for those chunks: PrefillOnTensorCores)
+  bool tc_prefill = false;
   int tc_nb = 64;                  // rows per MMA tile of the step and prefill projections
   // engines below 16 slots fuse each attention with its out-projection (fixed-point sums in
   // acc_self / acc_cross); the next launch adds bias and residual and normalises (IN_ACC)
@@ -845,6 +854,31 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
   return S2R_OK;
 }
 
+// For the lifetime of this object, an engine whose decode runs on the CUDA-core
+// kernels (fused attention and out-projection, fixed-point sums) enqueues layers
+// as a tensor-core engine does: LayerNorm pre-pass and tcgen05 GEMMs for every
+// projection, attention rows without the fused out-projection, float32
+// residual rows.  Used for prefill chunks of many rows, whose projections are
+// dense GEMMs; the fixed-point accumulators of the decode path are not touched,
+// and no buffer the decode path keeps across steps is written.
+struct PrefillOnTensorCores {
+  s2r_ctx* c;
+  bool on, tc, fuse_out, fuse_ffn;
+  PrefillOnTensorCores(s2r_ctx* ctx, bool enable)
+      : c(ctx), on(enable), tc(ctx->tc), fuse_out(ctx->fuse_out), fuse_ffn(ctx->fuse_ffn) {
+    if (!on) return;
+    c->tc = true;
+    c->fuse_out = false;
+    c->fuse_ffn = false;
+  }
+  ~PrefillOnTensorCores() {
+    if (!on) return;
+    c->tc = tc;
+    c->fuse_out = fuse_out;
+    c->fuse_ffn = fuse_ffn;
+  }
+};
+
 int enqueue_step(s2r_ctx* c, cudaStream_t s, const int64_t* forced, float* logits, int64_t* greedy) {
   RowMap rm{0, 0, 0, nullptr};
   c->fence_next = true;
@@ -980,9 +1014,10 @@ int setup_tensor_core(s2r_ctx* c) {
   if (allowed && !tensor_map_encoder()) return fail(S2R_ECUDA, "the driver has no cuTensorMapEncodeTiled");
   c->tc_cross = allowed;
   c->tc = allowed && c->B >= kTcMinBatch && c->D >= kTcBlockN;
+  c->tc_prefill = allowed && !c->tc && c->D >= kTcBlockN;
   c->tc_nb = c->maxM <= 64 ? 64 : c->maxM <= 128 ? 128 : 256;
   if (!allowed) return S2R_OK;
-  if (c->tc) {
+  if (c->tc || c->tc_prefill) {
     TRY(dalloc(c, &c->xln, (size_t)c->maxM * kch_for(c->D) * 256));
     CK(cudaMemset(c->xln, 0, (size_t)c->maxM * kch_for(c->D) * 256 * sizeof(bf16)));
   }
@@ -1541,6 +1576,7 @@ int32_t s2r_load_slot(s2r_ctx* c, int32_t slot, const void* memory, int32_t memo
     CK(cudaMemcpyAsync(dst, toks.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     RowMap rm{1, slot, p0, dst};
     c->fence_next = true;
+    PrefillOnTensorCores mode(c, c->tc_prefill && rows > kFusedPrefillMaxRows);
     for (int l = 0; l < c->L; ++l) TRY(enqueue_layer(c, rm, rows, l, l == c->L - 1, s));
   }
   CK(cudaGetLastError());

@@ -173,4 +173,22 @@ def teacher_forced_compare(engine, oracle, tokens, prefix_len, steps, slot=0):
     return max_diff, max_err, within / count, same / steps, mismatches
 
 
+def prefill_compare(la: np.ndarray, lb: np.ndarray, ga: int, gb: int, exact: bool, what) -> None:
+    """A decode step after a prefilled prefix (``la``, ``ga``) against the same step after the prefix
+    was forced token by token (``lb``, ``gb``).
+
+    ``exact``: the prefill ran on the decode step's kernels, so logits and choice are bit-identical.
+    Otherwise the prefill ran on tensor cores (float32 sums in another order than the decode step's):
+    logits within the parity tolerance, and a different choice only at a near-tie.
+    """
+
+    if exact:
+        assert np.array_equal(la, lb) and ga == gb, what
+        return
+    assert logit_error(la, lb) <= 1.0, (what, float(np.abs(la - lb).max()))
+    w, n = logit_within(la, lb)
+    assert w / n >= LOGIT_WITHIN_FRACTION, (what, w, n)
+    assert ga == gb or near_tie(la, int(ga), int(gb)), (what, ga, gb)
+
+
 __all__ = ["sc"]

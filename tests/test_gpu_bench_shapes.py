@@ -26,7 +26,7 @@ import torch
 
 import scenarios as sc
 from helpers import (LOGIT_WITHIN_FRACTION, TOKEN_AGREEMENT, cuda_engine, logit_error, logit_within, loader, masked,
-                     near_tie, oracle_engine)
+                     near_tie, oracle_engine, prefill_compare)
 from sheetsage2_refined_b200.grammar import TableGrammar
 from sheetsage2_refined_b200.vocab_table import OUT, SOS
 from sheetsage2_refined_b200.weights import DecoderConfig
@@ -124,11 +124,13 @@ def test_single_song_long_rows_vs_oracle_bf16():
     check("batch 1, 5050 positions", forced_compare(eng, ora, [0], 8, rng, WIDE.vocab_size))
 
 
-@pytest.mark.parametrize("batch", [1, 16], ids=["cuda-core", "tensor-core"])
+@pytest.mark.parametrize("batch", [1, 16], ids=["one-slot", "tensor-core"])
 def test_wide_prefill_equals_token_by_token(batch):
-    """At the benchmark's width (d1024, K up to 4096) a 150-token prefix prefilled in chunks gives
-    bit-identical logits to forcing it one token at a time: every LayerNorm normalises in one fixed
-    order whatever kernel stages it, and the out-projection sums do not depend on arrival order."""
+    """At the benchmark's width (d1024, K up to 4096) a 150-token prefix prefilled in chunks against
+    forcing it one token at a time.  A 16-slot engine prefills and decodes on the same tensor-core
+    kernels: bit-identical logits (every LayerNorm normalises in one fixed order whatever kernel stages
+    it).  A one-slot engine decodes on the CUDA-core kernels but prefills chunks of 64 rows on tensor
+    cores: the same logits within the parity tolerance."""
 
     rng = np.random.default_rng(11)
     seq = [SOS, OUT] + rng.integers(4, WIDE.vocab_size, 160).tolist()
@@ -145,4 +147,4 @@ def test_wide_prefill_equals_token_by_token(batch):
         forced[slot] = seq[152 + k]
         la, ga = a.step_debug(forced)
         lb, gb = b.step_debug(forced)
-        assert np.array_equal(la[slot], lb[slot]) and ga[slot] == gb[slot], k
+        prefill_compare(la[slot], lb[slot], ga[slot], gb[slot], batch >= 16, k)

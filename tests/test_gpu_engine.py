@@ -17,7 +17,8 @@ import torch
 
 import scenarios as sc
 from helpers import (LOGIT_WITHIN_FRACTION, TOKEN_AGREEMENT, cuda_engine, logit_error, logit_within, loader,
-                     masked, masked_logits_at, near_tie, oracle_engine, teacher_forced_compare, window_agreement)
+                     masked, masked_logits_at, near_tie, oracle_engine, prefill_compare, teacher_forced_compare,
+                     window_agreement)
 from oracle.grammar import TableGrammarOracle
 from sheetsage2_refined_b200.grammar import ClassGrammar
 from sheetsage2_refined_b200.vocab_table import NO_KEY, OUT, SOS, VocabTable
@@ -258,23 +259,33 @@ def test_continuous_batch_vs_oracle_bf16(flags):
     assert same / total >= TOKEN_AGREEMENT
 
 
-@STEP_PATHS
-def test_prefill_equals_token_by_token(flags):
-    """A 150-token prefix (several prefill chunks) gives bit-identical K/V to forcing it one token at a time."""
+NO_TC = 32  # S2R_FLAG_NO_TENSOR_CORE
+
+
+@pytest.mark.parametrize("flags,n,exact", [
+    (0, 9, True), (3, 9, True),                # 8 prefix rows: the decode kernels
+    (NO_TC, 152, True), (NO_TC | 3, 152, True),  # every chunk on the CUDA-core decode kernels
+    (0, 152, False), (3, 152, False),          # chunks of 64 and 23 rows on tensor cores
+], ids=["short-graph", "short-plain", "cuda-core-graph", "cuda-core-plain", "tensor-core-graph",
+        "tensor-core-plain"])
+def test_prefill_equals_token_by_token(flags, n, exact):
+    """A prefilled prefix against forcing it one token at a time.  Prefill chunks of up to 8 rows (and
+    every chunk without tensor cores) run on the decode step's kernels: bit-identical K/V.  Longer chunks
+    run on tensor cores: the same values within the parity tolerance."""
 
     rng = np.random.default_rng(11)
     grammar = sc.c1_grammar()
     seq = [SOS, OUT] + rng.integers(4, sc.C1.vocab_size, 160).tolist()
     a = cuda_engine(sc.C1, sc.C1_SEED, grammar, 1, sc.C1_FRAMES, flags=flags)
     b = cuda_engine(sc.C1, sc.C1_SEED, grammar, 1, sc.C1_FRAMES, flags=flags)
-    loader(a, sc.C1.width, sc.C1_FRAMES)(0, 3, seq[:152], None, 200, 10_000)
+    loader(a, sc.C1.width, sc.C1_FRAMES)(0, 3, seq[:n], None, 200, 10_000)
     loader(b, sc.C1.width, sc.C1_FRAMES)(0, 3, seq[:2], None, 200, 10_000)
-    for k in range(150):
+    for k in range(n - 2):
         b.step_debug(np.array([seq[2 + k]]), want_logits=False)
     for k in range(8):
-        la, ga = a.step_debug(np.array([seq[152 + k]]))
-        lb, gb = b.step_debug(np.array([seq[152 + k]]))
-        assert np.array_equal(la, lb) and ga[0] == gb[0], k
+        la, ga = a.step_debug(np.array([seq[n + k]]))
+        lb, gb = b.step_debug(np.array([seq[n + k]]))
+        prefill_compare(la[0], lb[0], ga[0], gb[0], exact, k)
 
 
 @STEP_PATHS
