@@ -299,24 +299,27 @@ def load_launches(eng, layers: int, prefix_len: int = 2) -> int:
     """Kernel launches of one ``load`` of a bfloat16 window and a prefix of ``prefix_len`` tokens.
 
     The cross K/V projection (one launch for up to 32 layers), then the prefill
-    of the prefix positions before the last in chunks of 64 rows: each chunk a
-    full layer but only the K/V projection in the last one (5 or 6 launches per
-    layer on the CUDA-core path, 11 on tensor-core engines).  One-slot engines
-    decode with a fused FFN (4 launches per layer) but prefill with fc1 and
-    fc2 (5).
+    of the prefix positions before the last in chunks of 128 rows: each chunk
+    a full layer but only the K/V projection in the last one.  Chunks of more
+    than 8 rows (and every chunk of a tensor-core engine) run the tensor-core
+    layer, 11 launches; shorter ones the engine's CUDA-core decode kernels (5
+    or 6 a layer; one-slot engines decode with a fused FFN, 4 launches a
+    layer, but prefill with fc1 and fc2, 5).
     """
 
     L, per_step = layers, eng.step_launches
-    cross = (L + 31) // 32
-    chunks = (prefix_len - 1 + 63) // 64
-    if chunks <= 0:
-        return cross
-    if per_step == 11 * L + 2:
-        return cross + chunks * (11 * (L - 1) + 2)
+    n = (L + 31) // 32
+    rows = max(0, prefix_len - 1)
+    chunks = [128] * (rows // 128) + ([rows % 128] if rows % 128 else [])
     per_layer = (per_step - 1) // L
     if per_layer == 4:  # fused FFN in decode only
         per_layer = 5
-    return cross + chunks * (per_layer * (L - 1) + 1)
+    for r in chunks:
+        if per_step == 11 * L + 2 or r > 8:
+            n += 11 * (L - 1) + 2
+        else:
+            n += per_layer * (L - 1) + 1
+    return n
 
 
 class SingleSong:

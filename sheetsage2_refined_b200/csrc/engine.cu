@@ -56,7 +56,7 @@ int fail(int code, const char* fmt, ...) {
     if (err_ != cudaSuccess) return fail(S2R_ECUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(err_), __FILE__, __LINE__); \
   } while (0)
 
-constexpr int kPrefillRows = 64;
+constexpr int kPrefillRows = kPfRows;  // positions per prefill chunk (128: one tensor-core attention tile)
 // Prefill chunks of at most this many rows run on the engine's decode kernels (for engines
 // below 16 slots: the CUDA-core kernels, one pass over the weights for up to 8 rows, and the
 // same arithmetic as a decode step, so a short prefix gives bit-identical K/V to forcing it
@@ -635,6 +635,44 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   return S2R_OK;
 }
 
+// Attention of a prefill chunk on tensor cores (prefill_attn.cuh): the chunk's
+// M rows (positions pos0 .. pos0 + M - 1 of one slot) of every head against
+// the slot's keys, key tiles split over a cluster of up to 8 CTAs per head.
+int launch_prefill_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_t s) {
+  if (M > kPfRows) return fail(S2R_EINVAL, "a prefill chunk holds at most %d rows", kPfRows);
+  const int n_max = cross ? c->h_frames[rm.slot] : rm.pos0 + M;
+  const int tiles = (n_max + kPfKeys - 1) / kPfKeys;
+  int splits = std::min(kPfMaxSplits, std::max(1, (tiles + 3) / 4));  // at least 4 key tiles a CTA
+  const int per = (tiles + splits - 1) / splits;
+  splits = (tiles + per - 1) / per;  // no CTA without keys
+  const LayerBufs& w = c->layers[layer];
+  CUtensorMap map_q, map_k, map_v;
+  TRY(encode_rows(&map_q, c->q, c->D, (uint64_t)M, (uint64_t)c->D * sizeof(bf16), kPfRows));
+  const uint64_t key_rows = cross ? (uint64_t)c->B * c->H * c->F : (uint64_t)c->n_pages * c->H * kPageTokens;
+  TRY(encode_rows(&map_k, cross ? w.ck : w.kpool, kHeadDim, key_rows, kHeadDim * sizeof(bf16), kPfKeys));
+  TRY(encode_rows(&map_v, cross ? w.cv : w.vpool, kHeadDim, key_rows, kHeadDim * sizeof(bf16), kPfKeys));
+  PrefillAttnArgs a{};
+  a.rows = M;
+  a.pos0 = rm.pos0;
+  a.slot = rm.slot;
+  a.cross = cross;
+  a.H = c->H;
+  a.D = c->D;
+  a.pages_per_slot = c->pps;
+  a.frames_cap = c->F;
+  a.tiles = tiles;
+  a.per = per;
+  a.page_table = c->st.page_table;
+  a.frames = c->st.frames;
+  a.out = c->att;
+  a.err = c->dev_error;
+  PrefillAttnFn fn = prefill_attn_fn();
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PfSmem::total));
+  CK(launch_ex(fn, dim3(splits, c->H), dim3(kPfThreads), PfSmem::total, s, next_pdl(c), splits > 1 ? splits : 0, map_q,
+               map_k, map_v, a));
+  return S2R_OK;
+}
+
 // One decoder layer for M rows.  `last_kv_only`: only the K/V append (the
 // prefill's last layer needs nothing else).
 int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaStream_t s) {
@@ -760,7 +798,10 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
       TRY(mark(c, K_FC1, s));
     }
   } else {
-  TRY(launch_attn(c, rm, M, l, false, s));  // 2. self-attention
+  // 2. self-attention (prefill chunks of more than kFusedPrefillMaxRows rows: all rows of a head
+  // in one tensor-core tile; shorter ones, like decode rows, one cluster per row and head)
+  const bool pf_tile = rm.prefill && M > kFusedPrefillMaxRows;
+  TRY(pf_tile ? launch_prefill_attn(c, rm, M, l, false, s) : launch_attn(c, rm, M, l, false, s));
   TRY(mark(c, K_SELF_ATTN, s));
   {                                         // 3. out-projection + residual
     ProjArgs a = proj_base(c);
@@ -794,7 +835,7 @@ int enqueue_layer(s2r_ctx* c, RowMap rm, int M, int l, bool last_kv_only, cudaSt
     TRY(launch_proj(c, a, IN_LN, EPI_BF16, s));
     TRY(mark(c, K_CROSS_Q, s));
   }
-  TRY(launch_attn(c, rm, M, l, true, s));  // 5. cross-attention
+  TRY(pf_tile ? launch_prefill_attn(c, rm, M, l, true, s) : launch_attn(c, rm, M, l, true, s));  // 5. cross-attention
   TRY(mark(c, K_CROSS_ATTN, s));
   {                                        // 6. cross out-projection + residual
     ProjArgs a = proj_base(c);
@@ -1015,7 +1056,7 @@ int setup_tensor_core(s2r_ctx* c) {
   c->tc_cross = allowed;
   c->tc = allowed && c->B >= kTcMinBatch && c->D >= kTcBlockN;
   c->tc_prefill = allowed && !c->tc && c->D >= kTcBlockN;
-  c->tc_nb = c->maxM <= 64 ? 64 : c->maxM <= 128 ? 128 : 256;
+  c->tc_nb = c->B <= 64 ? 64 : c->B <= 128 ? 128 : 256;  // prefill chunks of more rows take several row tiles
   if (!allowed) return S2R_OK;
   if (c->tc || c->tc_prefill) {
     TRY(dalloc(c, &c->xln, (size_t)c->maxM * kch_for(c->D) * 256));
@@ -1043,6 +1084,7 @@ int check_device_error(s2r_ctx* c, cudaStream_t s) {
               : err == kErrAttnStage ? "a bulk copy of the attention kernel did not complete in time"
               : err == kErrAttnExchange ? "a value sent between attention CTAs did not arrive in time"
               : err == kErrGemmWait  ? "a wait of the tensor-core projection timed out"
+              : err == kErrPrefillWait ? "a wait of the prefill attention timed out"
               : err == kErrFfnStage  ? "a bulk copy of the fused FFN did not complete in time"
               : err == kErrAccRange  ? "an out-projection partial was too large (or NaN) for the fixed-point sum"
                                      : "unknown code");

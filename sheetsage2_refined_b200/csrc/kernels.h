@@ -9,6 +9,7 @@
 #include "crosskv.cuh"
 #include "gemm_tc.cuh"
 #include "logits.cuh"
+#include "prefill_attn.cuh"
 #include "proj.cuh"
 
 namespace s2r {
@@ -18,6 +19,7 @@ typedef void (*LogitsFn)(const LogitsArgs);
 typedef void (*GemmFn)(CUtensorMap, CUtensorMap, TcArgs);
 typedef void (*LnFn)(const ProjArgs, bf16*);
 typedef void (*CrossKvFn)(CUtensorMap, CUtensorMap, CrossKvArgs);
+typedef void (*PrefillAttnFn)(CUtensorMap, CUtensorMap, CUtensorMap, PrefillAttnArgs);
 
 // CUDA-core projection for in (InMode) x epi (EpiMode), K in kch 256-column
 // chunks, mc rows per pass; nullptr for a combination the engine never runs.
@@ -30,6 +32,8 @@ GemmFn gemm_fn(int nb, int epi);
 LnFn ln_fn(int in, int kch);
 // Cross K/V projection of a window for a group of layers (persistent tcgen05 GEMM).
 CrossKvFn crosskv_fn();
+// Attention of a prefill chunk (tcgen05, online softmax, cluster split over the keys).
+PrefillAttnFn prefill_attn_fn();
 
 // ---- template pickers shared by the kernels_*.cu translation units
 

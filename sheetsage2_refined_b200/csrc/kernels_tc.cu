@@ -1,5 +1,5 @@
-// Instantiations of the tensor-core GEMM, its LayerNorm pre-pass and the
-// all-layer cross K/V projection.
+// Instantiations of the tensor-core GEMM, its LayerNorm pre-pass, the
+// all-layer cross K/V projection and the prefill attention.
 #include "kernels.h"
 
 namespace s2r {
@@ -38,6 +38,8 @@ LnFn pick_ln(int kch) {
 }
 
 CrossKvFn crosskv_fn() { return crosskv_kernel<kCkvStages>; }
+
+PrefillAttnFn prefill_attn_fn() { return prefill_attn_kernel<0>; }
 
 LnFn ln_fn(int in, int kch) { return in == IN_EMBED ? pick_ln<IN_EMBED>(kch) : pick_ln<IN_LN>(kch); }
 

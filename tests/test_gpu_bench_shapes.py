@@ -126,11 +126,10 @@ def test_single_song_long_rows_vs_oracle_bf16():
 
 @pytest.mark.parametrize("batch", [1, 16], ids=["one-slot", "tensor-core"])
 def test_wide_prefill_equals_token_by_token(batch):
-    """At the benchmark's width (d1024, K up to 4096) a 150-token prefix prefilled in chunks against
-    forcing it one token at a time.  A 16-slot engine prefills and decodes on the same tensor-core
-    kernels: bit-identical logits (every LayerNorm normalises in one fixed order whatever kernel stages
-    it).  A one-slot engine decodes on the CUDA-core kernels but prefills chunks of 64 rows on tensor
-    cores: the same logits within the parity tolerance."""
+    """At the benchmark's width (d1024, K up to 4096) a 150-token prefix prefilled in chunks (128 and
+    21 rows, on tensor cores: projections and the prefill attention) against forcing it one token at a
+    time on the decode kernels: the same logits within the parity tolerance, a different choice only
+    at a near-tie."""
 
     rng = np.random.default_rng(11)
     seq = [SOS, OUT] + rng.integers(4, WIDE.vocab_size, 160).tolist()
@@ -147,4 +146,4 @@ def test_wide_prefill_equals_token_by_token(batch):
         forced[slot] = seq[152 + k]
         la, ga = a.step_debug(forced)
         lb, gb = b.step_debug(forced)
-        prefill_compare(la[slot], lb[slot], ga[slot], gb[slot], batch >= 16, k)
+        prefill_compare(la[slot], lb[slot], ga[slot], gb[slot], False, k)
