@@ -379,6 +379,8 @@ void tc_split(int tiles, int k_tiles, int sms, int* splits, int* per) {
 int launch_proj_tc(s2r_ctx* c, ProjArgs a, int in, int epi, cudaStream_t s, const LogitsArgs* lg = nullptr) {
   if (in != IN_LN && in != IN_EMBED && in != IN_BF16)
     return fail(S2R_ENOTSUP, "tensor-core projections take LayerNorm'd or bf16 rows (input mode %d)", in);
+  // prefill chunks of more rows than a decode tile take several row tiles (128-row tiles for
+  // 128-row chunks measured slower: one CTA an SM)
   const int nb = c->tc_nb;
   const void* x = a.xin;
   int ldx = a.ldx;
