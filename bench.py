@@ -1020,6 +1020,38 @@ def reference_gpu(torch, device, seconds: float = 20.0):
     return out
 
 
+def run_prefill(args):
+    """One GPU: ``load`` of a single-song window (12L d1024, 1,500 frames, memory on the device)
+    with an ``args.prefill``-token prefix, timed with CUDA events (the case the prefill profiles
+    capture)."""
+
+    import torch
+
+    from sheetsage2_refined_b200 import BatchDecoder
+    from sheetsage2_refined_b200.weights import memory_array
+
+    device = torch.device("cuda", 0)
+    flags = int(os.environ.get("S2R_ENGINE_FLAGS", "0"))
+    dec = DecoderWeights(CONFIG, synthetic_state_dict(CONFIG, WEIGHT_SEED))
+    eng = BatchDecoder(dec, None, batch=1, frames=SINGLE_FRAMES, grammar=c2_grammar(), device=device, flags=flags)
+    mem = torch.from_numpy(memory_array(SINGLE_FRAMES, CONFIG.width, MEMORY_SEED)).to(torch.bfloat16).to(device)
+    n = args.prefill
+    prefix = [SOS, OUT] + np.random.default_rng(PREFIX_SEED).integers(4, CONFIG.vocab_size, n - 2).tolist()
+    for _ in range(args.warmup):
+        eng.load(0, mem, prefix, None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        eng.load(0, mem, prefix, None, SINGLE_FRAMES, target=SINGLE_TOKENS)
+    end.record()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / max(1, args.steps)
+    print(json.dumps({"case": "prefill", "prefix_tokens": n, "ms_per_load": ms,
+                      "prefill_tokens_per_s": (n - 1) / (ms / 1000.0), "flags": flags}))
+    eng.close()
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -1129,6 +1161,9 @@ def main():
     ap.add_argument("--layers", type=int, default=None, help="override the decoder depth (profiling cases)")
     ap.add_argument("--max-tokens", type=int, default=None, help="override the context length (profiling cases)")
     ap.add_argument("--batch-frames", type=int, default=None, help="override the batched frames cap (profiling cases)")
+    ap.add_argument("--prefill", type=int, default=None, metavar="TOKENS",
+                    help="profiling case: only `load` a single-song window with a prefix of TOKENS tokens, "
+                         "--warmup + --steps times, and print its prefill rate (not a bench line)")
     args = ap.parse_args()
     global CONFIG, REAL, BATCH_FRAMES, OVERRIDES
     if args.layers or args.max_tokens:
@@ -1140,6 +1175,9 @@ def main():
         BATCH_FRAMES = args.batch_frames
         OVERRIDES.update(batch_frames=BATCH_FRAMES)
     world, rank, local = dist_env()
+    if args.prefill:
+        run_prefill(args)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
     else:

@@ -291,12 +291,20 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const __grid_con
   const int D = a.D;
   const int stride = gridDim.x * NW;
   const int first = blockIdx.x * NW + warp;
+  // Embedding rows a warp keeps in flight: narrow rows (D <= 512) of a large vocabulary leave a
+  // warp ~14 rows of 1 KB, so it loads U of them before the first dot product; wide rows leave
+  // it about one.
+  constexpr int U = (KCH <= 2 && MC == 1) ? 4 : 1;
 
-  uint4 w[KCH];
+  uint4 w[U][KCH];
 #pragma unroll
-  for (int c = 0; c < KCH; ++c) {
-    const int col = c * 256 + lane * 8;
-    w[c] = (first < a.V && col < D) ? ld_stream(a.emb + (size_t)first * D + col) : make_uint4(0, 0, 0, 0);
+  for (int u = 0; u < U; ++u) {
+    const int v = first + u * stride;
+#pragma unroll
+    for (int c = 0; c < KCH; ++c) {
+      const int col = c * 256 + lane * 8;
+      w[u][c] = (v < a.V && col < D) ? ld_stream(a.emb + (size_t)v * D + col) : make_uint4(0, 0, 0, 0);
+    }
   }
   if (threadIdx.x == 0) l2_ahead(a.ahead, blockIdx.x, gridDim.x);
   pdl_launch_dependents();
@@ -340,32 +348,43 @@ __global__ void __launch_bounds__(kLogitsThreads) logits_kernel(const __grid_con
     unsigned long long best[MC];
 #pragma unroll
     for (int i = 0; i < MC; ++i) best[i] = 0ull;
-    for (int v = first; v < a.V; v += stride) {
-      if (v != first || m0 > 0) {
+    // rows v0 + u * stride, u < U, of this warp per pass (a row's arithmetic does not depend on U)
+    for (int v0 = first; v0 < a.V; v0 += U * stride) {
+      if (v0 != first || m0 > 0) {
 #pragma unroll
-        for (int c = 0; c < KCH; ++c) {
-          const int col = c * 256 + lane * 8;
-          w[c] = col < D ? ld_stream(a.emb + (size_t)v * D + col) : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < U; ++u) {
+          const int v = v0 + u * stride;
+#pragma unroll
+          for (int c = 0; c < KCH; ++c) {
+            const int col = c * 256 + lane * 8;
+            w[u][c] = (v < a.V && col < D) ? ld_stream(a.emb + (size_t)v * D + col) : make_uint4(0, 0, 0, 0);
+          }
         }
       }
-      const float bias = a.bias ? a.bias[v] : 0.f;
-      const int cls = a.gr.kind == 1 ? 0 : a.gr.token_class[v];
-      const bool rescored = rescored_token(a.rs, v);
 #pragma unroll
-      for (int i = 0; i < MC; ++i) {
-        float acc = 0.f;
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * stride;
+        if (U > 1 && v >= a.V) break;  // uniform across the warp (with U = 1 the loop bound checks it)
+        const float bias = a.bias ? a.bias[v] : 0.f;
+        const int cls = a.gr.kind == 1 ? 0 : a.gr.token_class[v];
+        const bool rescored = rescored_token(a.rs, v);
 #pragma unroll
-        for (int c = 0; c < KCH; ++c)
-          acc += dot8(w[c], *reinterpret_cast<const uint4*>(xs + (size_t)i * KP + c * 256 + lane * 8));
-        acc = warp_sum(acc);
-        if (i < mc) {
-          const float logit = round_bf16(acc);
-          if (a.logits_out && lane == 0) a.logits_out[(size_t)(m0 + i) * a.V + v] = logit;
-          const bool ok = a.gr.kind == 1 ? a.gr.table[(size_t)rule[i] * a.V + v] != 0 : ((rule[i] >> cls) & 1u) != 0;
-          if (ok) {
-            const float x = rescored ? rescore_logit_call(a.rs, rrow[i], m0 + i, v, logit + bias) : logit + bias;
-            const unsigned long long k = argmax_key(x, v);
-            best[i] = k > best[i] ? k : best[i];
+        for (int i = 0; i < MC; ++i) {
+          float acc = 0.f;
+#pragma unroll
+          for (int c = 0; c < KCH; ++c)
+            acc += dot8(w[u][c], *reinterpret_cast<const uint4*>(xs + (size_t)i * KP + c * 256 + lane * 8));
+          acc = warp_sum(acc);
+          if (i < mc) {
+            const float logit = round_bf16(acc);
+            if (a.logits_out && lane == 0) a.logits_out[(size_t)(m0 + i) * a.V + v] = logit;
+            const bool ok =
+                a.gr.kind == 1 ? a.gr.table[(size_t)rule[i] * a.V + v] != 0 : ((rule[i] >> cls) & 1u) != 0;
+            if (ok) {
+              const float x = rescored ? rescore_logit_call(a.rs, rrow[i], m0 + i, v, logit + bias) : logit + bias;
+              const unsigned long long k = argmax_key(x, v);
+              best[i] = k > best[i] ? k : best[i];
+            }
           }
         }
       }
