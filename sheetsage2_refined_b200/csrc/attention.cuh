@@ -55,10 +55,10 @@ struct AttnArgs {
   int D;
   const bf16* wo;                 // out-projection weight [D, D]
   unsigned long long* acc_out;    // [M][D]
-  // fuse_q (cross attention, kAttnPreStage with kAccOut, 8 splits, D <= 1024): the kernel
+  // fuse_q (cross attention, kAttnPreStage with kAccOut, 8 or 16 splits, D <= 1024): the kernel
   // forms its input row itself, x = LayerNorm(x_in + bf16(acc_in + bias_in)) (the previous
   // attention's residual sum and norm, engine.py:312), writes it to x_out once, and computes
-  // its head's query rows from it, q = bf16(x Wq^T + bq), 8 rows per CTA
+  // its head's query rows from it, q = bf16(x Wq^T + bq), 64 / splits rows per CTA
   const unsigned long long* acc_in;  // [M][D]
   const bf16* bias_in;               // [D]
   const float* x_in;                 // [M][D]
@@ -85,15 +85,16 @@ constexpr int kAttnPreRegs = 1;   // the first pass of the CTA's earlier keys in
 constexpr int kAttnPreStage = 2;  // all of them (up to stage_cap rows) bulk-copied to shared memory
 // static shared memory of the kernel plus the 1 KB the SM reserves per CTA (upper bound)
 constexpr size_t kAttnStaticSmem = 4096;
+constexpr size_t kAttnStaticSmemWide = 8192;  // the same for the 16-split instantiations
 // shared memory of an SM left to the projection kernels that run beside the attention
 constexpr size_t kAttnOtherSmem = 32768;
 
 constexpr int kAttnThreads = 256;
-constexpr int kAttnMaxSplits = 8;  // CTAs per (row, head) at most
+constexpr int kAttnMaxSplits = 16;  // CTAs per (row, head) at most (above 8: non-portable clusters)
 constexpr int kAttnGroups = kAttnThreads / 8;  // 8 lanes x 16 bytes per key row
 static_assert(kAttnThreads == 4 * kHeadDim && kAttnGroups % 4 == 0, "the partial-output sum takes 4 threads per dimension");
 constexpr int kAttnUnroll = 4;  // keys per group and pass (kAttnPreNone / kAttnPreRegs)
-constexpr int kAttnQRows = 8;  // fuse_q: query rows computed per CTA (one per warp)
+constexpr int kAttnQRows = 8;  // fuse_q: query rows per CTA at most (64 / splits, one per warp)
 constexpr int kAttnQLnGroups = 128;  // fuse_q: 8-column groups of the input row (D <= 1024)
 constexpr int kAttnUnrollStaged = 8;  // the same from shared memory (kAttnPreStage): more keys in flight
 
@@ -155,7 +156,9 @@ struct AttnSmem {
 // attention CTAs and a projection CTA share an SM's 64K), the batched one 48
 // (five CTAs an SM).  Left to itself ptxas chose 80 for the fused kernels and
 // spilled.
-template <int kPre, bool kAccOut>
+// kMaxSplits sizes the exchange arrays: 8, or 16 for the wide cross attention (an instantiation
+// of its own, so that the 8-way kernels keep their shared memory).
+template <int kPre, bool kAccOut, int kMaxSplits = 8>
 __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
   constexpr bool kStage = kPre == kAttnPreStage;
   constexpr int kU = kStage ? kAttnUnrollStaged : kAttnUnroll;
@@ -165,6 +168,7 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
   const int h = blockIdx.y, m = a.order ? a.order[blockIdx.z] : (int)blockIdx.z;
   extern __shared__ __align__(16) unsigned char attn_smem[];
   const bool fuse_q = kStage && kAccOut && a.fuse_q;
+  const int qrows = fuse_q ? kHeadDim / C : 0;  // fuse_q: this CTA's query rows (8 or 4: 8 or 16 splits)
   const AttnSmem lay(a.chunk_cap, kStage ? a.stage_cap : 0, a.D, fuse_q);
   float* sc = reinterpret_cast<float*>(attn_smem);                // [chunk_cap] scores, then exp values
   float* part = reinterpret_cast<float*>(attn_smem + lay.part);   // [kAttnGroups][64] partial outputs
@@ -175,8 +179,8 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
   bf16* sbi = reinterpret_cast<bf16*>(attn_smem + lay.sbi);       //         previous out-projection bias [D]
   bf16* sw = reinterpret_cast<bf16*>(attn_smem + lay.sw);         //         this CTA's query weight rows [8][D]
   bf16* sxq = reinterpret_cast<bf16*>(attn_smem + lay.sxq);       //         the normalised input row [D]
-  __shared__ float xred[2][kAttnMaxSplits];          // every rank's partial max and sum
-  __shared__ float xo[kAttnMaxSplits][kHeadDim];      // every rank's partial output
+  __shared__ float xred[2][kMaxSplits];          // every rank's partial max and sum
+  __shared__ float xo[kMaxSplits][kHeadDim];      // every rank's partial output
   __shared__ float wmax[kAttnThreads / 32], wsum[kAttnThreads / 32];
   __shared__ __align__(16) bf16 sq[kHeadDim];  // kStage: the row's query for this head
   __shared__ __align__(8) uint64_t xbar[4];           // exchanges received: max, sum, output, query
@@ -190,7 +194,7 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
   const int lane = tid & 31, warp = tid >> 5;
   // The whole cluster sees the same row and the same launch shape, so every
   // early return below is taken by all of its CTAs together.
-  if (C != a.splits || C > kAttnMaxSplits) {
+  if (C != a.splits || C > kMaxSplits) {
     if (threadIdx.x == 0) atomicExch(a.err, kErrAttnCluster);
     return;
   }
@@ -231,13 +235,13 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
   if constexpr (kStage) {
     if (tid == 0) {
       mbar_expect_tx(&bars[0], (unsigned)(jbulk - j0) * (2 * kHeadDim * 2));
-      mbar_expect_tx(&bars[1], fuse_q ? (unsigned)a.D * 10 + (unsigned)(kAttnQRows * a.D * 2) : 0u);
+      mbar_expect_tx(&bars[1], fuse_q ? (unsigned)a.D * 10 + (unsigned)(qrows * a.D * 2) : 0u);
       if (fuse_q) {  // first: what the query rows need
         bulk_load(sg, a.ln_g, (unsigned)a.D * 4, &bars[1]);
         bulk_load(sb, a.ln_b, (unsigned)a.D * 4, &bars[1]);
         bulk_load(sbi, a.bias_in, (unsigned)a.D * 2, &bars[1]);
         // the CTA's 8 query rows of head h: contiguous in Wq
-        bulk_load(sw, a.wq + (size_t)(h * kHeadDim + rank * kAttnQRows) * a.D, (unsigned)(kAttnQRows * a.D * 2),
+        bulk_load(sw, a.wq + (size_t)(h * kHeadDim + rank * qrows) * a.D, (unsigned)(qrows * a.D * 2),
                   &bars[1]);
       }
       // one copy per run of rows that is contiguous in memory (a page of the
@@ -269,7 +273,8 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
     }
   }
   // fuse_q: the bias of this warp's query row
-  const float qbias = fuse_q && lane == 0 ? __bfloat162float(a.bq[h * kHeadDim + rank * kAttnQRows + warp]) : 0.f;
+  const float qbias =
+      fuse_q && lane == 0 && warp < qrows ? __bfloat162float(a.bq[h * kHeadDim + rank * qrows + warp]) : 0.f;
   if constexpr (kPre == kAttnPreRegs) {
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -326,7 +331,7 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
       }
     }
     __syncthreads();
-    // This CTA's 8 query rows of head h, one per warp, with the projection
+    // This CTA's query rows of head h (8, or 4 with 16 splits), one per warp, with the projection
     // kernel's arithmetic (16-byte pieces of 8 products, pieces added in
     // order, then the warp butterfly; + bias, rounded to bf16), sent to
     // every rank of the cluster.
@@ -341,9 +346,9 @@ __global__ void __maxnreg__(kAccOut ? 104 : 48) attn_kernel(const AttnArgs a) {
     }
     acc = warp_sum(acc);
     cluster_wait();  // every peer has started: the first store into its shared memory follows
-    if (lane == 0) {
+    if (lane == 0 && warp < qrows) {
       const float qb = round_bf16(acc + qbias);
-      for (int r = 0; r < C; ++r) st_async_f32(&sqx[rank * kAttnQRows + warp], r, qb, &xbar[3]);
+      for (int r = 0; r < C; ++r) st_async_f32(&sqx[rank * qrows + warp], r, qb, &xbar[3]);
     }
   }
   if constexpr (kStage) {

@@ -471,7 +471,12 @@ int launch_crosskv(s2r_ctx* c, const bf16* x, int frames, int slot, cudaStream_t
 // (row, head) pairs of a full batch cover the SMs about four times, and
 // twice that for the cross-attention, whose rows are long (every encoder
 // frame) and uneven.
-constexpr int kAttnSplits = kAttnMaxSplits;
+constexpr int kAttnSplits = 8;
+// Engines below 16 slots whose heads are few split the cross attention 16 ways (non-portable
+// clusters of 16) when one row's 16 CTAs per head fit the SMs in one wave: the product decoder's
+// 8 heads over 7,500 frames ran on only 64 CTAs with 8-way splits.  The choice depends on the
+// heads only, not on the slots, so a slot's result does not depend on the engine's batch.
+constexpr int kAttnWideSplits = 16;
 
 int attn_splits_for(const s2r_ctx* c, int cover) {
   if (!c->tc) return kAttnSplits;
@@ -518,7 +523,7 @@ AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
   p.pre = c->tc ? kAttnPreNone : kAttnPreRegs;
   // the cross attention of a fused engine can compute its own query rows
   // (8 per CTA, one per warp) when it stages and splits 8 ways
-  const bool can_fuse_q = cross && c->fuse_out && p.C * kAttnQRows == kHeadDim && c->D % 256 == 0 && c->D <= 1024;
+  const bool can_fuse_q = cross && c->fuse_out && (p.C == 8 || p.C == 16) && c->D % 256 == 0 && c->D <= 1024;
   if (!c->tc) {
     // Stage the CTAs' earlier keys and values in shared memory when the
     // launch fits on the SMs in one wave with room left for a CTA of the
@@ -527,7 +532,8 @@ AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
     const int ctas = M * c->H * p.C;
     const int per_sm = std::max(1, (ctas + c->num_sms - 1) / c->num_sms);
     const size_t budget = ((size_t)c->smem_per_sm - kAttnOtherSmem) / (2 * per_sm);
-    const size_t fixed = AttnSmem(p.chunk_cap, 0, c->D, can_fuse_q).total + kAttnStaticSmem;
+    const size_t fixed =
+        AttnSmem(p.chunk_cap, 0, c->D, can_fuse_q).total + (p.C > 8 ? kAttnStaticSmemWide : kAttnStaticSmem);
     if (budget > fixed) {
       const int cap = (int)std::min<size_t>(p.chunk_cap, (budget - fixed) / (2 * kHeadDim * 2));
       if (cap == p.chunk_cap || cap >= kAttnGroups * kAttnUnroll) {
@@ -539,6 +545,35 @@ AttnPlan plan_attn(const s2r_ctx* c, int M, bool cross) {
   }
   p.smem = AttnSmem(p.chunk_cap, p.stage_cap, c->D, p.fuse_q).total;
   return p;
+}
+
+// Switch the cross attention to kAttnWideSplits CTAs per (row, head) if the device can
+// schedule a cluster of that size with the kernel's shared memory (else keep 8).
+int widen_cross_splits(s2r_ctx* c) {
+  const int keep = c->attn_splits_cross;
+  c->attn_splits_cross = kAttnWideSplits;
+  const AttnPlan p = plan_attn(c, c->B, true);
+  void (*fn)(const AttnArgs) = p.pre == kAttnPreStage ? attn_kernel<kAttnPreStage, true, kAttnWideSplits>
+                                                      : attn_kernel<kAttnPreRegs, true, kAttnWideSplits>;
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kAttnWideSplits, c->H, 1);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = kAttnWideSplits;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) != cudaSuccess || clusters < 1) {
+    cudaGetLastError();  // not schedulable here: keep the portable split
+    c->attn_splits_cross = keep;
+  }
+  return S2R_OK;
 }
 
 // What a kernel of a one-slot decode step reads that no kernel of the step
@@ -629,10 +664,13 @@ int launch_attn(s2r_ctx* c, RowMap rm, int M, int layer, bool cross, cudaStream_
   // tensor-core engines read keys in the loops and keep their out-projection a GEMM; the
   // others load keys ahead of the wait and fuse the out-projection
   if ((pre == kAttnPreNone) == c->fuse_out) return fail(S2R_ENOTSUP, "no attention kernel for this engine");
-  void (*fn)(const AttnArgs) = pre == kAttnPreNone   ? attn_kernel<kAttnPreNone, false>
+  void (*fn)(const AttnArgs) = pre == kAttnPreNone ? attn_kernel<kAttnPreNone, false>
+                               : C > 8 ? (pre == kAttnPreRegs ? attn_kernel<kAttnPreRegs, true, kAttnWideSplits>
+                                                              : attn_kernel<kAttnPreStage, true, kAttnWideSplits>)
                                : pre == kAttnPreRegs ? attn_kernel<kAttnPreRegs, true>
                                                      : attn_kernel<kAttnPreStage, true>;
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (C > 8) CK(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   CK(launch_ex(fn, dim3(C, c->H, M), dim3(kAttnThreads), smem, s, next_pdl(c), C, a));
   return S2R_OK;
 }
@@ -1284,6 +1322,7 @@ int32_t s2r_create(const s2r_config* cfg, const s2r_weights* w, const s2r_gramma
   }
   c->attn_splits = attn_splits_for(c, 4);
   c->attn_splits_cross = attn_splits_for(c, 8);
+  if (!c->tc && c->H * kAttnWideSplits <= c->num_sms) TRYC(widen_cross_splits(c));
   c->h_frames.assign(c->B, 0);
   if (c->tc) {
     TRYC(dalloc(c, &c->order_self, c->B));
