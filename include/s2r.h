@@ -181,6 +181,11 @@ int32_t s2r_load_frame_tables(s2r_ctx* ctx, int32_t slot, const float* const* ta
  * n-1 (n_prefix <= max_tokens - 1).  `stop_seconds` ends the slot at the
  * first time token at or after it (+inf: never).  `target` is the table
  * grammar's generated-token count (S2R_NO_TARGET: none).
+ * The cross K/V of every layer is projected in one tensor-core launch; the
+ * prefix is prefilled in chunks of 128 positions, chunks of more than 8 on
+ * tensor cores (the arithmetic of the reference's own prefill, so equal to
+ * forcing the prefix token by token within the parity tolerance), shorter
+ * ones on the decode step's kernels (equal bit for bit).
  * Replaces BatchDecoder.load (engine.py:180-232) without rescoring tables. */
 int32_t s2r_load_slot(s2r_ctx* ctx, int32_t slot, const void* memory, int32_t memory_dtype,
                       int32_t memory_frames, int32_t frames, const int64_t* prefix, int32_t n_prefix,
