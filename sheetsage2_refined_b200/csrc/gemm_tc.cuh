@@ -1,8 +1,9 @@
 // Tensor-core projection for many rows: D = W X^T with tcgen05 + TMA (sm_100a).
 //
-// The batched step (16 or more slots), its prefill chunks and the per-window
-// cross K/V projection multiply a weight matrix W [N, K] by tens to thousands
-// of activation rows X [R, K].  The weights are the large operand, so they are
+// The batched step (16 or more slots) and the prefill chunks of every engine
+// multiply a weight matrix W [N, K] by tens to hundreds of activation rows
+// X [R, K] (the per-window cross K/V projection has its own persistent kernel,
+// crosskv.cuh).  The weights are the large operand, so they are
 // the MMA's A operand (M = 128 output features per CTA) and the rows are its B
 // operand (NB rows, 64..256): D[n][r] = sum_k W[n][k] X[r][k], both operands
 // K-major, bf16 in, fp32 accumulated in tensor memory.
@@ -25,7 +26,7 @@
 // partial leaves the cluster and the sum order is fixed.
 //
 // Epilogues: those of proj.cuh (bias, bf16 rounding, residual, GELU, paged K/V
-// append, cross K/V scatter; the same function the CUDA-core kernel runs) and
+// append; the same function the CUDA-core kernel runs) and
 // EPI_LOGITS, the tied-embedding logits fused with the grammar mask, the mode
 // bias and the greedy argmax of logits.cuh: per row a warp reduces its
 // 64-bit (value, ~index) keys and publishes them with one atomicMax; the last
